@@ -1,0 +1,396 @@
+#!/usr/bin/env python
+"""Benchmark: FP8 128x128 block-scaled MoE layer on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--M 64] [--hot 0]
+
+Prints ONE JSON line (rank 0). A step is one MoE layer forward over the
+synthetic GLM-5-like decode batch (M=64 tokens by default: H=6144, I=2048,
+E=256 experts, top-8 sigmoid router, FP8 e4m3 weights with fp32 128x128 block
+scales, 1x128 activation scales, bf16 in/out).
+
+  value       tokens/s over all ranks, inputs resident in HBM, the five kernels
+              of the layer (route, gather+quant, GEMM1+SiLU+requant,
+              GEMM2+combine, top-k reduce) timed with CUDA events on their stream;
+  e2e         the same metric through the public API moe_decode_megakernel_full
+              with host (pinned) inputs copied in and the output copied out
+              inside the timed region;
+  roofline    the dominant kernel (GEMM1) against measured HBM bandwidth;
+  cpu_baseline the fp32 CPU oracle on a bounded sample of experts (rank 0, N=1).
+--impl reference times that CPU path alone (the reference is a Python/Triton
+package for AMD GPUs; its algorithm is restated by the oracle).
+
+N > 1 runs expert-parallel ranks when --ep is given, otherwise independent
+replicas of the layer, one per GPU (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE layer tokens/s + HBM GB/s at M=64–1024, FP8 128x128 blockscale, B200"
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--M", type=int, default=64, help="tokens per GPU")
+    ap.add_argument("--hot", type=int, default=0, help="experts with +2.0 router bias (skewed load)")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-sample-experts", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ----------------------------------------------------------------------------
+# helpers
+# ----------------------------------------------------------------------------
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(name: str):
+    """DRAM bytes per launch from a committed ncu summary (profiles/<name>.txt),
+    line 'dram_bytes_per_launch: N'."""
+    p = ROOT / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1]))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples of one GPU during the timed region."""
+
+    FIELDS = ["clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.hw_slowdown",
+              "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
+              "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + ",".join(self.FIELDS),
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != len(self.FIELDS):
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = max(smax, float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(backend):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1 and not dist.is_initialized():
+        dist.init_process_group(backend, timeout=timedelta(seconds=300))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, local, ws
+
+
+def layer_bytes(shape, active, pairs):
+    """Algorithmic HBM bytes of one layer step: every active expert's fp8
+    weights and block scales once, bf16 hidden in and bf16 out."""
+    from trials_b200 import synth
+
+    w = active * (synth.weight_bytes_per_expert(shape.H, shape.I) + synth.scale_bytes_per_expert(shape.H, shape.I))
+    return w + shape.M * shape.H * 2 * 2
+
+
+def gemm1_bytes(shape, active, pairs):
+    """Algorithmic bytes of one GEMM1 launch: w13 + its scales of every active
+    expert, the routed fp8 activation rows and scales read, the fp8 inter rows
+    and scales written."""
+    H, I = shape.H, shape.I
+    w = active * (2 * I * H + 4 * (2 * I // 128) * (H // 128))
+    return w + pairs * (H + 4 * H // 128) + pairs * (I + 4 * I // 128)
+
+
+# ----------------------------------------------------------------------------
+# CPU path (oracle): baseline and reference arm
+# ----------------------------------------------------------------------------
+def cpu_sample_setup(shape, n_sample, seed):
+    """A bounded CPU sample of the workload: the router over all M tokens, and
+    weights for only the first n_sample active experts."""
+    import torch
+
+    from oracle import moe_oracle as orc
+    from trials_b200 import synth
+
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn(shape.M, shape.E, generator=g)
+    if shape.hot_experts:
+        logits[:, : shape.hot_experts] += shape.hot_bias
+    tw, ids = synth.make_router(logits, shape.topk, shape.scoring)
+    active = torch.unique(ids).tolist()
+    sample = active[:n_sample]
+    emap = torch.full((shape.E,), -1, dtype=torch.int32)
+    emap[torch.tensor(sample)] = torch.arange(len(sample), dtype=torch.int32)
+    w13 = (torch.randn(len(sample), 2 * shape.I, shape.H, generator=g) * 0.02).to(torch.bfloat16)
+    w13_q, w13_s = orc.per_block_quant_fp8(w13)
+    del w13
+    w2 = (torch.randn(len(sample), shape.H, shape.I, generator=g) * 0.02).to(torch.bfloat16)
+    w2_q, w2_s = orc.per_block_quant_fp8(w2)
+    del w2
+    hidden = torch.randn(shape.M, shape.H, generator=g).to(torch.bfloat16)
+    return dict(hidden=hidden, tw=tw, ids=ids, emap=emap, n=len(sample), active=len(active), w13_q=w13_q,
+                w13_s=w13_s, w2_q=w2_q, w2_s=w2_s)
+
+
+def cpu_sample_run(s):
+    """One timed pass of the fp32 oracle over the sampled experts; returns
+    seconds per expert."""
+    import torch
+
+    from oracle import moe_oracle as orc
+
+    t0 = time.perf_counter()
+    orc.moe_layer(s["hidden"], s["w13_q"], s["w13_s"], s["w2_q"], s["w2_s"], s["tw"], s["ids"],
+                  expert_map=s["emap"].numpy(), num_local=s["n"], dtype=torch.float32)
+    return (time.perf_counter() - t0) / s["n"]
+
+
+def cpu_baseline(shape, n_sample, seed, reps=1):
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    s = cpu_sample_setup(shape, n_sample, seed)
+    per_expert = min(cpu_sample_run(s) for _ in range(reps))
+    tps = shape.M / (per_expert * s["active"])
+    return {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"fp32 torch oracle (dequantise + matmul per expert) over {s['n']} of {s['active']} active "
+                      f"experts of the M={shape.M} batch; seconds per expert x active experts = layer time"}
+
+
+def run_reference(args, shape, config):
+    import torch
+
+    rank, _, ws = dist_setup("gloo")
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    s = cpu_sample_setup(shape, args.cpu_sample_experts, args.seed)
+    for _ in range(args.warmup):
+        cpu_sample_run(s)
+    times = [cpu_sample_run(s) for _ in range(args.steps)]
+    per_expert = sum(times) / len(times)
+    layer_s = per_expert * s["active"]
+    tps = shape.M * ws / layer_s
+    sample = (f"fp32 torch oracle (restatement of the reference's torch path) over {s['n']} of {s['active']} "
+              f"active experts per step; layer time = seconds per expert x active experts")
+    line = {"metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": layer_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config, "impl": "reference",
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+def run_ours(args, shape, config):
+    import torch
+    import torch.distributed as dist
+
+    from trials_b200 import moe, stages, synth
+
+    rank, local, ws = dist_setup("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    L = synth.make_layer(shape, moe.per_block_quant_fp8, seed=args.seed + rank, device=dev)
+    active = synth.active_experts(L.topk_ids, shape.E)
+    pairs = int(((L.topk_ids >= 0) & (L.topk_ids < shape.E)).sum().item())
+    pipe = stages.LayerPipeline(shape.M, shape.H, shape.I, shape.E, shape.topk, dev)
+    args_run = (L.hidden, L.topk_ids, L.topk_weights, L.w13, L.w13_scale, L.w2, L.w2_scale)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if ws == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing (value)
+    for _ in range(args.warmup):
+        pipe.run(*args_run)
+    n_ev = 6
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    start.record()
+    for k in range(args.steps):
+        pipe.run(*args_run, events=evs[k])
+    end.record()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    stage_ms = {name: statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(args.steps))
+                for i, name in enumerate(stages.LayerPipeline.STAGES)}
+    err = int(pipe.err.item())
+    if err:
+        raise RuntimeError(f"device error word {err} after the timed steps")
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        h_host = L.hidden.cpu().pin_memory()
+        ids_host = L.topk_ids.cpu().pin_memory()
+        tw_host = L.topk_weights.cpu().pin_memory()
+        out_host = torch.empty(shape.M, shape.H, dtype=torch.bfloat16).pin_memory()
+        h_dev, ids_dev, tw_dev = torch.empty_like(L.hidden), torch.empty_like(L.topk_ids), \
+            torch.empty_like(L.topk_weights)
+
+        def e2e_step():
+            h_dev.copy_(h_host, non_blocking=True)
+            ids_dev.copy_(ids_host, non_blocking=True)
+            tw_dev.copy_(tw_host, non_blocking=True)
+            out = moe.moe_decode_megakernel_full(h_dev, L.w13, L.w13_scale, L.w2, L.w2_scale, tw_dev, ids_dev)
+            out_host.copy_(out, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        s2.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e2.record()
+        barrier()
+        ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps)
+        h2d = h_host.numel() * 2 + ids_host.numel() * 4 + tw_host.numel() * 4
+        e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": out_host.numel() * 2, "ms_per_step": ms_e2e}
+
+    # ---- CPU baseline (rank 0, one GPU only)
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(shape, args.cpu_sample_experts, args.seed)
+
+    if rank != 0:
+        if ws > 1:
+            dist.destroy_process_group()
+        return 0
+    peak, peak_kind = measured_peaks()
+    g1_bytes = gemm1_bytes(shape, active, pairs)
+    g1_ms = stage_ms["gemm1_silu"]
+    achieved = g1_bytes / (g1_ms / 1e3) / 1e9
+    traffic_name = f"gemm1_silu_glm_decode_m{shape.M}" + (f"_hot{shape.hot_experts}" if shape.hot_experts else "")
+    step_bytes = layer_bytes(shape, active, pairs)
+    line = {
+        "metric": METRIC,
+        "value": shape.M * ws / (ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8e4m3 (fp32 accumulate)",
+        "data": "synthetic",
+        "config": config,
+        "hbm_gbs": step_bytes / (ms / 1e3) / 1e9,
+        "hbm_frac": step_bytes / (ms / 1e3) / 1e9 / peak,
+        "active_experts": active,
+        "stage_ms": stage_ms,
+        "roofline": {"kernel": "gemm1_silu (grouped GEMM stage 1)", "bound": "hbm", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": f"{peak_kind} HBM copy bandwidth",
+                     "algorithmic_bytes_per_launch": g1_bytes, "traffic": ncu_traffic(traffic_name)},
+        "gpu_launches": 5 * args.steps,
+        "clocks": clk,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    from trials_b200 import synth
+
+    shape = synth.glm(args.M, args.hot)
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    config = {"workload": f"glm_decode_M{args.M}" + (f"_hot{args.hot}" if args.hot else ""),
+              "tokens_per_gpu": shape.M, "hidden": shape.H, "moe_intermediate": shape.I, "experts": shape.E,
+              "topk": shape.topk, "router": "sigmoid top-k, renormalised",
+              "quant": "e4m3 weights with fp32 128x128 block scales, 1x128 activation scales",
+              "l2": "no flush: each step streams the active experts' fp8 weights (8.4-9.7 GB) >> 126 MB L2",
+              "parallelism": "single GPU" if ws == 1 else f"{ws} independent replicas (one per GPU)"}
+    if args.impl == "reference":
+        return run_reference(args, shape, config)
+    return run_ours(args, shape, config)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,203 @@
+/*
+ * b200moe: FP8 128x128 block-scaled Mixture-of-Experts layer for NVIDIA B200 (sm_100a).
+ *
+ * C ABI. Every function takes raw device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream and returns an int
+ * status: B200MOE_OK (0) or a negative B200MOE_ERR_* code for bad arguments or
+ * unsupported shapes (checked on the host, before anything is launched).
+ * No function allocates device memory: callers pass outputs and, where needed,
+ * a workspace whose size the matching *_workspace_size() call reports.
+ *
+ * Data-dependent problems found on the device (an expert id outside the
+ * expert range, a pipeline wait that timed out) are OR-ed into a caller-owned
+ * int32 "device error word" (B200MOE_DEVERR_* bits); read it with
+ * b200moe_read_error() after the stream has run.
+ *
+ * Data types: bf16 = __nv_bfloat16 (passed as void*), fp8 = E4M3FN bytes
+ * (uint8_t), scales float32, ids int32.
+ */
+#ifndef B200MOE_H_
+#define B200MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200MOE_API __attribute__((visibility("default")))
+#else
+#define B200MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200MOE_OK 0
+#define B200MOE_ERR_INVALID_ARG (-1)
+#define B200MOE_ERR_UNSUPPORTED (-2)
+#define B200MOE_ERR_WORKSPACE (-3)
+#define B200MOE_ERR_CUDA (-4)
+
+#define B200MOE_DEVERR_BAD_EXPERT_ID 1 /* an id outside [0, num_experts) other than -1 */
+#define B200MOE_DEVERR_TIMEOUT 2       /* a bounded pipeline wait gave up */
+#define B200MOE_DEVERR_CAPACITY 4      /* routed rows exceeded the given capacity */
+
+/* Library version (major*10000 + minor*100 + patch). */
+B200MOE_API int b200moe_version(void);
+
+/* Text for a status code. */
+B200MOE_API const char* b200moe_status_string(int status);
+
+/* Message describing the last non-OK status returned on this host thread. */
+B200MOE_API const char* b200moe_last_error_message(void);
+
+/* ------------------------------------------------------------------------
+ * Routing: moe_align_block_size.
+ * Replaces sglang's moe_align_block_size(topk_ids, block_size, num_experts)
+ * as called by the reference orchestrator
+ * (sglang_integration/aiter.py:95-97, 113-115).
+ *
+ * topk_ids (M, topk) int32. Entries equal to -1 are dropped silently (the
+ * expert-parallel "not on this rank" convention); other ids outside
+ * [0, num_experts) are dropped and set B200MOE_DEVERR_BAD_EXPERT_ID.
+ * expert_map (nullable, num_experts entries) maps an id to the index of its
+ * weights, or to -1 to drop it.
+ *
+ * Outputs, same meaning as the reference:
+ *   sorted_token_ids[sorted_capacity]: flat indices t*topk+j grouped by expert,
+ *       each expert padded to a multiple of block_m with the sentinel M*topk.
+ *       Order within an expert is ascending flat index (stable).
+ *       Every entry past the routed rows is the sentinel.
+ *   expert_ids[blocks_capacity]: (mapped) expert of each block_m block; blocks
+ *       past num_tokens_post_pad/block_m are -1 (never left uninitialised).
+ *   num_tokens_post_pad[1]: total padded rows (device scalar; no host sync).
+ * Capacities must be at least b200moe_align_capacity_rows() /
+ * b200moe_align_capacity_blocks() (sglang's numel + (E+1)*(block_m-1) sizing).
+ * num_experts <= 1024.
+ * ---------------------------------------------------------------------- */
+B200MOE_API int64_t b200moe_align_capacity_rows(int64_t numel, int num_experts, int block_m);
+B200MOE_API int64_t b200moe_align_capacity_blocks(int64_t numel, int num_experts, int block_m);
+B200MOE_API int b200moe_align(const int32_t* topk_ids, int64_t M, int topk, int num_experts, int block_m,
+                  const int32_t* expert_map, int num_local_experts, int32_t* sorted_token_ids,
+                  int64_t sorted_capacity, int32_t* expert_ids, int64_t blocks_capacity,
+                  int32_t* num_tokens_post_pad, int32_t* err_word, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Activation quantisation: per_token_group_quant_fp8(x, 128).
+ * Replaces sglang's per_token_group_quant_fp8 called at
+ * sglang_integration/aiter.py:132-133 and :151-152 (torch form of the same
+ * formula: phase5_orchestrator.py:26-32).
+ * x (M, K) bf16 with row stride ldx elements; q (M, K) fp8 with row stride ldq;
+ * s[m * s_stride_row + g * s_stride_group] = max(amax(x[m, 128g:128g+128])/448, 1e-12);
+ * q = e4m3(clamp(x / s, -448, 448)), round to nearest even. K % 128 == 0.
+ * ---------------------------------------------------------------------- */
+B200MOE_API int b200moe_quant_1x128(const void* x, int64_t M, int64_t K, int64_t ldx, uint8_t* q, int64_t ldq, float* s,
+                        int64_t s_stride_row, int64_t s_stride_group, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Weight quantisation: per_block_quant_fp8(w, 128, 128)
+ * (phase5_orchestrator.py:35-41). w (E, N, K) bf16 contiguous -> q (E, N, K)
+ * fp8 and s (E, N/128, K/128) fp32, s = max(block amax/448, 1e-12).
+ * ---------------------------------------------------------------------- */
+B200MOE_API int b200moe_quant_block128(const void* w, int64_t E, int64_t N, int64_t K, uint8_t* q, float* s, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Full layer: replaces _moe_decode_megakernel_full
+ * (sglang_integration/aiter.py:74-177) and, for the arguments it supports,
+ * the aiter fused_moe call (sglang_integration/aiter.py:459-478) with
+ * quant_type=per_128x128, activation=Silu, gate_mode=interleave.
+ *
+ * hidden (M, H) bf16 row-major; w13 (E_w, 2I, H) fp8 with gate/up rows
+ * interleaved (row 2j = gate j, row 2j+1 = up j); w13_scale (E_w, 2I/128, H/128);
+ * w2 (E_w, H, I) fp8; w2_scale (E_w, H/128, I/128); topk_weights (M, topk) f32;
+ * topk_ids (M, topk) int32; expert_map as in b200moe_align (nullable; then
+ * E_w = num_experts). out (M, H) bf16:
+ *   out[t] = bf16( sum_j topk_weights[t,j] * W2[e] . q(silu(g) * u) ),
+ *   (g, u) = W13[e] . q(hidden[t]), e = expert of slot (t, j);
+ * slots whose id is -1 or maps to -1 contribute nothing.
+ * Requirements: H % 256 == 0, I % 128 == 0, num_experts <= 1024.
+ * workspace: b200moe_layer_workspace_size() bytes, 256-byte aligned; its first
+ * 4 bytes are the device error word and must be zeroed once by the caller.
+ * No host synchronisation: the call can be captured in a CUDA graph.
+ * ---------------------------------------------------------------------- */
+B200MOE_API size_t b200moe_layer_workspace_size(int64_t M, int64_t H, int64_t I, int num_experts, int num_local_experts,
+                                    int topk);
+B200MOE_API int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
+                  const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                  const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map,
+                  int num_local_experts, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Stage-level entry points used by b200moe_layer, exposed for staged callers
+ * and tests. They work on the layer's internal expert-sorted row layout:
+ * routed rows grouped by expert, each expert padded to a multiple of 16 rows.
+ * These replace the reference's kernel launchers
+ * moe_decode_megakernel_stage1 (aiter_module/moe_decode_megakernel.py:88-123),
+ * ..._stage1_fused(fused_silu) (aiter_module/moe_decode_megakernel_fused.py:125-139)
+ * and ..._stage2_fused (aiter_module/moe_decode_megakernel_fused.py:142-157).
+ *
+ * b200moe_route: the align above with block 16 into sorted_ids (capacity
+ * rows_capacity >= b200moe_route_capacity_rows()), plus the GEMM work list:
+ * each expert's padded rows cut into chunks of at most tile_tokens rows
+ * (16, 32, 64 or 128); chunk_expert/chunk_row0/chunk_rows[chunks_capacity],
+ * n_chunks[1] and num_rows[1] (total padded rows) on the device.
+ * ---------------------------------------------------------------------- */
+B200MOE_API int64_t b200moe_route_capacity_rows(int64_t numel, int num_local_experts);
+B200MOE_API int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_experts, int tile_tokens);
+B200MOE_API int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
+                  int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
+                  int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
+                  int32_t* n_chunks, int32_t* num_rows, int32_t* err_word, void* stream);
+
+/* Quantise hidden rows into the sorted layout: row p of a_q (ld = H) holds
+ * q(hidden[sorted_ids[p] / topk]) or zeros for a padding row; scales go to
+ * a_sT[g * a_s_ld + p] (transposed). Rows p >= num_rows are not touched. */
+B200MOE_API int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* sorted_ids,
+                         const int32_t* num_rows, int64_t rows_capacity, uint8_t* a_q, float* a_sT, int64_t a_s_ld,
+                         void* stream);
+
+/* Stage 1: inter = silu(gate) * up of (a1 . w13^T), re-quantised 1x128 into
+ * a2_q (rows_capacity, I) and a2_sT (I/128, a_s_ld). grid_ctas = 0 picks one
+ * CTA per SM; any other value fixes the persistent grid (results are
+ * bit-identical for every grid). */
+B200MOE_API int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
+                       const uint8_t* w13, const float* w13_scale, int num_local_experts, int64_t H, int64_t I,
+                       const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
+                       const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens, uint8_t* a2_q,
+                       float* a2_sT, int32_t* err_word, int grid_ctas, void* stream);
+
+/* Stage 2: out_pair[f, :] = topk_weights[f] * (a2 . w2^T)[p, :] for every
+ * sorted row p with f = sorted_ids[p] < M*topk. out_pair is (M*topk, H) f32;
+ * rows of dropped slots are not written. */
+B200MOE_API int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, int64_t rows_capacity,
+                          const uint8_t* w2, const float* w2_scale, int num_local_experts, int64_t H, int64_t I,
+                          const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
+                          const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
+                          const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
+                          float* out_pair, int32_t* err_word, int grid_ctas, void* stream);
+
+/* out[t, :] = bf16( sum_{j valid} out_pair[t*topk + j, :] ), slots summed in
+ * order j = 0..topk-1; a slot is valid when its id is in [0, num_experts)
+ * and (expert_map == NULL or expert_map[id] >= 0). Replaces the unpermute of
+ * sglang_integration/aiter.py:164-177. */
+B200MOE_API int b200moe_combine_reduce(const float* out_pair, const int32_t* topk_ids, const int32_t* expert_map,
+                           int num_experts, int64_t M, int topk, int64_t H, void* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Diagnostics.
+ * ---------------------------------------------------------------------- */
+/* Copies the device error word to *value (synchronises `stream`); when clear
+ * is non-zero the word is reset to 0 afterwards. */
+B200MOE_API int b200moe_read_error(int32_t* err_word, int32_t* value, int clear, void* stream);
+
+/* Runs a one-CTA kernel that waits on an mbarrier nothing will complete,
+ * with a limit of timeout_us microseconds, and reports the timeout through
+ * the error word (B200MOE_DEVERR_TIMEOUT). Exercises the bounded-wait path
+ * of the pipelines without faulting or hanging the GPU. */
+B200MOE_API int b200moe_selftest_wait_timeout(int32_t* err_word, int timeout_us, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MOE_H_ */

@@ -1,0 +1,95 @@
+"""The C-ABI library: loads, exports every symbol include/b200moe.h declares,
+and rejects bad arguments on the host (no GPU needed: these calls return
+before anything is launched)."""
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from trials_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "b200moe.h"
+
+
+def header_functions():
+    text = HEADER.read_text()
+    return re.findall(r"B200MOE_API\s+[\w\s\*]+?\b(b200moe_\w+)\s*\(", text)
+
+
+def test_library_loads_and_exports_header_symbols():
+    L = _lib.lib()
+    names = header_functions()
+    assert len(names) >= 19
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures must cover the header exactly"
+
+
+def test_version_and_status_strings():
+    L = _lib.lib()
+    assert L.b200moe_version() >= 100
+    assert L.b200moe_status_string(0) == b"ok"
+    assert L.b200moe_status_string(_lib.ERR_UNSUPPORTED) == b"unsupported shape or option"
+
+
+def test_capacity_formulas():
+    L = _lib.lib()
+    # sglang sizing: numel + (E + 1) * (BM - 1); GLM decode M=64, k=8, E=256, BM=128 -> 259 blocks
+    assert L.b200moe_align_capacity_rows(512, 256, 128) == 512 + 257 * 127
+    assert L.b200moe_align_capacity_blocks(512, 256, 128) == 259
+    assert L.b200moe_route_capacity_rows(512, 256) == 512 + 256 * 15
+    rows = 512 + 256 * 15
+    assert L.b200moe_route_capacity_chunks(512, 256, 32) == -(-rows // 32) + 256
+
+
+def test_host_side_argument_checks():
+    L = _lib.lib()
+    # unsupported hidden size (not a multiple of 256)
+    assert L.b200moe_layer(1, 4, 100, 128, 8, 2, 1, 1, 1, 1, 1, 1, None, 8, 1, 1, 1 << 30, None) == \
+        _lib.ERR_UNSUPPORTED
+    # K not a multiple of 128
+    assert L.b200moe_quant_1x128(16, 4, 100, 100, 16, 100, 16, 1, 1, None) == _lib.ERR_INVALID_ARG
+    # tile size outside {16, 32, 64, 128}
+    assert L.b200moe_route(16, 4, 2, 8, None, 8, 48, 16, 1000, 16, 16, 16, 1000, 16, 16, 16, None) == \
+        _lib.ERR_INVALID_ARG
+    # too many experts
+    assert L.b200moe_align(16, 4, 2, 2000, 128, None, 0, 16, 1 << 20, 16, 1 << 20, 16, 16, None) == \
+        _lib.ERR_UNSUPPORTED
+    # output capacity below the sglang sizing
+    assert L.b200moe_align(16, 4, 2, 8, 128, None, 0, 16, 10, 16, 10, 16, 16, None) == _lib.ERR_WORKSPACE
+    # workspace too small
+    ws = L.b200moe_layer_workspace_size(4, 256, 128, 8, 8, 2)
+    assert ws > 0
+    assert L.b200moe_layer(256, 4, 256, 128, 8, 2, 256, 256, 256, 256, 256, 256, None, 8, 256, 256, ws - 1,
+                           None) == _lib.ERR_WORKSPACE
+    assert b"workspace" in L.b200moe_last_error_message()
+
+
+def test_python_errors_map_to_exceptions():
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.ERR_UNSUPPORTED, "x")
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_INVALID_ARG, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.ERR_CUDA, "x")
+
+
+def test_fused_moe_rejects_unsupported_options_before_launch():
+    from trials_b200 import fused_moe, QuantType
+
+    h = torch.zeros(2, 256, dtype=torch.bfloat16)
+    w = torch.zeros(1)
+    for kw in [dict(quant_type=QuantType.per_Token), dict(activation="Gelu"), dict(bias1=w),
+               dict(no_combine=True), dict(gate_mode="separated"), dict(a2_scale=w), dict(swiglu_limit=7.0),
+               dict(doweight_stage1=True)]:
+        with pytest.raises(NotImplementedError):
+            fused_moe(h, w, w, w, w, **kw)
+
+
+def test_ops_refuse_cpu_tensors():
+    from trials_b200 import moe_decode_megakernel_full
+
+    h = torch.zeros(2, 256, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        moe_decode_megakernel_full(h, h, h, h, h, h, h)

@@ -1,0 +1,451 @@
+// extern "C" entry points: argument checks, workspace carving, TMA tensor
+// maps and kernel sequencing. No function here allocates device memory or
+// synchronises the stream (except b200moe_read_error, which exists to do so).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/b200moe.h"
+#include "launch.h"
+#include "moe_gemm.cuh"
+
+using namespace b200moe;
+
+namespace {
+
+thread_local char g_last_error[256] = "";
+
+int fail(int status, const char* fmt, const char* detail = "") {
+  snprintf(g_last_error, sizeof(g_last_error), fmt, detail);
+  return status;
+}
+
+int cuda_status(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return B200MOE_OK;
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s", where, cudaGetErrorString(e));
+  return B200MOE_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
+
+// ---- TMA descriptor encoding through the driver entry point (no -lcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2D byte matrix [rows][cols] (row pitch = cols), box = 128 bytes x box_rows,
+// 128-byte swizzle (the K-major canonical layout of the tcgen05 descriptors).
+int make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable%s");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed%s");
+  return B200MOE_OK;
+}
+
+int sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int cache[64] = {0};
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (n <= 0) n = 1;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+bool valid_tile(int t) { return t == 16 || t == 32 || t == 64 || t == 128; }
+
+int pick_tile_tokens(int64_t numel, int E_local) {
+  const double avg = (double)numel / (double)(E_local > 0 ? E_local : 1);
+  if (avg <= 12.0) return 32;
+  if (avg <= 40.0) return 64;
+  return 128;
+}
+
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
+
+struct LayerPlan {
+  int tile_tokens;
+  int64_t rows_cap, chunks_cap, as_ld;
+  size_t off_sorted, off_ce, off_cr0, off_crows, off_counts, off_a1, off_a1s, off_a2, off_a2s, off_pair, total;
+};
+
+LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
+  LayerPlan p{};
+  const int64_t numel = M * topk;
+  p.tile_tokens = pick_tile_tokens(numel, E_local);
+  p.rows_cap = b200moe_route_capacity_rows(numel, E_local);
+  p.chunks_cap = b200moe_route_capacity_chunks(numel, E_local, p.tile_tokens);
+  p.as_ld = round_up(p.rows_cap + 128, 64);
+  size_t off = 256;  // device error word
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (size_t)round_up((int64_t)bytes, 256);
+    return o;
+  };
+  p.off_sorted = take(sizeof(int32_t) * p.rows_cap);
+  p.off_ce = take(sizeof(int32_t) * p.chunks_cap);
+  p.off_cr0 = take(sizeof(int32_t) * p.chunks_cap);
+  p.off_crows = take(sizeof(int32_t) * p.chunks_cap);
+  p.off_counts = take(sizeof(int32_t) * 4);
+  p.off_a1 = take((size_t)p.rows_cap * H);
+  p.off_a1s = take(sizeof(float) * (size_t)(H / 128) * p.as_ld);
+  p.off_a2 = take((size_t)p.rows_cap * I);
+  p.off_a2s = take(sizeof(float) * (size_t)(I / 128) * p.as_ld);
+  p.off_pair = take(sizeof(float) * (size_t)numel * H);
+  p.total = off;
+  return p;
+}
+
+int check_gemm_shapes(int64_t H, int64_t I) {
+  if (H <= 0 || I <= 0 || H % 256 != 0 || I % 128 != 0)
+    return fail(B200MOE_ERR_UNSUPPORTED, "hidden must be a multiple of 256 and intermediate of 128%s");
+  if (H > (1 << 20) || I > (1 << 20)) return fail(B200MOE_ERR_UNSUPPORTED, "dimension too large%s");
+  return B200MOE_OK;
+}
+
+int run_gemm(int epi, const uint8_t* a_q, const float* a_sT, int64_t as_ld, int64_t rows_cap, const uint8_t* w,
+             const float* w_scale, int E_local, int64_t Nw, int64_t K, const int32_t* ce, const int32_t* cr0,
+             const int32_t* crows, const int32_t* n_chunks, int64_t chunks_cap, int tile_tokens, GemmParams p,
+             int grid_ctas, cudaStream_t stream) {
+  CUtensorMap tm_w, tm_a;
+  int st = make_tmap_u8(&tm_w, w, (int64_t)E_local * Nw, K, 256);
+  if (st) return st;
+  st = make_tmap_u8(&tm_a, a_q, rows_cap, K, gemm_tile_rows(tile_tokens));
+  if (st) return st;
+  p.chunk_expert = ce;
+  p.chunk_row0 = cr0;
+  p.chunk_rows = crows;
+  p.n_chunks = n_chunks;
+  p.w_scale = w_scale;
+  p.a_sT = a_sT;
+  p.as_ld = as_ld;
+  p.K = (int)K;
+  p.Nw = (int)Nw;
+  p.timeout_ns = kTimeoutNs;
+  const int64_t units_cap = chunks_cap * (Nw / 256);
+  int64_t grid = grid_ctas > 0 ? grid_ctas : sm_count();
+  if (grid > units_cap) grid = units_cap;
+  return cuda_status(launch_grouped_gemm(epi, tile_tokens, tm_w, tm_a, p, (int)grid, stream), "grouped gemm");
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200moe_version(void) { return 100; }
+
+const char* b200moe_status_string(int status) {
+  switch (status) {
+    case B200MOE_OK:
+      return "ok";
+    case B200MOE_ERR_INVALID_ARG:
+      return "invalid argument";
+    case B200MOE_ERR_UNSUPPORTED:
+      return "unsupported shape or option";
+    case B200MOE_ERR_WORKSPACE:
+      return "workspace too small";
+    case B200MOE_ERR_CUDA:
+      return "CUDA error";
+    default:
+      return "unknown status";
+  }
+}
+
+const char* b200moe_last_error_message(void) { return g_last_error; }
+
+int64_t b200moe_align_capacity_rows(int64_t numel, int num_experts, int block_m) {
+  return numel + (int64_t)(num_experts + 1) * (block_m - 1);
+}
+
+int64_t b200moe_align_capacity_blocks(int64_t numel, int num_experts, int block_m) {
+  return ceil_div(b200moe_align_capacity_rows(numel, num_experts, block_m), block_m);
+}
+
+int b200moe_align(const int32_t* topk_ids, int64_t M, int topk, int num_experts, int block_m,
+                  const int32_t* expert_map, int num_local_experts, int32_t* sorted_token_ids,
+                  int64_t sorted_capacity, int32_t* expert_ids, int64_t blocks_capacity,
+                  int32_t* num_tokens_post_pad, int32_t* err_word, void* stream) {
+  if (M < 0 || topk <= 0 || num_experts <= 0 || block_m <= 0 || !sorted_token_ids || !num_tokens_post_pad ||
+      !err_word || (M > 0 && !topk_ids))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_align: bad argument%s");
+  const int E = expert_map ? num_local_experts : num_experts;
+  if (E <= 0 || E > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_align: 1..1024 experts supported%s");
+  const int64_t numel = M * topk;
+  if (numel > INT32_MAX / 2) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_align: too many tokens%s");
+  if (sorted_capacity < b200moe_align_capacity_rows(numel, E, block_m) ||
+      (expert_ids && blocks_capacity < b200moe_align_capacity_blocks(numel, E, block_m)))
+    return fail(B200MOE_ERR_WORKSPACE, "b200moe_align: output capacity too small%s");
+  AlignArgs a{};
+  a.topk_ids = topk_ids;
+  a.n = numel;
+  a.num_experts = num_experts;
+  a.expert_map = expert_map;
+  a.E = E;
+  a.block_m = block_m;
+  a.sentinel = (int32_t)numel;
+  a.sorted_ids = sorted_token_ids;
+  a.sorted_cap = sorted_capacity;
+  a.expert_ids = expert_ids;
+  a.blocks_cap = blocks_capacity;
+  a.ntp = num_tokens_post_pad;
+  a.err = err_word;
+  return cuda_status(launch_align(a, (cudaStream_t)stream), "align");
+}
+
+int b200moe_quant_1x128(const void* x, int64_t M, int64_t K, int64_t ldx, uint8_t* q, int64_t ldq, float* s,
+                        int64_t s_stride_row, int64_t s_stride_group, void* stream) {
+  if (M < 0 || K <= 0 || K % 128 != 0 || ldx < K || ldq < K || (M > 0 && (!x || !q || !s)))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_quant_1x128: bad argument%s");
+  if (!aligned16(x) || ldx % 8 != 0 || (reinterpret_cast<uintptr_t>(q) & 7) || ldq % 8 != 0)
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_quant_1x128: x rows must be 16-byte aligned, q rows 8-byte%s");
+  QuantArgs a{};
+  a.x = x;
+  a.ldx = ldx;
+  a.K = K;
+  a.rows = M;
+  a.q = q;
+  a.ldq = ldq;
+  a.s = s;
+  a.s_row = s_stride_row;
+  a.s_grp = s_stride_group;
+  return cuda_status(launch_quant_1x128(a, (cudaStream_t)stream), "quant_1x128");
+}
+
+int b200moe_quant_block128(const void* w, int64_t E, int64_t N, int64_t K, uint8_t* q, float* s, void* stream) {
+  if (E < 0 || N <= 0 || K <= 0 || N % 128 != 0 || K % 128 != 0 || (E > 0 && (!w || !q || !s)))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_quant_block128: bad argument%s");
+  if (!aligned16(w) || !aligned16(q) || E > 65535 || N / 128 > 65535)
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_quant_block128: alignment or size%s");
+  return cuda_status(launch_quant_block128(w, E, N, K, q, s, (cudaStream_t)stream), "quant_block128");
+}
+
+int64_t b200moe_route_capacity_rows(int64_t numel, int num_local_experts) {
+  return numel + (int64_t)num_local_experts * 15;
+}
+
+int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_experts, int tile_tokens) {
+  if (tile_tokens <= 0) return 0;
+  return ceil_div(b200moe_route_capacity_rows(numel, num_local_experts), tile_tokens) + num_local_experts;
+}
+
+int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
+                  int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
+                  int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
+                  int32_t* n_chunks, int32_t* num_rows, int32_t* err_word, void* stream) {
+  if (M < 0 || topk <= 0 || num_experts <= 0 || !valid_tile(tile_tokens) || !sorted_ids || !chunk_expert ||
+      !chunk_row0 || !chunk_rows || !n_chunks || !num_rows || !err_word || (M > 0 && !topk_ids))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_route: bad argument%s");
+  const int E = expert_map ? num_local_experts : num_experts;
+  if (E <= 0 || E > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_route: 1..1024 experts supported%s");
+  const int64_t numel = M * topk;
+  if (numel > INT32_MAX / 2) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_route: too many tokens%s");
+  if (rows_capacity < b200moe_route_capacity_rows(numel, E) ||
+      chunks_capacity < b200moe_route_capacity_chunks(numel, E, tile_tokens))
+    return fail(B200MOE_ERR_WORKSPACE, "b200moe_route: capacity too small%s");
+  AlignArgs a{};
+  a.topk_ids = topk_ids;
+  a.n = numel;
+  a.num_experts = num_experts;
+  a.expert_map = expert_map;
+  a.E = E;
+  a.block_m = 16;
+  a.sentinel = (int32_t)numel;
+  a.sorted_ids = sorted_ids;
+  a.sorted_cap = rows_capacity;
+  a.expert_ids = nullptr;
+  a.ntp = num_rows;
+  a.tile_tokens = tile_tokens;
+  a.chunk_expert = chunk_expert;
+  a.chunk_row0 = chunk_row0;
+  a.chunk_rows = chunk_rows;
+  a.chunks_cap = chunks_capacity;
+  a.n_chunks = n_chunks;
+  a.err = err_word;
+  return cuda_status(launch_align(a, (cudaStream_t)stream), "route");
+}
+
+int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* sorted_ids,
+                         const int32_t* num_rows, int64_t rows_capacity, uint8_t* a_q, float* a_sT, int64_t a_s_ld,
+                         void* stream) {
+  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || rows_capacity < 0 || a_s_ld < rows_capacity ||
+      (rows_capacity > 0 && (!hidden || !sorted_ids || !num_rows || !a_q || !a_sT)))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_gather_quant: bad argument%s");
+  if (!aligned16(hidden) || (reinterpret_cast<uintptr_t>(a_q) & 7))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_gather_quant: alignment%s");
+  QuantArgs a{};
+  a.x = hidden;
+  a.ldx = H;
+  a.K = H;
+  a.rows = rows_capacity;
+  a.num_rows = num_rows;
+  a.sorted_ids = sorted_ids;
+  a.topk = topk;
+  a.sentinel = (int32_t)(M * topk);
+  a.q = a_q;
+  a.ldq = H;
+  a.s = a_sT;
+  a.s_row = 1;
+  a.s_grp = a_s_ld;
+  return cuda_status(launch_quant_1x128(a, (cudaStream_t)stream), "gather_quant");
+}
+
+int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
+                       const uint8_t* w13, const float* w13_scale, int num_local_experts, int64_t H, int64_t I,
+                       const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
+                       const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens, uint8_t* a2_q,
+                       float* a2_sT, int32_t* err_word, int grid_ctas, void* stream) {
+  int st = check_gemm_shapes(H, I);
+  if (st) return st;
+  if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 ||
+      a_s_ld < rows_capacity + gemm_tile_rows(tile_tokens) || a_s_ld % 4 != 0 || !a1_q || !a1_sT || !w13 ||
+      !w13_scale || !chunk_expert || !chunk_row0 || !chunk_rows || !n_chunks || !a2_q || !a2_sT || !err_word)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_gemm1_silu: bad argument%s");
+  if (!aligned16(a1_q) || !aligned16(w13) || !aligned16(a1_sT) || !aligned16(a2_q))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_gemm1_silu: 16-byte alignment required%s");
+  GemmParams p{};
+  p.out_q = a2_q;
+  p.out_q_ld = I;
+  p.out_sT = a2_sT;
+  p.out_s_ld = a_s_ld;
+  p.err = err_word;
+  return run_gemm(EPI_SILU, a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, 2 * I, H,
+                  chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, p, grid_ctas,
+                  (cudaStream_t)stream);
+}
+
+int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, int64_t rows_capacity,
+                          const uint8_t* w2, const float* w2_scale, int num_local_experts, int64_t H, int64_t I,
+                          const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
+                          const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
+                          const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
+                          float* out_pair, int32_t* err_word, int grid_ctas, void* stream) {
+  int st = check_gemm_shapes(H, I);
+  if (st) return st;
+  if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 || M < 0 || topk <= 0 ||
+      a_s_ld < rows_capacity + gemm_tile_rows(tile_tokens) || a_s_ld % 4 != 0 || !a2_q || !a2_sT || !w2 ||
+      !w2_scale || !chunk_expert || !chunk_row0 || !chunk_rows || !n_chunks || !sorted_ids || !topk_weights ||
+      !out_pair || !err_word)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_gemm2_combine: bad argument%s");
+  if (!aligned16(a2_q) || !aligned16(w2) || !aligned16(a2_sT))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_gemm2_combine: 16-byte alignment required%s");
+  GemmParams p{};
+  p.sorted_ids = sorted_ids;
+  p.topk_w = topk_weights;
+  p.sentinel = (int32_t)(M * topk);
+  p.out_pair = out_pair;
+  p.err = err_word;
+  return run_gemm(EPI_COMBINE, a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I,
+                  chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, p, grid_ctas,
+                  (cudaStream_t)stream);
+}
+
+int b200moe_combine_reduce(const float* out_pair, const int32_t* topk_ids, const int32_t* expert_map,
+                           int num_experts, int64_t M, int topk, int64_t H, void* out, void* stream) {
+  if (M < 0 || topk <= 0 || H <= 0 || H % 8 != 0 || num_experts <= 0 ||
+      (M > 0 && (!out_pair || !topk_ids || !out)))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_combine_reduce: bad argument%s");
+  if (!aligned16(out_pair) || !aligned16(out))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_combine_reduce: 16-byte alignment required%s");
+  return cuda_status(
+      launch_combine_reduce(out_pair, topk_ids, expert_map, num_experts, M, topk, H, out, (cudaStream_t)stream),
+      "combine_reduce");
+}
+
+size_t b200moe_layer_workspace_size(int64_t M, int64_t H, int64_t I, int num_experts, int num_local_experts,
+                                    int topk) {
+  if (M < 0 || H <= 0 || I <= 0 || topk <= 0) return 0;
+  const int E = num_local_experts > 0 ? num_local_experts : num_experts;
+  return plan_layer(M, H, I, E, topk).total;
+}
+
+int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
+                  const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                  const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map,
+                  int num_local_experts, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_gemm_shapes(H, I);
+  if (st) return st;
+  if (M < 0 || topk <= 0 || num_experts <= 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer: bad argument%s");
+  if (M == 0) return B200MOE_OK;
+  if (!hidden || !w13 || !w13_scale || !w2 || !w2_scale || !topk_weights || !topk_ids || !out || !workspace)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer: null pointer%s");
+  const int E = expert_map ? num_local_experts : num_experts;
+  if (E <= 0 || E > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_layer: 1..1024 experts supported%s");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer: workspace must be 256-byte aligned%s");
+  const LayerPlan pl = plan_layer(M, H, I, E, topk);
+  if (workspace_bytes < pl.total) return fail(B200MOE_ERR_WORKSPACE, "b200moe_layer: workspace too small%s");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* err = reinterpret_cast<int32_t*>(ws);
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws + pl.off_sorted);
+  int32_t* ce = reinterpret_cast<int32_t*>(ws + pl.off_ce);
+  int32_t* cr0 = reinterpret_cast<int32_t*>(ws + pl.off_cr0);
+  int32_t* crows = reinterpret_cast<int32_t*>(ws + pl.off_crows);
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + pl.off_counts);  // [0] n_chunks, [1] num_rows
+  uint8_t* a1 = ws + pl.off_a1;
+  float* a1s = reinterpret_cast<float*>(ws + pl.off_a1s);
+  uint8_t* a2 = ws + pl.off_a2;
+  float* a2s = reinterpret_cast<float*>(ws + pl.off_a2s);
+  float* pair = reinterpret_cast<float*>(ws + pl.off_pair);
+
+  st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,
+                     crows, pl.chunks_cap, counts, counts + 1, err, stream);
+  if (st) return st;
+  st = b200moe_gather_quant(hidden, M, H, topk, sorted, counts + 1, pl.rows_cap, a1, a1s, pl.as_ld, stream);
+  if (st) return st;
+  st = b200moe_gemm1_silu(a1, a1s, pl.as_ld, pl.rows_cap, w13, w13_scale, E, H, I, ce, cr0, crows, counts,
+                          pl.chunks_cap, pl.tile_tokens, a2, a2s, err, 0, stream);
+  if (st) return st;
+  st = b200moe_gemm2_combine(a2, a2s, pl.as_ld, pl.rows_cap, w2, w2_scale, E, H, I, ce, cr0, crows, counts,
+                             pl.chunks_cap, pl.tile_tokens, sorted, topk_weights, M, topk, pair, err, 0, stream);
+  if (st) return st;
+  return b200moe_combine_reduce(pair, topk_ids, expert_map, num_experts, M, topk, H, out, stream);
+}
+
+int b200moe_read_error(int32_t* err_word, int32_t* value, int clear, void* stream) {
+  if (!err_word || !value) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_read_error: null pointer%s");
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = cuda_status(cudaMemcpyAsync(value, err_word, sizeof(int32_t), cudaMemcpyDeviceToHost, s), "read_error");
+  if (st) return st;
+  st = cuda_status(cudaStreamSynchronize(s), "read_error sync");
+  if (st) return st;
+  if (clear) return cuda_status(cudaMemsetAsync(err_word, 0, sizeof(int32_t), s), "read_error clear");
+  return B200MOE_OK;
+}
+
+int b200moe_selftest_wait_timeout(int32_t* err_word, int timeout_us, void* stream) {
+  if (!err_word || timeout_us <= 0 || timeout_us > 10000000)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_selftest_wait_timeout: bad argument%s");
+  return cuda_status(launch_wait_timeout_selftest(err_word, (uint64_t)timeout_us * 1000ull, (cudaStream_t)stream),
+                     "selftest");
+}
+
+}  // extern "C"

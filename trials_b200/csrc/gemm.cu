@@ -1,0 +1,59 @@
+// Instantiations and launcher of the persistent grouped GEMM.
+#include "launch.h"
+#include "moe_gemm.cuh"
+
+namespace b200moe {
+
+namespace {
+
+template <int T, int EW, int EPI>
+cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p, int grid,
+                       cudaStream_t stream) {
+  using C = GemmCfg<T, EW>;
+  auto kernel = moe_grouped_gemm_kernel<T, EW, EPI>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (err != cudaSuccess) return err;
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_a, p);
+  return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p,
+                       int grid, cudaStream_t stream) {
+  switch (tile_tokens) {
+    case 16:
+    case 32:
+      return launch_cfg<32, 4, EPI>(tm_w, tm_a, p, grid, stream);
+    case 64:
+      return launch_cfg<64, 8, EPI>(tm_w, tm_a, p, grid, stream);
+    case 128:
+      return launch_cfg<128, 8, EPI>(tm_w, tm_a, p, grid, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+int gemm_tile_rows(int tile_tokens) {
+  switch (tile_tokens) {
+    case 16:
+    case 32:
+      return 32;
+    case 64:
+      return 64;
+    case 128:
+      return 128;
+    default:
+      return 0;
+  }
+}
+
+cudaError_t launch_grouped_gemm(int epi, int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a,
+                                const GemmParams& p, int grid, cudaStream_t stream) {
+  if (grid <= 0) return cudaSuccess;
+  if (epi == EPI_SILU) return launch_epi<EPI_SILU>(tile_tokens, tm_w, tm_a, p, grid, stream);
+  return launch_epi<EPI_COMBINE>(tile_tokens, tm_w, tm_a, p, grid, stream);
+}
+
+}  // namespace b200moe

@@ -1,0 +1,72 @@
+// Internal launcher interfaces between the C-ABI layer (capi.cu) and the
+// kernel translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace b200moe {
+
+struct AlignArgs {
+  const int32_t* topk_ids;
+  int64_t n;               // M * topk
+  int num_experts;         // id range of topk_ids
+  const int32_t* expert_map;
+  int E;                   // weight experts (map targets)
+  int block_m;
+  int32_t sentinel;
+  int32_t* sorted_ids;
+  int64_t sorted_cap;
+  int32_t* expert_ids;     // nullable
+  int64_t blocks_cap;
+  int32_t* ntp;
+  int tile_tokens;         // 0 = no chunk list
+  int32_t* chunk_expert;
+  int32_t* chunk_row0;
+  int32_t* chunk_rows;
+  int64_t chunks_cap;
+  int32_t* n_chunks;
+  int32_t* err;
+};
+
+size_t align_smem_bytes(int E);
+cudaError_t launch_align(const AlignArgs& a, cudaStream_t stream);
+
+// Per-token-group (1 x 128) FP8 quantisation. With sorted_ids != nullptr the
+// output row p takes its input from token sorted_ids[p] / topk (zeros for the
+// sentinel) and the number of rows is read from *num_rows on the device.
+struct QuantArgs {
+  const void* x;
+  int64_t ldx;
+  int64_t K;
+  int64_t rows;            // rows (M) or the row capacity in gather mode
+  const int32_t* num_rows; // gather mode: device row count
+  const int32_t* sorted_ids;
+  int topk;
+  int32_t sentinel;
+  uint8_t* q;
+  int64_t ldq;
+  float* s;
+  int64_t s_row;
+  int64_t s_grp;
+};
+cudaError_t launch_quant_1x128(const QuantArgs& a, cudaStream_t stream);
+
+cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K, uint8_t* q, float* s,
+                                  cudaStream_t stream);
+
+cudaError_t launch_combine_reduce(const float* pair, const int32_t* ids, const int32_t* expert_map,
+                                  int num_experts, int64_t M, int topk, int64_t H, void* out, cudaStream_t stream);
+
+cudaError_t launch_wait_timeout_selftest(int32_t* err, uint64_t timeout_ns, cudaStream_t stream);
+
+struct GemmParams;
+// epi: 0 = SiLU + requant (stage 1), 1 = weighted combine (stage 2).
+cudaError_t launch_grouped_gemm(int epi, int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a,
+                                const GemmParams& p, int grid, cudaStream_t stream);
+// Activation tile rows the kernel for this tile_tokens loads per stage.
+int gemm_tile_rows(int tile_tokens);
+
+}  // namespace b200moe

@@ -1,0 +1,404 @@
+// Persistent FP8 block-scaled grouped GEMM for the two MoE stages (sm_100a).
+//
+// Math (both stages), for one expert e and the rows p of the expert-sorted
+// activation matrix A that were routed to e:
+//   C[p, n] = sum_kb  w_s[e, n/128, kb] * a_s[p, kb] * sum_{k in kb} W[e, n, k] * A[p, k]
+// which is the block-scaled dequant order of the reference Triton kernel
+// (aiter_module/moe_decode_megakernel.py:71-81: acc += dot(a, b) * a_s * b_s per
+// 128-wide K block).
+//
+// Orientation ("swap-AB"): the tensor-core MMA M side is 128 weight rows (N of
+// the layer), the MMA N side is the expert's routed tokens (16..T columns).
+// At decode an expert sees a handful of tokens, so the weight tile fills the
+// 128-row MMA and the token count only sets the (cheap) N width.
+//
+// One work unit = (token chunk of one expert, 256 consecutive weight rows).
+// Per 128-wide K block the MMA warp issues 4 (K=32) x 2 (two 128-row halves)
+// tcgen05.mma into a fresh TMEM buffer; the epilogue warps read that partial
+// sum back with tcgen05.ld, multiply by the two block scales and accumulate in
+// fp32 registers ("promotion" - the fp32 128x128 scales are not MX scales, so
+// the tensor core cannot apply them). TMEM holds NBUF partial buffers so the
+// MMA of block kb+1.. overlaps the promotion of block kb.
+//
+// Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM owner),
+// warps 2.. = epilogue (EW warps; warp w reads TMEM lanes 32*(w%4)..+31).
+//
+// Epilogues:
+//   EPI_SILU    (stage 1, gate/up interleaved rows): inter = silu(gate) * up in
+//               fp32, then 1x128 FP8 re-quantisation of inter (amax/448 scale)
+//               straight into the stage-2 activation buffer (sorted row order).
+//   EPI_COMBINE (stage 2): out_pair[f, n] = topk_w[f] * C[p, n] for the flat
+//               (token, slot) id f = sorted_ids[p]; padding rows are skipped.
+#pragma once
+
+#include <cuda_fp8.h>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace b200moe {
+
+enum { EPI_SILU = 0, EPI_COMBINE = 1 };
+
+struct GemmParams {
+  // routing: chunk list produced by the route kernel (device memory)
+  const int32_t* chunk_expert;
+  const int32_t* chunk_row0;
+  const int32_t* chunk_rows;
+  const int32_t* n_chunks;
+  // weight block scales (E, Nw/128, K/128) contiguous
+  const float* w_scale;
+  // activation scales, transposed: a_sT[kb * as_ld + p]
+  const float* a_sT;
+  int64_t as_ld;
+  int K;        // reduction width (bytes of fp8)
+  int Nw;       // weight rows per expert
+  // EPI_SILU outputs: q rows p (width Nw/2), scales transposed (Nw/256 x as_ld)
+  uint8_t* out_q;
+  int64_t out_q_ld;
+  float* out_sT;
+  int64_t out_s_ld;
+  // EPI_COMBINE
+  const int32_t* sorted_ids;
+  const float* topk_w;
+  int32_t sentinel;   // M * topk
+  float* out_pair;    // (M*topk, Nw) fp32
+  // diagnostics
+  int32_t* err;
+  uint64_t timeout_ns;
+};
+
+template <int T_, int EW_>
+struct GemmCfg {
+  static constexpr int T = T_;                 // max tokens (MMA N) per unit
+  static constexpr int EW = EW_;               // epilogue warps
+  static constexpr int NSUB = 2;               // 128-row halves per unit
+  static constexpr int UNIT_ROWS = 128 * NSUB; // weight rows per unit
+  static constexpr int THREADS = 64 + 32 * EW;
+  static constexpr int COL_SPLIT = EW / 4;     // epilogue warps sharing one TMEM lane quarter
+  static constexpr int TC = T / COL_SPLIT;     // token columns per epilogue thread
+  static constexpr int W_BYTES = UNIT_ROWS * 128;
+  static constexpr int A_BYTES = T * 128;
+  static constexpr int TILE_BYTES = W_BYTES + A_BYTES;  // multiple of 1024
+  static constexpr int S_BYTES = T * 4;                 // activation scales per stage
+  static constexpr uint32_t STAGE_TX = TILE_BYTES + S_BYTES;
+  static constexpr int NBUF = 512 / (NSUB * T);         // TMEM partial buffers
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int STAGING = T * 128;               // EPI_SILU output tile
+  static constexpr int RED = 4 * COL_SPLIT * T * 4;     // EPI_SILU amax exchange
+  static constexpr int SMEM_LIMIT = 232448;
+  static constexpr int FIXED = 1024 /*align slack*/ + STAGING + RED + 1024 /*barriers etc*/;
+  static constexpr int NSTAGE_RAW = (SMEM_LIMIT - FIXED) / (TILE_BYTES + S_BYTES);
+  static constexpr int NSTAGE = NSTAGE_RAW > 8 ? 8 : NSTAGE_RAW;
+  static constexpr int SMEM_BYTES = FIXED + NSTAGE * (TILE_BYTES + S_BYTES);
+  static_assert(T % 16 == 0 && T >= 16 && T <= 256, "MMA N must be a multiple of 16 in [16, 256]");
+  static_assert(EW % 4 == 0, "epilogue warps must cover the 4 TMEM lane quarters");
+  static_assert(TC % 16 == 0, "columns per thread must be a multiple of 16");
+  static_assert(NBUF >= 2, "need at least two TMEM buffers");
+  static_assert(NSTAGE >= 2, "shared memory too small");
+  static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
+};
+
+__device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + __expf(-g)); }
+
+template <int T, int EW, int EPI>
+__global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
+    moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
+                            const GemmParams p) {
+  using C = GemmCfg<T, EW>;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzled TMA tiles.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;                                             // NSTAGE * TILE_BYTES
+  float* sscale = reinterpret_cast<float*>(tiles + C::NSTAGE * C::TILE_BYTES);  // NSTAGE * T
+  uint8_t* staging = reinterpret_cast<uint8_t*>(sscale + C::NSTAGE * T);      // T * 128
+  float* red = reinterpret_cast<float*>(staging + C::STAGING);                // 4 * COL_SPLIT * T
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + C::RED);
+  uint64_t* empty = full + C::NSTAGE;
+  uint64_t* tfull = empty + C::NSTAGE;
+  uint64_t* tempty = tfull + C::NBUF;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + C::NBUF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int NKB = p.K >> 7;
+  const int NT = p.Nw / C::UNIT_ROWS;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + EW);  // MMA commit + each epilogue warp (scales read)
+    }
+    for (int b = 0; b < C::NBUF; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], EW);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_a);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_units = (*p.n_chunks) * NT;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const int chunk = u / NT;
+        const int nt = u - chunk * NT;
+        const int e = __ldg(&p.chunk_expert[chunk]);
+        const int p0 = __ldg(&p.chunk_row0[chunk]);
+        const int wrow = e * p.Nw + nt * C::UNIT_ROWS;
+        for (int kb = 0; kb < NKB; ++kb) {
+          if (*abort_flag || !mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          uint8_t* tile = tiles + stage * C::TILE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_TX);
+          tma_load_2d(tile, &tm_w, &full[stage], kb * 128, wrow, pol_w);
+          tma_load_2d(tile + C::W_BYTES, &tm_a, &full[stage], kb * 128, p0, pol_a);
+          bulk_load(sscale + stage * T, p.a_sT + (int64_t)kb * p.as_ld + p0, C::S_BYTES, &full[stage]);
+          ++issued;
+          if (++stage == C::NSTAGE) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        atomicOr(p.err, ERR_DEV_TIMEOUT);
+        *abort_flag = 1;
+        // Let every load already issued land before the CTA exits.
+        long first = issued > C::NSTAGE ? issued - C::NSTAGE : 0;
+        for (long g = first; g < issued; ++g)
+          mbar_wait_bounded(&full[g % C::NSTAGE], (uint32_t)((g / C::NSTAGE) & 1), p.timeout_ns);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0, buf = 0;
+      uint32_t phase = 0, bphase = 0;
+      long committed = 0;
+      int last_buf = 0;
+      uint32_t last_bphase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const int chunk = u / NT;
+        const int rows = __ldg(&p.chunk_rows[chunk]);
+        const uint32_t idesc = idesc_e4m3_f32(128, rows);
+        for (int kb = 0; kb < NKB; ++kb) {
+          if (*abort_flag || !mbar_wait_bounded(&tempty[buf], bphase ^ 1, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (*abort_flag || !mbar_wait_bounded(&full[stage], phase, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t w_addr = smem_u32(tiles + stage * C::TILE_BYTES);
+          const uint32_t a_addr = w_addr + C::W_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+            for (int s = 0; s < C::NSUB; ++s) {
+              const uint32_t d = tmem_base + (uint32_t)(buf * C::NSUB * T + s * T);
+              umma_f8(d, sdesc_kmajor_sw128(w_addr + s * 16384 + ks * 32), sdesc_kmajor_sw128(a_addr + ks * 32),
+                      idesc, ks > 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[stage]);
+          umma_commit(&tfull[buf]);
+          ++committed;
+          last_buf = buf;
+          last_bphase = bphase;
+          if (++stage == C::NSTAGE) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (++buf == C::NBUF) {
+            buf = 0;
+            bphase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        atomicOr(p.err, ERR_DEV_TIMEOUT);
+        *abort_flag = 1;
+      }
+      // The tensor core must be done with TMEM before it is released.
+      if (committed > 0) mbar_wait_bounded(&tfull[last_buf], last_bphase, p.timeout_ns);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;                 // 0..EW-1
+    const int q = warp & 3;                  // TMEM lane quarter
+    const int h = ew >> 2;                   // column slice
+    const int col0 = h * C::TC;              // first token column of this thread
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    int stage = 0, buf = 0;
+    uint32_t phase = 0, bphase = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int chunk = u / NT;
+      const int nt = u - chunk * NT;
+      const int e = __ldg(&p.chunk_expert[chunk]);
+      const int p0 = __ldg(&p.chunk_row0[chunk]);
+      const int rows = __ldg(&p.chunk_rows[chunk]);
+      const float* wsp0 = p.w_scale + ((int64_t)e * (p.Nw >> 7) + nt * 2) * NKB;
+      const float* wsp1 = wsp0 + NKB;
+
+      float acc[2][C::TC];
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+#pragma unroll
+        for (int j = 0; j < C::TC; ++j) acc[s][j] = 0.f;
+
+      float ws0 = __ldg(wsp0), ws1 = __ldg(wsp1);
+      for (int kb = 0; kb < NKB && ok; ++kb) {
+        const float ws0n = (kb + 1 < NKB) ? __ldg(wsp0 + kb + 1) : 0.f;
+        const float ws1n = (kb + 1 < NKB) ? __ldg(wsp1 + kb + 1) : 0.f;
+        if (*abort_flag || !mbar_wait_bounded(&tfull[buf], bphase, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // Acquire the stage's TMA writes (the activation scales) directly; the
+        // phase completed before the MMA ran, so this returns at once.
+        if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        const float* ss = sscale + stage * T + col0;
+#pragma unroll
+        for (int cc = 0; cc < C::TC / 16; ++cc) {
+          if (col0 + cc * 16 < rows) {  // warp-uniform
+            uint32_t r0[16], r1[16];
+            const uint32_t col = (uint32_t)(buf * 2 * T + col0 + cc * 16);
+            tmem_ld16(tmem_base + lane_base + col, r0);
+            tmem_ld16(tmem_base + lane_base + col + T, r1);
+            tmem_wait_ld16(r0);
+            tmem_wait_ld16(r1);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float as = ss[cc * 16 + i];
+              acc[0][cc * 16 + i] = fmaf(__uint_as_float(r0[i]), ws0 * as, acc[0][cc * 16 + i]);
+              acc[1][cc * 16 + i] = fmaf(__uint_as_float(r1[i]), ws1 * as, acc[1][cc * 16 + i]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&tempty[buf]);
+          mbar_arrive(&empty[stage]);
+        }
+        ws0 = ws0n;
+        ws1 = ws1n;
+        if (++stage == C::NSTAGE) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (++buf == C::NBUF) {
+          buf = 0;
+          bphase ^= 1;
+        }
+      }
+      if (!ok) {
+        atomicOr(p.err, ERR_DEV_TIMEOUT);
+        *abort_flag = 1;
+      }
+
+      if constexpr (EPI == EPI_SILU) {
+        // Row r of this unit: r = s*128 + q*32 + lane; gate rows are even, up rows odd.
+        // Even lanes produce inter column i = s*64 + q*16 + lane/2 of this 128-wide group.
+        const bool even = (lane & 1) == 0;
+#pragma unroll
+        for (int j = 0; j < C::TC; ++j) {
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            const float partner = __shfl_xor_sync(0xffffffffu, acc[s][j], 1);
+            acc[s][j] = even ? silu_f32(acc[s][j]) * partner : 0.f;
+          }
+          float m = fmaxf(fabsf(acc[0][j]), fabsf(acc[1][j]));
+#pragma unroll
+          for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0) red[(h * 4 + q) * T + col0 + j] = m;
+        }
+        named_bar_sync(1, EW * 32);
+        const bool stop = *abort_flag != 0;
+        if (stop) break;
+#pragma unroll
+        for (int j = 0; j < C::TC; ++j) {
+          const float* rr = red + h * 4 * T + col0 + j;
+          const float amax = fmaxf(fmaxf(rr[0], rr[T]), fmaxf(rr[2 * T], rr[3 * T]));
+          const float scale = group_scale(amax);
+          if (even) {
+            const int c = col0 + j;
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+              const int i = s * 64 + q * 16 + (lane >> 1);
+              staging[c * 128 + i] = quant_e4m3(acc[s][j], scale);
+            }
+          }
+          if (q == 0 && lane == (j & 31) && col0 + j < rows)
+            p.out_sT[(int64_t)nt * p.out_s_ld + p0 + col0 + j] = scale;
+        }
+        named_bar_sync(1, EW * 32);
+        // Coalesced copy of the quantised rows: 8 x 16 B per row.
+        const int tid = threadIdx.x - 64;
+        for (int idx = tid; idx < rows * 8; idx += EW * 32) {
+          const int c = idx >> 3, part = idx & 7;
+          const uint4 v = *reinterpret_cast<const uint4*>(staging + c * 128 + part * 16);
+          *reinterpret_cast<uint4*>(p.out_q + (int64_t)(p0 + c) * p.out_q_ld + nt * 128 + part * 16) = v;
+        }
+      } else {
+        if (!ok) break;
+#pragma unroll
+        for (int j = 0; j < C::TC; ++j) {
+          const int c = col0 + j;
+          if (c < rows) {
+            const int f = __ldg(&p.sorted_ids[p0 + c]);
+            if (f < p.sentinel) {
+              const float w = __ldg(&p.topk_w[f]);
+              float* dst = p.out_pair + (int64_t)f * p.Nw + nt * C::UNIT_ROWS + q * 32 + lane;
+              dst[0] = w * acc[0][j];
+              dst[128] = w * acc[1][j];
+            }
+          }
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace b200moe

@@ -1,0 +1,196 @@
+// FP8 quantisation kernels (HBM-bound) and the top-k combine reduction.
+#include "common.cuh"
+#include "launch.h"
+#include "ptx.cuh"
+
+namespace b200moe {
+
+// ---------------------------------------------------------------------------
+// 1 x 128 per-token-group quantisation (per_token_group_quant_fp8,
+// phase5_orchestrator.py:26-32). One warp per output row; each lane converts 8
+// consecutive bf16 (one 16-byte load), a half-warp covers one 128-column
+// group, so a warp step handles 256 columns.
+// ---------------------------------------------------------------------------
+constexpr int kQuantWarps = 8;
+
+__global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const QuantArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
+  const int64_t n_rows = a.num_rows ? (int64_t)(*a.num_rows) : a.rows;
+  if (row >= n_rows || row >= a.rows) return;
+  int64_t src = row;
+  if (a.sorted_ids) {
+    const int f = __ldg(&a.sorted_ids[row]);
+    src = (f >= 0 && f < a.sentinel) ? (int64_t)(f / a.topk) : -1;
+  }
+  const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
+  uint8_t* qr = a.q + row * a.ldq;
+  for (int64_t c0 = 0; c0 < a.K; c0 += 256) {
+    const int64_t c = c0 + lane * 8;
+    const bool in = c < a.K;
+    float v[8];
+    if (src >= 0 && in) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + c));
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f2 = __bfloat1622float2(h2[i]);
+        v[2 * i] = f2.x;
+        v[2 * i + 1] = f2.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (!in) continue;
+    uint32_t lo = 0, hi = 0;
+    float scale = 0.f;
+    if (src >= 0) {
+      scale = group_scale(m);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) lo |= (uint32_t)quant_e4m3(v[i], scale) << (8 * i);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hi |= (uint32_t)quant_e4m3(v[4 + i], scale) << (8 * i);
+    }
+    *reinterpret_cast<uint2*>(qr + c) = make_uint2(lo, hi);
+    if ((lane & 15) == 0) a.s[row * a.s_row + (c >> 7) * a.s_grp] = scale;
+  }
+}
+
+cudaError_t launch_quant_1x128(const QuantArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return cudaSuccess;
+  const int64_t blocks = (a.rows + kQuantWarps - 1) / kQuantWarps;
+  quant_1x128_kernel<<<(unsigned)blocks, kQuantWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// 128 x 128 block quantisation of weights (per_block_quant_fp8,
+// phase5_orchestrator.py:35-41). One CTA of 256 threads per block; thread t
+// owns row t/2, columns (t%2)*64 .. +64.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) quant_block128_kernel(const __nv_bfloat16* __restrict__ w, int64_t N,
+                                                             int64_t K, uint8_t* __restrict__ q,
+                                                             float* __restrict__ s) {
+  __shared__ float wmax[8];
+  const int kb = blockIdx.x, nb = blockIdx.y;
+  const int64_t e = blockIdx.z;
+  const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int64_t off = (e * N + (int64_t)nb * 128 + r) * K + (int64_t)kb * 128 + half * 64;
+  float v[64];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(w + off) + i);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f2 = __bfloat1622float2(h2[k]);
+      v[i * 8 + 2 * k] = f2.x;
+      v[i * 8 + 2 * k + 1] = f2.y;
+    }
+  }
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) m = fmaxf(m, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float amax = wmax[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, wmax[i]);
+  const float scale = group_scale(amax);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t word[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t b = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) b |= (uint32_t)quant_e4m3(v[i * 16 + k * 4 + t], scale) << (8 * t);
+      word[k] = b;
+    }
+    *reinterpret_cast<uint4*>(q + off + i * 16) = make_uint4(word[0], word[1], word[2], word[3]);
+  }
+  if (threadIdx.x == 0) s[(e * (N / 128) + nb) * (K / 128) + kb] = scale;
+}
+
+cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K, uint8_t* q, float* s,
+                                  cudaStream_t stream) {
+  if (E <= 0) return cudaSuccess;
+  dim3 grid((unsigned)(K / 128), (unsigned)(N / 128), (unsigned)E);
+  quant_block128_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(w), N, K, q, s);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Top-k combine: out[t, n] = bf16(sum_j pair[t*topk + j, n]) over valid slots,
+// summed in slot order (the view(M, k, K).sum(1) of
+// sglang_integration/aiter.py:176-177, on fp32 rows that already carry the
+// router weight). One thread per 8 output columns.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __restrict__ pair,
+                                                             const int32_t* __restrict__ ids,
+                                                             const int32_t* __restrict__ emap, int num_experts,
+                                                             int64_t M, int topk, int64_t H,
+                                                             __nv_bfloat16* __restrict__ out) {
+  const int64_t per_row = H / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t t = idx / per_row;
+  if (t >= M) return;
+  const int64_t c = (idx - t * per_row) * 8;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int j = 0; j < topk; ++j) {
+    const int id = __ldg(&ids[t * topk + j]);
+    bool valid = id >= 0 && id < num_experts;
+    if (valid && emap) valid = __ldg(&emap[id]) >= 0;
+    if (!valid) continue;
+    const float4* src = reinterpret_cast<const float4*>(pair + (t * topk + j) * H + c);
+    const float4 a = __ldg(src), b = __ldg(src + 1);
+    acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+    acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+  }
+  __nv_bfloat162 o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+  *reinterpret_cast<uint4*>(out + t * H + c) = *reinterpret_cast<const uint4*>(o);
+}
+
+cudaError_t launch_combine_reduce(const float* pair, const int32_t* ids, const int32_t* expert_map,
+                                  int num_experts, int64_t M, int topk, int64_t H, void* out, cudaStream_t stream) {
+  const int64_t n = M * (H / 8);
+  if (n <= 0) return cudaSuccess;
+  const int64_t blocks = (n + 255) / 256;
+  combine_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pair, ids, expert_map, num_experts, M, topk, H,
+                                                              reinterpret_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Bounded-wait self test: waits on an mbarrier that nothing completes.
+// ---------------------------------------------------------------------------
+__global__ void wait_timeout_selftest_kernel(int32_t* err, uint64_t timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!mbar_wait_bounded(&bar, 0, timeout_ns)) atomicOr(err, ERR_DEV_TIMEOUT);
+  }
+}
+
+cudaError_t launch_wait_timeout_selftest(int32_t* err, uint64_t timeout_ns, cudaStream_t stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(err, timeout_ns);
+  return cudaGetLastError();
+}
+
+}  // namespace b200moe

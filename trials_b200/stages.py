@@ -1,0 +1,203 @@
+"""Stage-level calls of the layer (route -> gather/quantise -> GEMM1+SiLU ->
+GEMM2+combine -> top-k reduce) on explicit torch buffers.
+
+These mirror the reference's kernel launchers (moe_decode_megakernel_stage1,
+..._stage1_fused with fused_silu, ..._stage2_fused:
+aiter_module/moe_decode_megakernel.py:88-123,
+aiter_module/moe_decode_megakernel_fused.py:125-157) on the library's own
+expert-sorted row layout (each expert padded to 16 rows).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .moe import FP8, _ptr, _require_cuda, _stream
+
+
+@dataclass
+class Routing:
+    tile_tokens: int
+    rows_cap: int
+    chunks_cap: int
+    sorted_ids: torch.Tensor    # (rows_cap,) int32
+    chunk_expert: torch.Tensor  # (chunks_cap,) int32
+    chunk_row0: torch.Tensor
+    chunk_rows: torch.Tensor
+    counts: torch.Tensor        # [n_chunks, num_rows] int32
+    err: torch.Tensor           # (1,) int32
+
+    @property
+    def n_chunks(self):
+        return self.counts[0:1]
+
+    @property
+    def num_rows(self):
+        return self.counts[1:2]
+
+    def a_s_ld(self) -> int:
+        return (self.rows_cap + 128 + 63) // 64 * 64
+
+
+def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map: Optional[torch.Tensor] = None,
+          num_local_experts: Optional[int] = None, err: Optional[torch.Tensor] = None) -> Routing:
+    dev = _require_cuda(topk_ids)
+    ids = topk_ids.to(torch.int32).contiguous()
+    M, topk = ids.shape
+    E = num_local_experts if expert_map is not None else num_experts
+    L = _lib.lib()
+    rows_cap = L.b200moe_route_capacity_rows(M * topk, E)
+    chunks_cap = L.b200moe_route_capacity_chunks(M * topk, E, tile_tokens)
+    z = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=dev)  # noqa: E731
+    r = Routing(tile_tokens, rows_cap, chunks_cap, z(rows_cap), z(chunks_cap), z(chunks_cap), z(chunks_cap),
+                torch.zeros(2, dtype=torch.int32, device=dev),
+                err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev))
+    if expert_map is not None:
+        expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
+    _lib.check(L.b200moe_route(_ptr(ids), M, topk, num_experts, _ptr(expert_map), E, tile_tokens,
+                               _ptr(r.sorted_ids), rows_cap, _ptr(r.chunk_expert), _ptr(r.chunk_row0),
+                               _ptr(r.chunk_rows), chunks_cap, _ptr(r.n_chunks), _ptr(r.num_rows), _ptr(r.err),
+                               _stream(dev)), "route")
+    return r
+
+
+def gather_quant(hidden: torch.Tensor, topk: int, r: Routing):
+    """-> (a_q (rows_cap, H) e4m3, a_sT (H/128, ld) f32) in sorted row order."""
+    dev = _require_cuda(hidden)
+    hidden = hidden.contiguous()
+    M, H = hidden.shape
+    ld = r.a_s_ld()
+    a_q = torch.empty(r.rows_cap, H, dtype=FP8, device=dev)
+    a_sT = torch.empty(H // 128, ld, dtype=torch.float32, device=dev)
+    _lib.check(_lib.lib().b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(r.sorted_ids), _ptr(r.num_rows),
+                                               r.rows_cap, _ptr(a_q), _ptr(a_sT), ld, _stream(dev)), "gather_quant")
+    return a_q, a_sT
+
+
+def gemm1_silu(a1_q, a1_sT, w13, w13_scale, r: Routing, grid_ctas: int = 0):
+    """-> (a2_q (rows_cap, I) e4m3, a2_sT (I/128, ld) f32)."""
+    dev = _require_cuda(a1_q, w13)
+    E, N2, H = w13.shape
+    I = N2 // 2
+    ld = r.a_s_ld()
+    a2_q = torch.zeros(r.rows_cap, I, dtype=FP8, device=dev)
+    a2_sT = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
+    _lib.check(_lib.lib().b200moe_gemm1_silu(
+        _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13), _ptr(w13_scale.contiguous()), E, H, I,
+        _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows), _ptr(r.n_chunks), r.chunks_cap,
+        r.tile_tokens, _ptr(a2_q), _ptr(a2_sT), _ptr(r.err), grid_ctas, _stream(dev)), "gemm1_silu")
+    return a2_q, a2_sT
+
+
+def gemm2_combine(a2_q, a2_sT, w2, w2_scale, r: Routing, topk_weights: torch.Tensor, grid_ctas: int = 0,
+                  out_pair: Optional[torch.Tensor] = None):
+    """-> out_pair (M*topk, H) f32 (rows of dropped slots untouched)."""
+    dev = _require_cuda(a2_q, w2)
+    E, H, I = w2.shape
+    M, topk = topk_weights.shape
+    tw = topk_weights.to(torch.float32).contiguous()
+    if out_pair is None:
+        out_pair = torch.zeros(M * topk, H, dtype=torch.float32, device=dev)
+    _lib.check(_lib.lib().b200moe_gemm2_combine(
+        _ptr(a2_q), _ptr(a2_sT), r.a_s_ld(), r.rows_cap, _ptr(w2), _ptr(w2_scale.contiguous()), E, H, I,
+        _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows), _ptr(r.n_chunks), r.chunks_cap,
+        r.tile_tokens, _ptr(r.sorted_ids), _ptr(tw), M, topk, _ptr(out_pair), _ptr(r.err), grid_ctas,
+        _stream(dev)), "gemm2_combine")
+    return out_pair
+
+
+def combine_reduce(out_pair: torch.Tensor, topk_ids: torch.Tensor, num_experts: int,
+                   expert_map: Optional[torch.Tensor] = None) -> torch.Tensor:
+    dev = _require_cuda(out_pair, topk_ids)
+    ids = topk_ids.to(torch.int32).contiguous()
+    M, topk = ids.shape
+    H = out_pair.shape[1]
+    out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    if expert_map is not None:
+        expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
+    _lib.check(_lib.lib().b200moe_combine_reduce(_ptr(out_pair), _ptr(ids), _ptr(expert_map), num_experts, M,
+                                                 topk, H, _ptr(out), _stream(dev)), "combine_reduce")
+    return out
+
+
+def selftest_wait_timeout(err: torch.Tensor, timeout_us: int = 20000) -> None:
+    dev = _require_cuda(err)
+    _lib.check(_lib.lib().b200moe_selftest_wait_timeout(_ptr(err), timeout_us, _stream(dev)), "selftest")
+
+
+def pick_tile_tokens(numel: int, num_local_experts: int) -> int:
+    """Token columns per GEMM unit; the same rule as the C layer (capi.cu)."""
+    avg = numel / max(num_local_experts, 1)
+    if avg <= 12.0:
+        return 32
+    if avg <= 40.0:
+        return 64
+    return 128
+
+
+class LayerPipeline:
+    """The five launches of the layer on preallocated buffers, with optional
+    CUDA events between stages (used by the benchmark to time each kernel on
+    the launching stream). Same kernels and order as b200moe_layer."""
+
+    STAGES = ("route", "gather_quant", "gemm1_silu", "gemm2_combine", "combine_reduce")
+
+    def __init__(self, M: int, H: int, I: int, num_experts: int, topk: int, device, tile_tokens: int = 0,
+                 expert_map: Optional[torch.Tensor] = None, num_local_experts: Optional[int] = None):
+        self.M, self.H, self.I, self.topk = M, H, I, topk
+        self.num_experts = num_experts
+        self.E = num_local_experts if expert_map is not None else num_experts
+        self.expert_map = None if expert_map is None else expert_map.to(device=device, dtype=torch.int32).contiguous()
+        self.device = torch.device(device)
+        L = _lib.lib()
+        numel = M * topk
+        self.tile = tile_tokens or pick_tile_tokens(numel, self.E)
+        self.rows_cap = L.b200moe_route_capacity_rows(numel, self.E)
+        self.chunks_cap = L.b200moe_route_capacity_chunks(numel, self.E, self.tile)
+        self.ld = (self.rows_cap + 128 + 63) // 64 * 64
+        z = lambda n: torch.zeros(max(n, 1), dtype=torch.int32, device=device)  # noqa: E731
+        self.sorted_ids, self.ce, self.cr0, self.crows = z(self.rows_cap), z(self.chunks_cap), z(self.chunks_cap), \
+            z(self.chunks_cap)
+        self.counts = z(2)
+        self.err = z(1)
+        self.a1 = torch.zeros(self.rows_cap, H, dtype=FP8, device=device)
+        self.a1s = torch.zeros(H // 128, self.ld, dtype=torch.float32, device=device)
+        self.a2 = torch.zeros(self.rows_cap, I, dtype=FP8, device=device)
+        self.a2s = torch.zeros(I // 128, self.ld, dtype=torch.float32, device=device)
+        self.pair = torch.zeros(max(numel, 1), H, dtype=torch.float32, device=device)
+        self.out = torch.zeros(M, H, dtype=torch.bfloat16, device=device)
+
+    def run(self, hidden, topk_ids, topk_weights, w13, w13_scale, w2, w2_scale, events=None, grid_ctas: int = 0):
+        L = _lib.lib()
+        st = _stream(self.device)
+        ev = events or [None] * 6
+        rec = lambda i: ev[i].record() if ev[i] is not None else None  # noqa: E731
+        M, H, I, topk, E = self.M, self.H, self.I, self.topk, self.E
+        cnt = _ptr(self.counts)
+        rows = cnt + 4
+        rec(0)
+        _lib.check(L.b200moe_route(_ptr(topk_ids), M, topk, self.num_experts, _ptr(self.expert_map), E, self.tile,
+                                   _ptr(self.sorted_ids), self.rows_cap, _ptr(self.ce), _ptr(self.cr0),
+                                   _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.err), st), "route")
+        rec(1)
+        _lib.check(L.b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(self.sorted_ids), rows, self.rows_cap,
+                                          _ptr(self.a1), _ptr(self.a1s), self.ld, st), "gather_quant")
+        rec(2)
+        _lib.check(L.b200moe_gemm1_silu(_ptr(self.a1), _ptr(self.a1s), self.ld, self.rows_cap, _ptr(w13),
+                                        _ptr(w13_scale), E, H, I, _ptr(self.ce), _ptr(self.cr0), _ptr(self.crows),
+                                        cnt, self.chunks_cap, self.tile, _ptr(self.a2), _ptr(self.a2s),
+                                        _ptr(self.err), grid_ctas, st), "gemm1_silu")
+        rec(3)
+        _lib.check(L.b200moe_gemm2_combine(_ptr(self.a2), _ptr(self.a2s), self.ld, self.rows_cap, _ptr(w2),
+                                           _ptr(w2_scale), E, H, I, _ptr(self.ce), _ptr(self.cr0), _ptr(self.crows),
+                                           cnt, self.chunks_cap, self.tile, _ptr(self.sorted_ids),
+                                           _ptr(topk_weights), M, topk, _ptr(self.pair), _ptr(self.err), grid_ctas,
+                                           st), "gemm2_combine")
+        rec(4)
+        _lib.check(L.b200moe_combine_reduce(_ptr(self.pair), _ptr(topk_ids), _ptr(self.expert_map),
+                                            self.num_experts, M, topk, H, _ptr(self.out), st), "combine_reduce")
+        rec(5)
+        return self.out
