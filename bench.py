@@ -42,11 +42,12 @@ METRIC = "MoE layer tokens/s + HBM GB/s at M=64–1024, FP8 128x128 blockscale, 
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--M", type=int, default=64, help="tokens per GPU")
     ap.add_argument("--hot", type=int, default=0, help="experts with +2.0 router bias (skewed load)")
+    ap.add_argument("--experts", type=int, default=256, help="routed experts (fewer only for small profiles)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-sample-experts", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -81,52 +82,71 @@ def ncu_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples of one GPU during the timed region."""
+    """nvidia-smi clock / throttle samples of one GPU, kept for the timed region."""
 
     FIELDS = ["clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.hw_slowdown",
               "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
               "clocks_event_reasons.sw_power_cap"]
+    REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.samples = []  # (time, sm_mhz, max_mhz, reasons)
+        self.windows = []
 
-    def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + ",".join(self.FIELDS),
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, FileNotFoundError):
-            self.proc = None
-
-    def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, smax, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+    def _reader(self):
+        for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) != len(self.FIELDS):
                 continue
             try:
-                sm.append(float(parts[0]))
-                smax = max(smax, float(parts[1]))
+                sm, smax = float(parts[0]), float(parts[1])
             except ValueError:
                 continue
-            for n, v in zip(names, parts[3:]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
+            act = {n for n, v in zip(self.REASONS, parts[3:]) if v.lower().startswith("active")}
+            self.samples.append((time.monotonic(), sm, smax, act))
+
+    def start(self):
+        import threading
+
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + ",".join(self.FIELDS),
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        threading.Thread(target=self._reader, daemon=True).start()
+        t0 = time.monotonic()
+        while not self.samples and time.monotonic() - t0 < 5.0:
+            time.sleep(0.02)
+
+    def mark(self):
+        return time.monotonic()
+
+    def window(self, t0, t1):
+        self.windows.append((t0, t1))
+
+    def stop(self):
+        if self.proc is None:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        time.sleep(0.12)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sel = [s for s in self.samples if any(a - 0.06 <= s[0] <= b + 0.06 for a, b in self.windows)]
+        if not sel and self.samples and self.windows:
+            mid = self.windows[0][0]
+            sel = [min(self.samples, key=lambda s: abs(s[0] - mid))]
+        if not sel:
+            return None
+        reasons = sorted(set().union(*[s[3] for s in sel]))
+        return {"sm_mhz": statistics.median(s[1] for s in sel), "sm_max_mhz": max(s[2] for s in sel),
+                "reasons": reasons, "samples": len(sel)}
 
 
 def dist_setup(backend):
@@ -279,14 +299,15 @@ def run_ours(args, shape, config):
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
-    barrier()
     clocks.start()
+    barrier()
+    t0 = clocks.mark()
     start.record()
     for k in range(args.steps):
         pipe.run(*args_run, events=evs[k])
     end.record()
     barrier()
-    clk = clocks.stop()
+    clocks.window(t0, clocks.mark())
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
     stage_ms = {name: statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(args.steps))
                 for i, name in enumerate(stages.LayerPipeline.STAGES)}
@@ -315,15 +336,19 @@ def run_ours(args, shape, config):
             e2e_step()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
+        t0 = clocks.mark()
         s2.record()
         for _ in range(args.steps):
             e2e_step()
         e2.record()
         barrier()
+        clocks.window(t0, clocks.mark())
         ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps)
         h2d = h_host.numel() * 2 + ids_host.numel() * 4 + tw_host.numel() * 4
         e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": out_host.numel() * 2, "ms_per_step": ms_e2e}
+
+    clk = clocks.stop()
 
     # ---- CPU baseline (rank 0, one GPU only)
     cpu = None
@@ -380,8 +405,13 @@ def main(argv=None):
     from trials_b200 import synth
 
     shape = synth.glm(args.M, args.hot)
+    if args.experts != shape.E:
+        from dataclasses import replace
+
+        shape = replace(shape, E=args.experts)
     ws = int(os.environ.get("WORLD_SIZE", "1"))
-    config = {"workload": f"glm_decode_M{args.M}" + (f"_hot{args.hot}" if args.hot else ""),
+    config = {"workload": f"glm_decode_M{args.M}" + (f"_hot{args.hot}" if args.hot else "") +
+                          (f"_E{shape.E}" if shape.E != 256 else ""),
               "tokens_per_gpu": shape.M, "hidden": shape.H, "moe_intermediate": shape.I, "experts": shape.E,
               "topk": shape.topk, "router": "sigmoid top-k, renormalised",
               "quant": "e4m3 weights with fp32 128x128 block scales, 1x128 activation scales",

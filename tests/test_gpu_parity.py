@@ -117,7 +117,9 @@ def test_route_chunks_exact(cuda_device, M, E, topk, tile):
     nc = int(r.counts[0].item())
     assert int(r.counts[1].item()) == rn
     assert nc == len(chunks)
-    assert np.array_equal(r.sorted_ids.cpu().numpy(), rs)
+    got_sorted = r.sorted_ids.cpu().numpy()
+    assert np.array_equal(got_sorted[:rn], rs[:rn])
+    assert (got_sorted[rn:] == M * topk).all() and (rs[rn:] == M * topk).all()
     got = np.stack([r.chunk_expert[:nc].cpu().numpy(), r.chunk_row0[:nc].cpu().numpy(),
                     r.chunk_rows[:nc].cpu().numpy()], 1)
     assert np.array_equal(got, chunks)

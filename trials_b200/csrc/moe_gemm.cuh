@@ -80,17 +80,22 @@ struct GemmCfg {
   static constexpr int W_BYTES = UNIT_ROWS * 128;
   static constexpr int A_BYTES = T * 128;
   static constexpr int TILE_BYTES = W_BYTES + A_BYTES;  // multiple of 1024
-  static constexpr int S_BYTES = T * 4;                 // activation scales per stage
-  static constexpr uint32_t STAGE_TX = TILE_BYTES + S_BYTES;
+  static constexpr int S_BYTES = T * 4;                 // activation scales of one K block
   static constexpr int NBUF = 512 / (NSUB * T);         // TMEM partial buffers
   static constexpr int TMEM_COLS = 512;
   static constexpr int STAGING = T * 128;               // EPI_SILU output tile
   static constexpr int RED = 4 * COL_SPLIT * T * 4;     // EPI_SILU amax exchange
   static constexpr int SMEM_LIMIT = 232448;
-  static constexpr int FIXED = 1024 /*align slack*/ + STAGING + RED + 1024 /*barriers etc*/;
-  static constexpr int NSTAGE_RAW = (SMEM_LIMIT - FIXED) / (TILE_BYTES + S_BYTES);
-  static constexpr int NSTAGE = NSTAGE_RAW > 8 ? 8 : NSTAGE_RAW;
-  static constexpr int SMEM_BYTES = FIXED + NSTAGE * (TILE_BYTES + S_BYTES);
+  static constexpr int MAX_STAGE = 8;
+  // Scale ring: the producer can run at most NSTAGE K blocks ahead of the MMA,
+  // which runs at most NBUF ahead of the epilogue, so NSTAGE + NBUF slots never
+  // make the producer wait on the epilogue.
+  static constexpr int FIXED = 1024 /*align slack*/ + STAGING + RED + (MAX_STAGE + NBUF) * S_BYTES +
+                               1024 /*barriers etc*/;
+  static constexpr int NSTAGE_RAW = (SMEM_LIMIT - FIXED) / TILE_BYTES;
+  static constexpr int NSTAGE = NSTAGE_RAW > MAX_STAGE ? MAX_STAGE : NSTAGE_RAW;
+  static constexpr int NSLOT = NSTAGE + NBUF;
+  static constexpr int SMEM_BYTES = FIXED + NSTAGE * TILE_BYTES;
   static_assert(T % 16 == 0 && T >= 16 && T <= 256, "MMA N must be a multiple of 16 in [16, 256]");
   static_assert(EW % 4 == 0, "epilogue warps must cover the 4 TMEM lane quarters");
   static_assert(TC % 16 == 0, "columns per thread must be a multiple of 16");
@@ -110,14 +115,16 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
   // 1024-byte alignment for the 128B-swizzled TMA tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;                                             // NSTAGE * TILE_BYTES
-  float* sscale = reinterpret_cast<float*>(tiles + C::NSTAGE * C::TILE_BYTES);  // NSTAGE * T
-  uint8_t* staging = reinterpret_cast<uint8_t*>(sscale + C::NSTAGE * T);      // T * 128
+  float* sscale = reinterpret_cast<float*>(tiles + C::NSTAGE * C::TILE_BYTES);  // NSLOT * T
+  uint8_t* staging = reinterpret_cast<uint8_t*>(sscale + C::NSLOT * T);       // T * 128
   float* red = reinterpret_cast<float*>(staging + C::STAGING);                // 4 * COL_SPLIT * T
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + C::RED);
   uint64_t* empty = full + C::NSTAGE;
   uint64_t* tfull = empty + C::NSTAGE;
   uint64_t* tempty = tfull + C::NBUF;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + C::NBUF);
+  uint64_t* sfull = tempty + C::NBUF;
+  uint64_t* sempty = sfull + C::NSLOT;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + C::NSLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -128,11 +135,15 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + EW);  // MMA commit + each epilogue warp (scales read)
+      mbar_init(&empty[s], 1);  // released by the MMA commit
     }
     for (int b = 0; b < C::NBUF; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], EW);
+    }
+    for (int s = 0; s < C::NSLOT; ++s) {
+      mbar_init(&sfull[s], 1);
+      mbar_init(&sempty[s], EW);  // released by every epilogue warp
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -157,8 +168,8 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
+      int stage = 0, slot = 0;
+      uint32_t phase = 0, sphase = 0;
       long issued = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
@@ -168,29 +179,38 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
         const int p0 = __ldg(&p.chunk_row0[chunk]);
         const int wrow = e * p.Nw + nt * C::UNIT_ROWS;
         for (int kb = 0; kb < NKB; ++kb) {
-          if (*abort_flag || !mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns)) {
+          if (*abort_flag || !mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns) ||
+              !mbar_wait_bounded(&sempty[slot], sphase ^ 1, p.timeout_ns)) {
             ok = false;
             break;
           }
           uint8_t* tile = tiles + stage * C::TILE_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_TX);
+          mbar_arrive_expect_tx(&full[stage], C::TILE_BYTES);
           tma_load_2d(tile, &tm_w, &full[stage], kb * 128, wrow, pol_w);
           tma_load_2d(tile + C::W_BYTES, &tm_a, &full[stage], kb * 128, p0, pol_a);
-          bulk_load(sscale + stage * T, p.a_sT + (int64_t)kb * p.as_ld + p0, C::S_BYTES, &full[stage]);
+          mbar_arrive_expect_tx(&sfull[slot], C::S_BYTES);
+          bulk_load(sscale + slot * T, p.a_sT + (int64_t)kb * p.as_ld + p0, C::S_BYTES, &sfull[slot]);
           ++issued;
           if (++stage == C::NSTAGE) {
             stage = 0;
             phase ^= 1;
+          }
+          if (++slot == C::NSLOT) {
+            slot = 0;
+            sphase ^= 1;
           }
         }
       }
       if (!ok) {
         atomicOr(p.err, ERR_DEV_TIMEOUT);
         *abort_flag = 1;
-        // Let every load already issued land before the CTA exits.
+        // Let every copy already issued land before the CTA exits.
         long first = issued > C::NSTAGE ? issued - C::NSTAGE : 0;
         for (long g = first; g < issued; ++g)
           mbar_wait_bounded(&full[g % C::NSTAGE], (uint32_t)((g / C::NSTAGE) & 1), p.timeout_ns);
+        first = issued > C::NSLOT ? issued - C::NSLOT : 0;
+        for (long g = first; g < issued; ++g)
+          mbar_wait_bounded(&sfull[g % C::NSLOT], (uint32_t)((g / C::NSLOT) & 1), p.timeout_ns);
       }
     }
   } else if (warp == 1) {
@@ -257,8 +277,8 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
     const int h = ew >> 2;                   // column slice
     const int col0 = h * C::TC;              // first token column of this thread
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    int stage = 0, buf = 0;
-    uint32_t phase = 0, bphase = 0;
+    int slot = 0, buf = 0;
+    uint32_t sphase = 0, bphase = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int chunk = u / NT;
@@ -284,13 +304,11 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
           break;
         }
         tc_fence_after();
-        // Acquire the stage's TMA writes (the activation scales) directly; the
-        // phase completed before the MMA ran, so this returns at once.
-        if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns)) {
+        if (!mbar_wait_bounded(&sfull[slot], sphase, p.timeout_ns)) {
           ok = false;
           break;
         }
-        const float* ss = sscale + stage * T + col0;
+        const float* ss = sscale + slot * T + col0;
 #pragma unroll
         for (int cc = 0; cc < C::TC / 16; ++cc) {
           if (col0 + cc * 16 < rows) {  // warp-uniform
@@ -312,13 +330,13 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&tempty[buf]);
-          mbar_arrive(&empty[stage]);
+          mbar_arrive(&sempty[slot]);
         }
         ws0 = ws0n;
         ws1 = ws1n;
-        if (++stage == C::NSTAGE) {
-          stage = 0;
-          phase ^= 1;
+        if (++slot == C::NSLOT) {
+          slot = 0;
+          sphase ^= 1;
         }
         if (++buf == C::NBUF) {
           buf = 0;
