@@ -46,24 +46,32 @@ GROUP = 128
 # ----------------------------------------------------------------------------
 # Quantisation
 # ----------------------------------------------------------------------------
+# Both quantisers run on the CPU whatever the input device: torch's CUDA kernels
+# evaluate "tensor / python scalar" as a multiplication by the reciprocal, which
+# is not the IEEE division the reference's formula (evaluated on the CPU) uses,
+# and a one-ulp change of a scale flips fp8 roundings.
 def per_token_group_quant_fp8(x: torch.Tensor, gk: int = GROUP):
     """(M, K) -> (q e4m3 (M, K), s fp32 (M, K/gk)). phase5_orchestrator.py:26-32."""
+    dev = x.device
+    x = x.cpu()
     M, K = x.shape
     xg = x.reshape(M, K // gk, gk)
     amax = xg.abs().amax(dim=-1).float()
     scale = (amax / FP8_MAX).clamp(min=1e-12)
     q = (xg.float() / scale.unsqueeze(-1)).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn).reshape(M, K)
-    return q, scale
+    return q.to(dev), scale.to(dev)
 
 
 def per_block_quant_fp8(w: torch.Tensor, bn: int = GROUP, bk: int = GROUP):
     """(E, N, K) -> (q e4m3, s fp32 (E, N/bn, K/bk)). phase5_orchestrator.py:35-41."""
+    dev = w.device
+    w = w.cpu()
     E, N, K = w.shape
     wg = w.reshape(E, N // bn, bn, K // bk, bk)
     amax = wg.abs().amax(dim=(2, 4)).float()
     scale = (amax / FP8_MAX).clamp(min=1e-12)
     q = (wg.float() / scale.unsqueeze(2).unsqueeze(4)).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
-    return q.reshape(E, N, K), scale
+    return q.reshape(E, N, K).to(dev), scale.to(dev)
 
 
 def dequant_rows(q: torch.Tensor, s: torch.Tensor, dtype=torch.float64):

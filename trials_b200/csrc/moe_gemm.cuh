@@ -106,6 +106,29 @@ struct GemmCfg {
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + __expf(-g)); }
 
+// Max over the 32 lanes of each of N per-lane values (N = 16 or 32), returned
+// transposed: lane l receives the max of value (l % N). Butterfly that halves
+// the values a lane keeps at each step (N - 1 shuffles for N = 32).
+template <int N>
+__device__ __forceinline__ float warp_transpose_max(const float* vals, int lane) {
+  static_assert(N == 16 || N == 32, "16 or 32 values");
+  float m[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) m[i] = fabsf(vals[i]);
+#pragma unroll
+  for (int o = N / 2; o >= 1; o >>= 1) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = hi ? m[i] : m[i + o];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, o);
+      m[i] = fmaxf(hi ? m[i + o] : m[i], recv);
+    }
+  }
+  if (N == 16) m[0] = fmaxf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 16));
+  return m[0];
+}
+
 template <int T, int EW, int EPI>
 __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
@@ -349,47 +372,56 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
       }
 
       if constexpr (EPI == EPI_SILU) {
-        // Row r of this unit: r = s*128 + q*32 + lane; gate rows are even, up rows odd.
-        // Even lanes produce inter column i = s*64 + q*16 + lane/2 of this 128-wide group.
-        const bool even = (lane & 1) == 0;
+        // Lane pair (2k, 2k+1) of quarter q holds weight rows s*128 + q*32 + 2k
+        // (gate) and + 1 (up) of both halves s. The even lane produces inter for
+        // half 0 and the odd lane for half 1, i.e. inter column
+        // i = s*64 + q*16 + k with s = lane & 1: one SiLU per lane and column.
+        const int sh = lane & 1;
+        const int icol = sh * 64 + q * 16 + (lane >> 1);
+        float v[C::TC];
 #pragma unroll
         for (int j = 0; j < C::TC; ++j) {
+          const float send = sh ? acc[0][j] : acc[1][j];
+          const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+          const float gate = sh ? recv : acc[0][j];
+          const float up = sh ? acc[1][j] : recv;
+          v[j] = silu_f32(gate) * up;
+        }
+        // Column amax over the warp, transposed: lane l ends with column l of
+        // each 32-column group (31 shuffles per group instead of 5 per column).
+        constexpr int NG = (C::TC + 31) / 32;
+        float colmax[NG];
 #pragma unroll
-          for (int s = 0; s < 2; ++s) {
-            const float partner = __shfl_xor_sync(0xffffffffu, acc[s][j], 1);
-            acc[s][j] = even ? silu_f32(acc[s][j]) * partner : 0.f;
-          }
-          float m = fmaxf(fabsf(acc[0][j]), fabsf(acc[1][j]));
+        for (int g = 0; g < NG; ++g) colmax[g] = warp_transpose_max<(C::TC < 32 ? C::TC : 32)>(v + g * 32, lane);
 #pragma unroll
-          for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if (lane == 0) red[(h * 4 + q) * T + col0 + j] = m;
+        for (int g = 0; g < NG; ++g) {
+          const int c = g * 32 + (lane & (C::TC < 32 ? C::TC - 1 : 31));
+          if (lane < C::TC) red[(h * 4 + q) * T + col0 + c] = colmax[g];
         }
         named_bar_sync(1, EW * 32);
         const bool stop = *abort_flag != 0;
         if (stop) break;
+        float colscale[NG];
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          const int c = col0 + g * 32 + (lane & (C::TC < 32 ? C::TC - 1 : 31));
+          const float* rr = red + h * 4 * T + c;
+          const float amax = fmaxf(fmaxf(rr[0], rr[T]), fmaxf(rr[2 * T], rr[3 * T]));
+          colscale[g] = group_scale(amax);
+          if (q == 0 && lane < C::TC && c < rows) p.out_sT[(int64_t)nt * p.out_s_ld + p0 + c] = colscale[g];
+        }
 #pragma unroll
         for (int j = 0; j < C::TC; ++j) {
-          const float* rr = red + h * 4 * T + col0 + j;
-          const float amax = fmaxf(fmaxf(rr[0], rr[T]), fmaxf(rr[2 * T], rr[3 * T]));
-          const float scale = group_scale(amax);
-          if (even) {
-            const int c = col0 + j;
-#pragma unroll
-            for (int s = 0; s < 2; ++s) {
-              const int i = s * 64 + q * 16 + (lane >> 1);
-              staging[c * 128 + i] = quant_e4m3(acc[s][j], scale);
-            }
-          }
-          if (q == 0 && lane == (j & 31) && col0 + j < rows)
-            p.out_sT[(int64_t)nt * p.out_s_ld + p0 + col0 + j] = scale;
+          const float sc = __shfl_sync(0xffffffffu, colscale[j / 32], j % 32);
+          staging[(col0 + j) * 128 + icol] = quant_e4m3(v[j], sc);
         }
         named_bar_sync(1, EW * 32);
         // Coalesced copy of the quantised rows: 8 x 16 B per row.
         const int tid = threadIdx.x - 64;
         for (int idx = tid; idx < rows * 8; idx += EW * 32) {
           const int c = idx >> 3, part = idx & 7;
-          const uint4 v = *reinterpret_cast<const uint4*>(staging + c * 128 + part * 16);
-          *reinterpret_cast<uint4*>(p.out_q + (int64_t)(p0 + c) * p.out_q_ld + nt * 128 + part * 16) = v;
+          const uint4 val = *reinterpret_cast<const uint4*>(staging + c * 128 + part * 16);
+          *reinterpret_cast<uint4*>(p.out_q + (int64_t)(p0 + c) * p.out_q_ld + nt * 128 + part * 16) = val;
         }
       } else {
         if (!ok) break;
