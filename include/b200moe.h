@@ -128,6 +128,27 @@ B200MOE_API int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t 
                   int num_local_experts, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * b200moe_layer without a workspace argument, for callers that cannot
+ * allocate device memory (a fixed memory pool, a host framework that forbids
+ * allocation inside an operator). No counterpart in the reference.
+ * Same arguments, kernels and result as b200moe_layer; the workspace is a
+ * 64 MiB device array inside the library, held by every GPU that loads it
+ * until the process exits. Layers whose b200moe_layer_workspace_size()
+ * exceeds 64 MiB are rejected with B200MOE_ERR_WORKSPACE (the GLM-5-like
+ * decode batch of 64 tokens needs about 50 MB). The call allocates nothing.
+ * The first call on each device looks up the array's device address; make it
+ * before any stream capture. All calls on a device share the array and it
+ * keeps the last call's contents: calls whose GPU work overlaps (for example
+ * on two streams) race. err_out (nullable, device int32) receives this call's
+ * device error word (B200MOE_DEVERR_* bits).
+ * ---------------------------------------------------------------------- */
+B200MOE_API int b200moe_layer_noalloc(const void* hidden, int64_t M, int64_t H, int64_t I, int num_experts,
+                                      int topk, const uint8_t* w13, const float* w13_scale, const uint8_t* w2,
+                                      const float* w2_scale, const float* topk_weights, const int32_t* topk_ids,
+                                      const int32_t* expert_map, int num_local_experts, void* out,
+                                      int32_t* err_out, void* stream);
+
+/* ------------------------------------------------------------------------
  * Stage-level entry points used by b200moe_layer, exposed for staged callers
  * and tests. They work on the layer's internal expert-sorted row layout:
  * routed rows grouped by expert, each expert padded to a multiple of 16 rows.

@@ -158,6 +158,10 @@ int run_gemm(int epi, const uint8_t* a_q, const float* a_sT, int64_t as_ld, int6
 
 }  // namespace
 
+namespace b200moe {
+int record_error(int status, const char* message) { return fail(status, "%s", message); }
+}  // namespace b200moe
+
 extern "C" {
 
 int b200moe_version(void) { return 100; }

@@ -69,4 +69,7 @@ cudaError_t launch_grouped_gemm(int epi, int tile_tokens, const CUtensorMap& tm_
 // Activation tile rows the kernel for this tile_tokens loads per stage.
 int gemm_tile_rows(int tile_tokens);
 
+// Records a message for b200moe_last_error_message() and returns status.
+int record_error(int status, const char* message);
+
 }  // namespace b200moe
