@@ -6,11 +6,11 @@ namespace b200moe {
 
 namespace {
 
-template <int T, int EW, int EPI>
+template <int T, int CS, int EPI>
 cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p, int grid,
                        cudaStream_t stream) {
-  using C = GemmCfg<T, EW>;
-  auto kernel = moe_grouped_gemm_kernel<T, EW, EPI>;
+  using C = GemmCfg<T, CS>;
+  auto kernel = moe_grouped_gemm_kernel<T, CS, EPI>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (err != cudaSuccess) return err;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_a, p);
@@ -23,11 +23,11 @@ cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorM
   switch (tile_tokens) {
     case 16:
     case 32:
-      return launch_cfg<32, 4, EPI>(tm_w, tm_a, p, grid, stream);
+      return launch_cfg<32, 1, EPI>(tm_w, tm_a, p, grid, stream);
     case 64:
-      return launch_cfg<64, 8, EPI>(tm_w, tm_a, p, grid, stream);
+      return launch_cfg<64, 1, EPI>(tm_w, tm_a, p, grid, stream);
     case 128:
-      return launch_cfg<128, 8, EPI>(tm_w, tm_a, p, grid, stream);
+      return launch_cfg<128, 2, EPI>(tm_w, tm_a, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -21,7 +21,9 @@
 // MMA of block kb+1.. overlaps the promotion of block kb.
 //
 // Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM owner),
-// warps 2.. = epilogue (EW warps; warp w reads TMEM lanes 32*(w%4)..+31).
+// warps 2.. = epilogue: 8 * CS warps, one per (TMEM lane quarter w%4, 128-row
+// half, token-column slice of T/CS columns); warp w reads TMEM lanes
+// 32*(w%4)..+31.
 //
 // Epilogues:
 //   EPI_SILU    (stage 1, gate/up interleaved rows): inter = silu(gate) * up in
@@ -68,15 +70,15 @@ struct GemmParams {
   uint64_t timeout_ns;
 };
 
-template <int T_, int EW_>
+template <int T_, int CS_>
 struct GemmCfg {
   static constexpr int T = T_;                 // max tokens (MMA N) per unit
-  static constexpr int EW = EW_;               // epilogue warps
+  static constexpr int CS = CS_;               // token-column slices of the epilogue
   static constexpr int NSUB = 2;               // 128-row halves per unit
+  static constexpr int EW = 4 * NSUB * CS;     // epilogue warps
   static constexpr int UNIT_ROWS = 128 * NSUB; // weight rows per unit
   static constexpr int THREADS = 64 + 32 * EW;
-  static constexpr int COL_SPLIT = EW / 4;     // epilogue warps sharing one TMEM lane quarter
-  static constexpr int TC = T / COL_SPLIT;     // token columns per epilogue thread
+  static constexpr int TC = T / CS;            // token columns per epilogue thread
   static constexpr int W_BYTES = UNIT_ROWS * 128;
   static constexpr int A_BYTES = T * 128;
   static constexpr int TILE_BYTES = W_BYTES + A_BYTES;  // multiple of 1024
@@ -84,7 +86,7 @@ struct GemmCfg {
   static constexpr int NBUF = 512 / (NSUB * T);         // TMEM partial buffers
   static constexpr int TMEM_COLS = 512;
   static constexpr int STAGING = T * 128;               // EPI_SILU output tile
-  static constexpr int RED = 4 * COL_SPLIT * T * 4;     // EPI_SILU amax exchange
+  static constexpr int RED = 4 * NSUB * T * 4;          // EPI_SILU amax exchange (per warp, per column)
   static constexpr int SMEM_LIMIT = 232448;
   static constexpr int MAX_STAGE = 8;
   // Scale ring: the producer can run at most NSTAGE K blocks ahead of the MMA,
@@ -97,8 +99,7 @@ struct GemmCfg {
   static constexpr int NSLOT = NSTAGE + NBUF;
   static constexpr int SMEM_BYTES = FIXED + NSTAGE * TILE_BYTES;
   static_assert(T % 16 == 0 && T >= 16 && T <= 256, "MMA N must be a multiple of 16 in [16, 256]");
-  static_assert(EW % 4 == 0, "epilogue warps must cover the 4 TMEM lane quarters");
-  static_assert(TC % 16 == 0, "columns per thread must be a multiple of 16");
+  static_assert(TC % 32 == 0, "columns per epilogue thread must be a multiple of 32");
   static_assert(NBUF >= 2, "need at least two TMEM buffers");
   static_assert(NSTAGE >= 2, "shared memory too small");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
@@ -106,34 +107,33 @@ struct GemmCfg {
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + __expf(-g)); }
 
-// Max over the 32 lanes of each of N per-lane values (N = 16 or 32), returned
-// transposed: lane l receives the max of value (l % N). Butterfly that halves
-// the values a lane keeps at each step (N - 1 shuffles for N = 32).
-template <int N>
-__device__ __forceinline__ float warp_transpose_max(const float* vals, int lane) {
-  static_assert(N == 16 || N == 32, "16 or 32 values");
-  float m[N];
+// Column maxima for values spread over lane pairs: lane l holds, for m < 16,
+// |value| of column 2m + (l & 1). Returns, in lane l, the max over the 16
+// lanes of l's parity for column l. Butterfly over lane bits 4..1 that halves
+// the values each lane keeps per step (15 shuffles).
+__device__ __forceinline__ float warp_pair_transpose_max(const float* vals, int lane) {
+  float m[16];
 #pragma unroll
-  for (int i = 0; i < N; ++i) m[i] = fabsf(vals[i]);
+  for (int i = 0; i < 16; ++i) m[i] = fabsf(vals[i]);
 #pragma unroll
-  for (int o = N / 2; o >= 1; o >>= 1) {
-    const bool hi = (lane & o) != 0;
+  for (int o = 8; o >= 1; o >>= 1) {
+    const bool hi = (lane & (2 * o)) != 0;
 #pragma unroll
     for (int i = 0; i < o; ++i) {
       const float send = hi ? m[i] : m[i + o];
-      const float recv = __shfl_xor_sync(0xffffffffu, send, o);
+      const float recv = __shfl_xor_sync(0xffffffffu, send, 2 * o);
       m[i] = fmaxf(hi ? m[i + o] : m[i], recv);
     }
   }
-  if (N == 16) m[0] = fmaxf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 16));
   return m[0];
 }
 
-template <int T, int EW, int EPI>
-__global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
+template <int T, int CS, int EPI>
+__global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                             const GemmParams p) {
-  using C = GemmCfg<T, EW>;
+  using C = GemmCfg<T, CS>;
+  constexpr int EW = C::EW;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled TMA tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -297,8 +297,8 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;                 // 0..EW-1
     const int q = warp & 3;                  // TMEM lane quarter
-    const int h = ew >> 2;                   // column slice
-    const int col0 = h * C::TC;              // first token column of this thread
+    const int hs = (ew >> 2) & 1;            // 128-row half of the unit
+    const int col0 = (ew >> 3) * C::TC;      // first token column of this warp
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     int slot = 0, buf = 0;
     uint32_t sphase = 0, bphase = 0;
@@ -309,19 +309,15 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
       const int e = __ldg(&p.chunk_expert[chunk]);
       const int p0 = __ldg(&p.chunk_row0[chunk]);
       const int rows = __ldg(&p.chunk_rows[chunk]);
-      const float* wsp0 = p.w_scale + ((int64_t)e * (p.Nw >> 7) + nt * 2) * NKB;
-      const float* wsp1 = wsp0 + NKB;
+      const float* wsp = p.w_scale + ((int64_t)e * (p.Nw >> 7) + nt * 2 + hs) * NKB;
 
-      float acc[2][C::TC];
+      float acc[C::TC];
 #pragma unroll
-      for (int s = 0; s < 2; ++s)
-#pragma unroll
-        for (int j = 0; j < C::TC; ++j) acc[s][j] = 0.f;
+      for (int j = 0; j < C::TC; ++j) acc[j] = 0.f;
 
-      float ws0 = __ldg(wsp0), ws1 = __ldg(wsp1);
+      float ws = __ldg(wsp);
       for (int kb = 0; kb < NKB && ok; ++kb) {
-        const float ws0n = (kb + 1 < NKB) ? __ldg(wsp0 + kb + 1) : 0.f;
-        const float ws1n = (kb + 1 < NKB) ? __ldg(wsp1 + kb + 1) : 0.f;
+        const float wsn = (kb + 1 < NKB) ? __ldg(wsp + kb + 1) : 0.f;
         if (*abort_flag || !mbar_wait_bounded(&tfull[buf], bphase, p.timeout_ns)) {
           ok = false;
           break;
@@ -335,18 +331,12 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
 #pragma unroll
         for (int cc = 0; cc < C::TC / 16; ++cc) {
           if (col0 + cc * 16 < rows) {  // warp-uniform
-            uint32_t r0[16], r1[16];
-            const uint32_t col = (uint32_t)(buf * 2 * T + col0 + cc * 16);
-            tmem_ld16(tmem_base + lane_base + col, r0);
-            tmem_ld16(tmem_base + lane_base + col + T, r1);
-            tmem_wait_ld16(r0);
-            tmem_wait_ld16(r1);
+            uint32_t r[16];
+            tmem_ld16(tmem_base + lane_base + (uint32_t)(buf * 2 * T + hs * T + col0 + cc * 16), r);
+            tmem_wait_ld16(r);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float as = ss[cc * 16 + i];
-              acc[0][cc * 16 + i] = fmaf(__uint_as_float(r0[i]), ws0 * as, acc[0][cc * 16 + i]);
-              acc[1][cc * 16 + i] = fmaf(__uint_as_float(r1[i]), ws1 * as, acc[1][cc * 16 + i]);
-            }
+            for (int i = 0; i < 16; ++i)
+              acc[cc * 16 + i] = fmaf(__uint_as_float(r[i]), ws * ss[cc * 16 + i], acc[cc * 16 + i]);
           }
         }
         tc_fence_before();
@@ -355,8 +345,7 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
           mbar_arrive(&tempty[buf]);
           mbar_arrive(&sempty[slot]);
         }
-        ws0 = ws0n;
-        ws1 = ws1n;
+        ws = wsn;
         if (++slot == C::NSLOT) {
           slot = 0;
           sphase ^= 1;
@@ -372,48 +361,45 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
       }
 
       if constexpr (EPI == EPI_SILU) {
-        // Lane pair (2k, 2k+1) of quarter q holds weight rows s*128 + q*32 + 2k
-        // (gate) and + 1 (up) of both halves s. The even lane produces inter for
-        // half 0 and the odd lane for half 1, i.e. inter column
-        // i = s*64 + q*16 + k with s = lane & 1: one SiLU per lane and column.
-        const int sh = lane & 1;
-        const int icol = sh * 64 + q * 16 + (lane >> 1);
-        float v[C::TC];
+        // Lane pair (2k, 2k+1) holds weight rows 2k (gate) and 2k+1 (up) of
+        // this half for every token column. The even lane produces inter for
+        // the even token columns and the odd lane for the odd ones; inter
+        // column i = hs*64 + q*16 + k of this unit's 128-wide group.
+        const int par = lane & 1;
+        const int icol = hs * 64 + q * 16 + (lane >> 1);
+        constexpr int TH = C::TC / 2;
+        float v[TH];
 #pragma unroll
-        for (int j = 0; j < C::TC; ++j) {
-          const float send = sh ? acc[0][j] : acc[1][j];
+        for (int m = 0; m < TH; ++m) {
+          const float send = par ? acc[2 * m] : acc[2 * m + 1];
           const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
-          const float gate = sh ? recv : acc[0][j];
-          const float up = sh ? acc[1][j] : recv;
-          v[j] = silu_f32(gate) * up;
+          const float gate = par ? recv : acc[2 * m];
+          const float up = par ? acc[2 * m + 1] : recv;
+          v[m] = silu_f32(gate) * up;  // token column col0 + 2m + par
         }
-        // Column amax over the warp, transposed: lane l ends with column l of
-        // each 32-column group (31 shuffles per group instead of 5 per column).
-        constexpr int NG = (C::TC + 31) / 32;
-        float colmax[NG];
+        // Column amax: within the warp (transposed, lane l ends with column
+        // l of each 32-column group), then over the 8 warps of this column slice.
+        constexpr int NG = C::TC / 32;
 #pragma unroll
-        for (int g = 0; g < NG; ++g) colmax[g] = warp_transpose_max<(C::TC < 32 ? C::TC : 32)>(v + g * 32, lane);
-#pragma unroll
-        for (int g = 0; g < NG; ++g) {
-          const int c = g * 32 + (lane & (C::TC < 32 ? C::TC - 1 : 31));
-          if (lane < C::TC) red[(h * 4 + q) * T + col0 + c] = colmax[g];
-        }
+        for (int g = 0; g < NG; ++g)
+          red[(hs * 4 + q) * T + col0 + g * 32 + lane] = warp_pair_transpose_max(v + g * 16, lane);
         named_bar_sync(1, EW * 32);
         const bool stop = *abort_flag != 0;
         if (stop) break;
         float colscale[NG];
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
-          const int c = col0 + g * 32 + (lane & (C::TC < 32 ? C::TC - 1 : 31));
-          const float* rr = red + h * 4 * T + c;
-          const float amax = fmaxf(fmaxf(rr[0], rr[T]), fmaxf(rr[2 * T], rr[3 * T]));
+          const int c = col0 + g * 32 + lane;
+          float amax = red[c];
+#pragma unroll
+          for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w * T + c]);
           colscale[g] = group_scale(amax);
-          if (q == 0 && lane < C::TC && c < rows) p.out_sT[(int64_t)nt * p.out_s_ld + p0 + c] = colscale[g];
+          if (hs == 0 && q == 0 && c < rows) p.out_sT[(int64_t)nt * p.out_s_ld + p0 + c] = colscale[g];
         }
 #pragma unroll
-        for (int j = 0; j < C::TC; ++j) {
-          const float sc = __shfl_sync(0xffffffffu, colscale[j / 32], j % 32);
-          staging[(col0 + j) * 128 + icol] = quant_e4m3(v[j], sc);
+        for (int m = 0; m < TH; ++m) {
+          const float sc = __shfl_sync(0xffffffffu, colscale[m / 16], 2 * (m % 16) + par);
+          staging[(col0 + 2 * m + par) * 128 + icol] = quant_e4m3(v[m], sc);
         }
         named_bar_sync(1, EW * 32);
         // Coalesced copy of the quantised rows: 8 x 16 B per row.
@@ -432,9 +418,7 @@ __global__ void __launch_bounds__(GemmCfg<T, EW>::THREADS, 1)
             const int f = __ldg(&p.sorted_ids[p0 + c]);
             if (f < p.sentinel) {
               const float w = __ldg(&p.topk_w[f]);
-              float* dst = p.out_pair + (int64_t)f * p.Nw + nt * C::UNIT_ROWS + q * 32 + lane;
-              dst[0] = w * acc[0][j];
-              dst[128] = w * acc[1][j];
+              p.out_pair[(int64_t)f * p.Nw + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane] = w * acc[j];
             }
           }
         }
