@@ -48,6 +48,7 @@ def parse_args(argv=None):
     ap.add_argument("--M", type=int, default=64, help="tokens per GPU")
     ap.add_argument("--hot", type=int, default=0, help="experts with +2.0 router bias (skewed load)")
     ap.add_argument("--experts", type=int, default=256, help="routed experts (fewer only for small profiles)")
+    ap.add_argument("--tile", type=int, default=0, help="tokens per GEMM unit (0 = the library's choice)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-sample-experts", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -277,7 +278,7 @@ def run_ours(args, shape, config):
     L = synth.make_layer(shape, moe.per_block_quant_fp8, seed=args.seed + rank, device=dev)
     active = synth.active_experts(L.topk_ids, shape.E)
     pairs = int(((L.topk_ids >= 0) & (L.topk_ids < shape.E)).sum().item())
-    pipe = stages.LayerPipeline(shape.M, shape.H, shape.I, shape.E, shape.topk, dev)
+    pipe = stages.LayerPipeline(shape.M, shape.H, shape.I, shape.E, shape.topk, dev, tile_tokens=args.tile)
     args_run = (L.hidden, L.topk_ids, L.topk_weights, L.w13, L.w13_scale, L.w2, L.w2_scale)
 
     def barrier():

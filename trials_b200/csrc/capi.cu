@@ -84,8 +84,8 @@ bool valid_tile(int t) { return t == 16 || t == 32 || t == 64 || t == 128; }
 
 int pick_tile_tokens(int64_t numel, int E_local) {
   const double avg = (double)numel / (double)(E_local > 0 ? E_local : 1);
-  if (avg <= 12.0) return 32;
-  if (avg <= 40.0) return 64;
+  if (avg <= 20.0) return 32;
+  if (avg <= 48.0) return 64;
   return 128;
 }
 

@@ -368,27 +368,34 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
         const int par = lane & 1;
         const int icol = hs * 64 + q * 16 + (lane >> 1);
         constexpr int TH = C::TC / 2;
+        constexpr int NG = C::TC / 32;
+        // 32-column groups holding at least one of the chunk's rows (warp-uniform).
+        const int live = rows > col0 ? ((rows - col0 + 31) >> 5) : 0;
         float v[TH];
 #pragma unroll
         for (int m = 0; m < TH; ++m) {
-          const float send = par ? acc[2 * m] : acc[2 * m + 1];
-          const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
-          const float gate = par ? recv : acc[2 * m];
-          const float up = par ? acc[2 * m + 1] : recv;
-          v[m] = silu_f32(gate) * up;  // token column col0 + 2m + par
+          v[m] = 0.f;
+          if (m / 16 < live) {
+            const float send = par ? acc[2 * m] : acc[2 * m + 1];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            const float gate = par ? recv : acc[2 * m];
+            const float up = par ? acc[2 * m + 1] : recv;
+            v[m] = silu_f32(gate) * up;  // token column col0 + 2m + par
+          }
         }
         // Column amax: within the warp (transposed, lane l ends with column
         // l of each 32-column group), then over the 8 warps of this column slice.
-        constexpr int NG = C::TC / 32;
 #pragma unroll
         for (int g = 0; g < NG; ++g)
-          red[(hs * 4 + q) * T + col0 + g * 32 + lane] = warp_pair_transpose_max(v + g * 16, lane);
+          if (g < live) red[(hs * 4 + q) * T + col0 + g * 32 + lane] = warp_pair_transpose_max(v + g * 16, lane);
         named_bar_sync(1, EW * 32);
         const bool stop = *abort_flag != 0;
         if (stop) break;
         float colscale[NG];
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
+          colscale[g] = 1.f;
+          if (g >= live) continue;
           const int c = col0 + g * 32 + lane;
           float amax = red[c];
 #pragma unroll
@@ -398,8 +405,10 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
         }
 #pragma unroll
         for (int m = 0; m < TH; ++m) {
-          const float sc = __shfl_sync(0xffffffffu, colscale[m / 16], 2 * (m % 16) + par);
-          staging[(col0 + 2 * m + par) * 128 + icol] = quant_e4m3(v[m], sc);
+          if (m / 16 < live) {
+            const float sc = __shfl_sync(0xffffffffu, colscale[m / 16], 2 * (m % 16) + par);
+            staging[(col0 + 2 * m + par) * 128 + icol] = quant_e4m3(v[m], sc);
+          }
         }
         named_bar_sync(1, EW * 32);
         // Coalesced copy of the quantised rows: 8 x 16 B per row.
@@ -411,15 +420,24 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
         }
       } else {
         if (!ok) break;
+        // Lane l fetches the slot id and router weight of column l of each
+        // 32-column group once; the stores below broadcast them by shuffle.
+        constexpr int NG = C::TC / 32;
+        int fl[NG];
+        float wl[NG];
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          const int c = col0 + g * 32 + lane;
+          fl[g] = c < rows ? __ldg(&p.sorted_ids[p0 + c]) : p.sentinel;
+          wl[g] = fl[g] < p.sentinel ? __ldg(&p.topk_w[fl[g]]) : 0.f;
+        }
+        float* dst = p.out_pair + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane;
 #pragma unroll
         for (int j = 0; j < C::TC; ++j) {
-          const int c = col0 + j;
-          if (c < rows) {
-            const int f = __ldg(&p.sorted_ids[p0 + c]);
-            if (f < p.sentinel) {
-              const float w = __ldg(&p.topk_w[f]);
-              p.out_pair[(int64_t)f * p.Nw + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane] = w * acc[j];
-            }
+          if (col0 + (j & ~31) < rows) {  // warp-uniform
+            const int f = __shfl_sync(0xffffffffu, fl[j / 32], j % 32);
+            const float w = __shfl_sync(0xffffffffu, wl[j / 32], j % 32);
+            if (f < p.sentinel) dst[(int64_t)f * p.Nw] = w * acc[j];
           }
         }
       }

@@ -131,9 +131,9 @@ def selftest_wait_timeout(err: torch.Tensor, timeout_us: int = 20000) -> None:
 def pick_tile_tokens(numel: int, num_local_experts: int) -> int:
     """Token columns per GEMM unit; the same rule as the C layer (capi.cu)."""
     avg = numel / max(num_local_experts, 1)
-    if avg <= 12.0:
+    if avg <= 20.0:
         return 32
-    if avg <= 40.0:
+    if avg <= 48.0:
         return 64
     return 128
 
