@@ -19,8 +19,8 @@ scales, 1x128 activation scales, bf16 in/out).
 --impl reference times that CPU path alone (the reference is a Python/Triton
 package for AMD GPUs; its algorithm is restated by the oracle).
 
-N > 1 runs expert-parallel ranks when --ep is given, otherwise independent
-replicas of the layer, one per GPU (weak scaling).
+N > 1 (torchrun, one rank per GPU) runs the expert-parallel layer: E/N experts
+and M tokens per GPU, NCCL all-to-all dispatch and combine (weak scaling).
 """
 from __future__ import annotations
 
@@ -156,7 +156,13 @@ def dist_setup(backend):
 
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     if ws > 1 and not dist.is_initialized():
-        dist.init_process_group(backend, timeout=timedelta(seconds=300))
+        kw = {}
+        if backend == "nccl":
+            import torch
+
+            kw["device_id"] = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+            torch.cuda.set_device(kw["device_id"])
+        dist.init_process_group(backend, timeout=timedelta(seconds=120), **kw)
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return rank, local, ws
@@ -266,6 +272,118 @@ def run_reference(args, shape, config):
 # ----------------------------------------------------------------------------
 # GPU arm
 # ----------------------------------------------------------------------------
+def run_ep(args, shape, config):
+    """N > 1: expert-parallel layer, E/N experts and M tokens per GPU."""
+    import torch
+    import torch.distributed as dist
+
+    from trials_b200 import ep, moe, synth
+
+    rank, local, ws = dist_setup("nccl")
+    dev = torch.device("cuda", local)
+    L = synth.make_layer(shape, moe.per_block_quant_fp8, seed=args.seed, device=dev)  # same weights on every rank
+    shards = [ep.shard_experts(t, rank, ws) for t in (L.w13, L.w13_scale, L.w2, L.w2_scale)]
+    del L
+    torch.cuda.empty_cache()
+    model = ep.ExpertParallelMoE(*shards, num_experts=shape.E, rows_per_rank=shape.M)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 1000 + rank)
+    logits = torch.randn(shape.M, shape.E, generator=g, device=dev)
+    if shape.hot_experts:
+        logits[:, : shape.hot_experts] += shape.hot_bias
+    tw, ids = synth.make_router(logits, shape.topk, shape.scoring)
+    hidden = torch.randn(shape.M, shape.H, generator=g, device=dev).to(torch.bfloat16)
+    all_ids = [torch.empty_like(ids) for _ in range(ws)]
+    dist.all_gather(all_ids, ids)
+    per = shape.E // ws
+    glob = torch.cat(all_ids).reshape(-1)
+    local_active = int(torch.unique(glob[(glob >= rank * per) & (glob < (rank + 1) * per)]).numel())
+
+    def barrier():
+        dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        model(hidden, tw, ids)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    t0 = clocks.mark()
+    start.record()
+    for k in range(args.steps):
+        model(hidden, tw, ids, events=evs[k])
+    end.record()
+    barrier()
+    clocks.window(t0, clocks.mark())
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    stage_ms = {name: max_over_ranks(statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1])
+                                                     for k in range(args.steps)))
+                for i, name in enumerate(ep.ExpertParallelMoE.STAGES)}
+    errs = model.device_errors()
+
+    e2e = None
+    if not args.no_e2e:
+        h_host, ids_host, tw_host = hidden.cpu().pin_memory(), ids.cpu().pin_memory(), tw.cpu().pin_memory()
+        out_host = torch.empty(shape.M, shape.H, dtype=torch.bfloat16).pin_memory()
+        h_dev, ids_dev, tw_dev = torch.empty_like(hidden), torch.empty_like(ids), torch.empty_like(tw)
+
+        def e2e_step():
+            h_dev.copy_(h_host, non_blocking=True)
+            ids_dev.copy_(ids_host, non_blocking=True)
+            tw_dev.copy_(tw_host, non_blocking=True)
+            out_host.copy_(model(h_dev, tw_dev, ids_dev), non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        t0 = clocks.mark()
+        s2.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e2.record()
+        barrier()
+        clocks.window(t0, clocks.mark())
+        ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps)
+        e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": (h_host.numel() * 2 + ids_host.numel() * 4 + tw_host.numel() * 4) * ws,
+               "d2h_bytes_per_step": out_host.numel() * 2 * ws, "ms_per_step": ms_e2e}
+    clk = clocks.stop()
+    worst_active = int(max_over_ranks(local_active))
+    if rank == 0:
+        from trials_b200 import synth as _s
+
+        peak, peak_kind = measured_peaks()
+        wbytes = worst_active * (_s.weight_bytes_per_expert(shape.H, shape.I) + _s.scale_bytes_per_expert(shape.H, shape.I))
+        achieved = wbytes / (stage_ms["layer_packed"] / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": shape.M * ws / (ms / 1e3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp8e4m3 (fp32 accumulate)", "data": "synthetic",
+            "config": config, "stage_ms": stage_ms, "local_active_experts_max": worst_active,
+            "roofline": {"kernel": "layer_packed (the five layer kernels on this rank's experts)", "bound": "hbm",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": f"{peak_kind} HBM copy bandwidth",
+                         "algorithmic_bytes_per_launch": wbytes, "traffic": None},
+            "gpu_launches": 10 * args.steps,
+            "clocks": clk,
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        if errs:
+            line["device_errors"] = errs
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+    return 0
+
+
 def run_ours(args, shape, config):
     import torch
     import torch.distributed as dist
@@ -417,9 +535,13 @@ def main(argv=None):
               "topk": shape.topk, "router": "sigmoid top-k, renormalised",
               "quant": "e4m3 weights with fp32 128x128 block scales, 1x128 activation scales",
               "l2": "no flush: each step streams the active experts' fp8 weights (8.4-9.7 GB) >> 126 MB L2",
-              "parallelism": "single GPU" if ws == 1 else f"{ws} independent replicas (one per GPU)"}
+              "parallelism": "single GPU" if ws == 1 else
+              f"expert parallel over {ws} GPUs: {shape.E // ws} experts and {shape.M} tokens per GPU, "
+              "NCCL all-to-all dispatch and combine"}
     if args.impl == "reference":
         return run_reference(args, shape, config)
+    if ws > 1:
+        return run_ep(args, shape, config)
     return run_ours(args, shape, config)
 
 

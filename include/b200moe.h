@@ -127,6 +127,54 @@ B200MOE_API int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t 
                   const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map,
                   int num_local_experts, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same layer with pre-quantised activations: hidden_q (M, H) fp8 e4m3 and
+ * hidden_scale (M, H/128) f32 from a 1x128 per-token-group quantisation. This
+ * is the reference's fp8-input case (sglang_integration/aiter.py:126-130 with
+ * a per-group a1_scale, the a1_scale argument of the fused_moe call at :470).
+ * Workspace: b200moe_layer_workspace_size(). */
+B200MOE_API int b200moe_layer_quantized(const uint8_t* hidden_q, const float* hidden_scale, int64_t M, int64_t H,
+                                        int64_t I, int num_experts, int topk, const uint8_t* w13,
+                                        const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                                        const float* topk_weights, const int32_t* topk_ids,
+                                        const int32_t* expert_map, int num_local_experts, void* out,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Expert parallelism over G ranks: rank r owns experts [r*E/G, (r+1)*E/G).
+ * Replaces the dispatch/combine that the reference consumes from DeepEP/Mori
+ * (sglang_integration/aiter.py:554-756: tokens arrive with local expert ids,
+ * -1 for experts on other ranks, and leave as per-token partial sums).
+ *
+ * Packed row (b200moe_ep_row_bytes(H, topk) bytes, 16-byte multiple):
+ *   [ fp8 row: H bytes | 1x128 scales: H/128 f32 | topk local ids: int32, -1 =
+ *     expert not on the destination | topk router weights: f32 | padding ]
+ * b200moe_ep_dispatch builds the send buffer from this rank's tokens (quantised
+ * with b200moe_quant_1x128): G blocks of rows_per_rank rows, block d holding,
+ * in ascending token order, every token with at least one expert on rank d;
+ * unused rows carry ids -1. pos[t*G + d] = row of token t in block d or -1;
+ * tok_of[d*rows_per_rank + r] = token of that row; counts[d] = rows used.
+ * Tokens beyond rows_per_rank for a destination set B200MOE_DEVERR_CAPACITY
+ * (rows_per_rank = M never overflows). After an equal-split all-to-all of the
+ * G blocks, the receiving rank runs b200moe_layer_packed on all G*rows_per_rank
+ * received rows (rows without a local expert give zero rows) and sends the
+ * (R, H) bf16 result back with a second equal-split all-to-all;
+ * b200moe_ep_combine then sums, for each token, the returned rows of the ranks
+ * it was sent to, in rank order. No host synchronisation anywhere.
+ * ---------------------------------------------------------------------- */
+B200MOE_API int64_t b200moe_ep_row_bytes(int64_t H, int topk);
+B200MOE_API int b200moe_ep_dispatch(const uint8_t* hidden_q, const float* hidden_scale, const int32_t* topk_ids,
+                                    const float* topk_weights, int64_t M, int64_t H, int topk, int num_experts,
+                                    int num_ranks, int64_t rows_per_rank, uint8_t* send_rows, int32_t* pos,
+                                    int32_t* tok_of, int32_t* counts, int32_t* err_word, void* stream);
+B200MOE_API size_t b200moe_layer_packed_workspace_size(int64_t R, int64_t H, int64_t I, int num_local_experts,
+                                                       int topk);
+B200MOE_API int b200moe_layer_packed(const uint8_t* rows, int64_t R, int64_t row_bytes, int64_t H, int64_t I,
+                                     int num_local_experts, int topk, const uint8_t* w13, const float* w13_scale,
+                                     const uint8_t* w2, const float* w2_scale, void* out, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+B200MOE_API int b200moe_ep_combine(const void* returned_rows, const int32_t* pos, int64_t M, int64_t H,
+                                   int num_ranks, int64_t rows_per_rank, void* out, void* stream);
+
 /* ------------------------------------------------------------------------
  * b200moe_layer without a workspace argument, for callers that cannot
  * allocate device memory (a fixed memory pool, a host framework that forbids

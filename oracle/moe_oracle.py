@@ -195,11 +195,13 @@ def bf16_truncate(x: torch.Tensor) -> torch.Tensor:
 
 def moe_layer(hidden, w13_q, w13_s, w2_q, w2_s, topk_weights, topk_ids, *, rounding: str = "exact",
               expert_map=None, num_local=None, stage2_a_by_token: bool = False, dtype=torch.float64,
-              return_stages: bool = False, gemm_cast=_bf16):
+              return_stages: bool = False, gemm_cast=_bf16, a1=None):
     """Full layer on the CPU (or any torch device), expert by expert.
 
     gemm_cast: fp32 -> bf16 cast of the GEMM outputs in "reference" rounding
     (bf16_truncate reproduces the Triton CPU interpreter).
+    a1=(q, s) gives the 1x128-quantised activations directly (hidden is then
+    only used for its shape and device).
     stage2_a_by_token=True plants the reference's historic A_BY_SORTED bug
     (stage-2 activations read by token index instead of by routed row,
     MBR/phase13_findings.md:21-25); used only to show the parity gate rejects it.
@@ -209,7 +211,7 @@ def moe_layer(hidden, w13_q, w13_s, w2_q, w2_s, topk_weights, topk_ids, *, round
     topk = topk_ids.shape[1]
     E_ids = w13_q.shape[0] if expert_map is None else len(expert_map)
     mapped, _ = map_ids(topk_ids.cpu().numpy(), E_ids, expert_map, num_local)
-    a1_q, a1_s = per_token_group_quant_fp8(hidden)
+    a1_q, a1_s = per_token_group_quant_fp8(hidden) if a1 is None else a1
     flat_w = topk_weights.reshape(-1)
     out = torch.zeros(M * topk, H, dtype=torch.float32, device=hidden.device)
     stages = {"gemm1": {}, "inter": {}, "a2": {}, "gemm2": {}}

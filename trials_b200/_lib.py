@@ -39,6 +39,12 @@ SIGNATURES = {
     "b200moe_quant_block128": (_I, [_P, _L, _L, _L, _P, _P, _P]),
     "b200moe_layer_workspace_size": (_S, [_L, _L, _L, _I, _I, _I]),
     "b200moe_layer": (_I, [_P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _S, _P]),
+    "b200moe_layer_quantized": (_I, [_P, _P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _S, _P]),
+    "b200moe_ep_row_bytes": (_L, [_L, _I]),
+    "b200moe_ep_dispatch": (_I, [_P, _P, _P, _P, _L, _L, _I, _I, _I, _L, _P, _P, _P, _P, _P, _P]),
+    "b200moe_layer_packed_workspace_size": (_S, [_L, _L, _L, _I, _I]),
+    "b200moe_layer_packed": (_I, [_P, _L, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _S, _P]),
+    "b200moe_ep_combine": (_I, [_P, _P, _L, _L, _I, _L, _P, _P]),
     "b200moe_layer_noalloc": (_I, [_P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P]),
     "b200moe_route_capacity_rows": (_L, [_L, _I]),
     "b200moe_route_capacity_chunks": (_L, [_L, _I, _I]),

@@ -390,40 +390,77 @@ size_t b200moe_layer_workspace_size(int64_t M, int64_t H, int64_t I, int num_exp
   return plan_layer(M, H, I, E, topk).total;
 }
 
-int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
-                  const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
-                  const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map,
-                  int num_local_experts, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Activation source of the layer: bf16 rows to quantise, or rows already
+// quantised 1x128 (fp8 with row stride ldq bytes, scales s[t * lds + g]).
+struct LayerInput {
+  const void* hidden;
+  const uint8_t* q;
+  int64_t ldq;
+  const float* s;
+  int64_t lds;
+};
+
+int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
+               const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+               const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map, int num_local_experts,
+               void* out, void* workspace, size_t workspace_bytes, size_t workspace_offset, void* stream) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
-  if (M < 0 || topk <= 0 || num_experts <= 0)
-    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer: bad argument%s");
+  if (M < 0 || topk <= 0 || num_experts <= 0) return fail(B200MOE_ERR_INVALID_ARG, "%s: bad argument", name);
   if (M == 0) return B200MOE_OK;
-  if (!hidden || !w13 || !w13_scale || !w2 || !w2_scale || !topk_weights || !topk_ids || !out || !workspace)
-    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer: null pointer%s");
+  if ((!in.hidden && !in.q) || !w13 || !w13_scale || !w2 || !w2_scale || !topk_weights || !topk_ids || !out ||
+      !workspace)
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: null pointer", name);
   const int E = expert_map ? num_local_experts : num_experts;
-  if (E <= 0 || E > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_layer: 1..1024 experts supported%s");
+  if (E <= 0 || E > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "%s: 1..1024 experts supported", name);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
-    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer: workspace must be 256-byte aligned%s");
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: workspace must be 256-byte aligned", name);
   const LayerPlan pl = plan_layer(M, H, I, E, topk);
-  if (workspace_bytes < pl.total) return fail(B200MOE_ERR_WORKSPACE, "b200moe_layer: workspace too small%s");
+  if (workspace_bytes < workspace_offset + pl.total) return fail(B200MOE_ERR_WORKSPACE, "%s: workspace too small", name);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* err = reinterpret_cast<int32_t*>(ws);
-  int32_t* sorted = reinterpret_cast<int32_t*>(ws + pl.off_sorted);
-  int32_t* ce = reinterpret_cast<int32_t*>(ws + pl.off_ce);
-  int32_t* cr0 = reinterpret_cast<int32_t*>(ws + pl.off_cr0);
-  int32_t* crows = reinterpret_cast<int32_t*>(ws + pl.off_crows);
-  int32_t* counts = reinterpret_cast<int32_t*>(ws + pl.off_counts);  // [0] n_chunks, [1] num_rows
-  uint8_t* a1 = ws + pl.off_a1;
-  float* a1s = reinterpret_cast<float*>(ws + pl.off_a1s);
-  uint8_t* a2 = ws + pl.off_a2;
-  float* a2s = reinterpret_cast<float*>(ws + pl.off_a2s);
-  float* pair = reinterpret_cast<float*>(ws + pl.off_pair);
+  uint8_t* wl = ws + workspace_offset;  // layer regions (the error word stays at offset 0)
+  int32_t* sorted = reinterpret_cast<int32_t*>(wl + pl.off_sorted);
+  int32_t* ce = reinterpret_cast<int32_t*>(wl + pl.off_ce);
+  int32_t* cr0 = reinterpret_cast<int32_t*>(wl + pl.off_cr0);
+  int32_t* crows = reinterpret_cast<int32_t*>(wl + pl.off_crows);
+  int32_t* counts = reinterpret_cast<int32_t*>(wl + pl.off_counts);  // [0] n_chunks, [1] num_rows
+  uint8_t* a1 = wl + pl.off_a1;
+  float* a1s = reinterpret_cast<float*>(wl + pl.off_a1s);
+  uint8_t* a2 = wl + pl.off_a2;
+  float* a2s = reinterpret_cast<float*>(wl + pl.off_a2s);
+  float* pair = reinterpret_cast<float*>(wl + pl.off_pair);
 
   st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,
                      crows, pl.chunks_cap, counts, counts + 1, err, stream);
   if (st) return st;
-  st = b200moe_gather_quant(hidden, M, H, topk, sorted, counts + 1, pl.rows_cap, a1, a1s, pl.as_ld, stream);
+  if (in.hidden) {
+    st = b200moe_gather_quant(in.hidden, M, H, topk, sorted, counts + 1, pl.rows_cap, a1, a1s, pl.as_ld, stream);
+  } else {
+    if (!aligned16(in.q) || in.ldq % 16 != 0 || in.ldq < H || in.lds < H / 128 || !in.s)
+      return fail(B200MOE_ERR_UNSUPPORTED, "%s: fp8 rows must be 16-byte aligned with scales per row", name);
+    QuantArgs a{};
+    a.xq = in.q;
+    a.ldxq = in.ldq;
+    a.xs = in.s;
+    a.ldxs = in.lds;
+    a.K = H;
+    a.rows = pl.rows_cap;
+    a.num_rows = counts + 1;
+    a.sorted_ids = sorted;
+    a.topk = topk;
+    a.sentinel = (int32_t)(M * topk);
+    a.q = a1;
+    a.ldq = H;
+    a.s = a1s;
+    a.s_row = 1;
+    a.s_grp = pl.as_ld;
+    st = cuda_status(launch_quant_1x128(a, (cudaStream_t)stream), "gather rows");
+  }
   if (st) return st;
   st = b200moe_gemm1_silu(a1, a1s, pl.as_ld, pl.rows_cap, w13, w13_scale, E, H, I, ce, cr0, crows, counts,
                           pl.chunks_cap, pl.tile_tokens, a2, a2s, err, 0, stream);
@@ -432,6 +469,90 @@ int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t I, int num_e
                              pl.chunks_cap, pl.tile_tokens, sorted, topk_weights, M, topk, pair, err, 0, stream);
   if (st) return st;
   return b200moe_combine_reduce(pair, topk_ids, expert_map, num_experts, M, topk, H, out, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
+                  const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                  const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map,
+                  int num_local_experts, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!hidden && M > 0) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer: null hidden%s");
+  LayerInput in{hidden, nullptr, 0, nullptr, 0};
+  return layer_core("b200moe_layer", in, M, H, I, num_experts, topk, w13, w13_scale, w2, w2_scale, topk_weights,
+                    topk_ids, expert_map, num_local_experts, out, workspace, workspace_bytes, 0, stream);
+}
+
+int b200moe_layer_quantized(const uint8_t* hidden_q, const float* hidden_scale, int64_t M, int64_t H, int64_t I,
+                            int num_experts, int topk, const uint8_t* w13, const float* w13_scale, const uint8_t* w2,
+                            const float* w2_scale, const float* topk_weights, const int32_t* topk_ids,
+                            const int32_t* expert_map, int num_local_experts, void* out, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if ((!hidden_q || !hidden_scale) && M > 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer_quantized: null input%s");
+  LayerInput in{nullptr, hidden_q, H, hidden_scale, H / 128};
+  return layer_core("b200moe_layer_quantized", in, M, H, I, num_experts, topk, w13, w13_scale, w2, w2_scale,
+                    topk_weights, topk_ids, expert_map, num_local_experts, out, workspace, workspace_bytes, 0,
+                    stream);
+}
+
+int64_t b200moe_ep_row_bytes(int64_t H, int topk) { return round_up(H + (H / 128) * 4 + 8 * (int64_t)topk, 16); }
+
+int b200moe_ep_dispatch(const uint8_t* hidden_q, const float* hidden_scale, const int32_t* topk_ids,
+                        const float* topk_weights, int64_t M, int64_t H, int topk, int num_experts, int num_ranks,
+                        int64_t rows_per_rank, uint8_t* send_rows, int32_t* pos, int32_t* tok_of, int32_t* counts,
+                        int32_t* err_word, void* stream) {
+  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || num_ranks <= 0 || num_experts % num_ranks != 0 ||
+      rows_per_rank < 0 || !err_word || !counts || (M > 0 && (!hidden_q || !hidden_scale || !topk_ids ||
+      !topk_weights || !pos)) || (rows_per_rank > 0 && (!send_rows || !tok_of)))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_dispatch: bad argument%s");
+  if (!aligned16(hidden_q) || !aligned16(send_rows))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_dispatch: 16-byte alignment required%s");
+  return cuda_status(launch_ep_dispatch(hidden_q, hidden_scale, topk_ids, topk_weights, M, H, topk, num_experts,
+                                        num_ranks, rows_per_rank, send_rows, b200moe_ep_row_bytes(H, topk), pos,
+                                        tok_of, counts, err_word, (cudaStream_t)stream),
+                     "ep_dispatch");
+}
+
+size_t b200moe_layer_packed_workspace_size(int64_t R, int64_t H, int64_t I, int num_local_experts, int topk) {
+  if (R < 0 || H <= 0 || I <= 0 || topk <= 0 || num_local_experts <= 0) return 0;
+  const size_t meta = (size_t)round_up(R * topk * 8 + 256, 256);
+  return meta + plan_layer(R, H, I, num_local_experts, topk).total;
+}
+
+int b200moe_layer_packed(const uint8_t* rows, int64_t R, int64_t row_bytes, int64_t H, int64_t I,
+                         int num_local_experts, int topk, const uint8_t* w13, const float* w13_scale,
+                         const uint8_t* w2, const float* w2_scale, void* out, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (R < 0 || row_bytes != b200moe_ep_row_bytes(H, topk) || !workspace || (R > 0 && !rows))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer_packed: bad argument%s");
+  if (R == 0) return B200MOE_OK;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer_packed: workspace must be 256-byte aligned%s");
+  const size_t meta = (size_t)round_up(R * topk * 8 + 256, 256);
+  if (workspace_bytes < b200moe_layer_packed_workspace_size(R, H, I, num_local_experts, topk))
+    return fail(B200MOE_ERR_WORKSPACE, "b200moe_layer_packed: workspace too small%s");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* ids = reinterpret_cast<int32_t*>(ws + 256);
+  float* w = reinterpret_cast<float*>(ids + R * topk);
+  int st = cuda_status(launch_ep_unpack_meta(rows, R, row_bytes, H, topk, ids, w, (cudaStream_t)stream),
+                       "ep_unpack_meta");
+  if (st) return st;
+  LayerInput in{nullptr, rows, row_bytes, reinterpret_cast<const float*>(rows + H), row_bytes / 4};
+  return layer_core("b200moe_layer_packed", in, R, H, I, num_local_experts, topk, w13, w13_scale, w2, w2_scale, w,
+                    ids, nullptr, num_local_experts, out, workspace, workspace_bytes, meta, stream);
+}
+
+int b200moe_ep_combine(const void* returned_rows, const int32_t* pos, int64_t M, int64_t H, int num_ranks,
+                       int64_t rows_per_rank, void* out, void* stream) {
+  if (M < 0 || H <= 0 || H % 8 != 0 || num_ranks <= 0 || (M > 0 && (!returned_rows || !pos || !out)))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_combine: bad argument%s");
+  if (!aligned16(returned_rows) || !aligned16(out))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_combine: 16-byte alignment required%s");
+  return cuda_status(launch_ep_combine(returned_rows, pos, M, H, num_ranks, rows_per_rank, out, (cudaStream_t)stream),
+                     "ep_combine");
 }
 
 int b200moe_read_error(int32_t* err_word, int32_t* value, int clear, void* stream) {

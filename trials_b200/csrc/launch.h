@@ -40,6 +40,12 @@ cudaError_t launch_align(const AlignArgs& a, cudaStream_t stream);
 struct QuantArgs {
   const void* x;
   int64_t ldx;
+  // Pre-quantised input (copy mode, x unused): fp8 rows with row stride ldxq
+  // bytes and 1x128 scales xs[t * ldxs + g].
+  const uint8_t* xq;
+  int64_t ldxq;
+  const float* xs;
+  int64_t ldxs;
   int64_t K;
   int64_t rows;            // rows (M) or the row capacity in gather mode
   const int32_t* num_rows; // gather mode: device row count
@@ -59,6 +65,15 @@ cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K
 
 cudaError_t launch_combine_reduce(const float* pair, const int32_t* ids, const int32_t* expert_map,
                                   int num_experts, int64_t M, int topk, int64_t H, void* out, cudaStream_t stream);
+
+cudaError_t launch_ep_dispatch(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t M,
+                               int64_t H, int topk, int num_experts, int G, int64_t rows_per_rank, uint8_t* send,
+                               int64_t row_bytes, int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err,
+                               cudaStream_t stream);
+cudaError_t launch_ep_unpack_meta(const uint8_t* rows, int64_t R, int64_t row_bytes, int64_t H, int topk,
+                                  int32_t* ids, float* w, cudaStream_t stream);
+cudaError_t launch_ep_combine(const void* comb, const int32_t* pos, int64_t M, int64_t H, int G,
+                              int64_t rows_per_rank, void* out, cudaStream_t stream);
 
 cudaError_t launch_wait_timeout_selftest(int32_t* err, uint64_t timeout_ns, cudaStream_t stream);
 

@@ -23,8 +23,22 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
     const int f = __ldg(&a.sorted_ids[row]);
     src = (f >= 0 && f < a.sentinel) ? (int64_t)(f / a.topk) : -1;
   }
-  const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
   uint8_t* qr = a.q + row * a.ldq;
+  if (a.xq != nullptr) {
+    // Copy mode: the input is already quantised.
+    const int64_t n16 = a.K / 16;
+    uint4* dq = reinterpret_cast<uint4*>(qr);
+    if (src >= 0) {
+      const uint4* sq = reinterpret_cast<const uint4*>(a.xq + src * a.ldxq);
+      for (int64_t i = lane; i < n16; i += 32) dq[i] = __ldg(&sq[i]);
+      for (int64_t g = lane; g < a.K / 128; g += 32) a.s[row * a.s_row + g * a.s_grp] = __ldg(&a.xs[src * a.ldxs + g]);
+    } else {
+      for (int64_t i = lane; i < n16; i += 32) dq[i] = make_uint4(0, 0, 0, 0);
+      for (int64_t g = lane; g < a.K / 128; g += 32) a.s[row * a.s_row + g * a.s_grp] = 0.f;
+    }
+    return;
+  }
+  const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
   for (int64_t c0 = 0; c0 < a.K; c0 += 256) {
     const int64_t c = c0 + lane * 8;
     const bool in = c < a.K;

@@ -1,0 +1,165 @@
+"""Expert-parallel MoE layer: one rank per GPU, experts sharded over ranks,
+tokens exchanged with two equal-split all-to-alls (NCCL over NVLink).
+
+Rank r of G owns experts [r*E/G, (r+1)*E/G). Per forward call:
+  1. quantise this rank's tokens 1x128 (fp8 + scales);
+  2. pack one row per (token, owning rank) - fp8 row, scales, the token's top-k
+     ids mapped to the destination's local experts (-1 elsewhere), weights -
+     into G fixed-size blocks of `rows_per_rank` rows (b200moe_ep_dispatch);
+  3. all-to-all the blocks;
+  4. run the layer on every received row with this rank's experts
+     (b200moe_layer_packed): one bf16 row per received row = the sum of that
+     token's weighted outputs over this rank's experts;
+  5. all-to-all those rows back;
+  6. sum each token's returned rows in rank order (b200moe_ep_combine).
+Blocks have a fixed size so the exchange needs no count all-to-all and no
+host synchronisation; rows_per_rank is the largest token count any rank passes.
+
+This is the dispatch/combine the reference consumes from DeepEP/Mori
+(sglang_integration/aiter.py:554-756), with the reference's conventions:
+per-group fp8 dispatch with fp32 scales (:614-617) and local ids, -1 for
+experts elsewhere (:660-668).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .moe import FP8, _ptr, _stream
+
+
+class CudaEPOps:
+    """The rank-local steps on the GPU through the C ABI."""
+
+    def row_bytes(self, H: int, topk: int) -> int:
+        return _lib.lib().b200moe_ep_row_bytes(H, topk)
+
+    def quant(self, hidden: torch.Tensor, q: torch.Tensor, s: torch.Tensor):
+        M, H = hidden.shape
+        _lib.check(_lib.lib().b200moe_quant_1x128(_ptr(hidden), M, H, H, _ptr(q), H, _ptr(s), H // 128, 1,
+                                                  _stream(hidden.device)), "ep quant")
+
+    def dispatch(self, q, s, topk_ids, topk_weights, num_experts, G, rows_per_rank, send, pos, tok_of, counts, err):
+        M, H = q.shape
+        topk = topk_ids.shape[1]
+        _lib.check(_lib.lib().b200moe_ep_dispatch(
+            _ptr(q), _ptr(s), _ptr(topk_ids), _ptr(topk_weights), M, H, topk, num_experts, G, rows_per_rank,
+            _ptr(send), _ptr(pos), _ptr(tok_of), _ptr(counts), _ptr(err), _stream(q.device)), "ep_dispatch")
+
+    def workspace_bytes(self, R, H, I, E_local, topk) -> int:
+        return _lib.lib().b200moe_layer_packed_workspace_size(R, H, I, E_local, topk)
+
+    def layer_packed(self, rows, R, H, I, E_local, topk, w13, w13_scale, w2, w2_scale, out, ws):
+        _lib.check(_lib.lib().b200moe_layer_packed(
+            _ptr(rows), R, self.row_bytes(H, topk), H, I, E_local, topk, _ptr(w13), _ptr(w13_scale), _ptr(w2),
+            _ptr(w2_scale), _ptr(out), _ptr(ws), ws.numel(), _stream(rows.device)), "layer_packed")
+
+    def combine(self, returned, pos, M, H, G, rows_per_rank, out):
+        _lib.check(_lib.lib().b200moe_ep_combine(_ptr(returned), _ptr(pos), M, H, G, rows_per_rank, _ptr(out),
+                                                 _stream(out.device)), "ep_combine")
+
+
+class ExpertParallelMoE:
+    """One rank's share of an expert-parallel MoE layer.
+
+    w13 (E/G, 2I, H), w2 (E/G, H, I) fp8 with their 128x128 scales are the
+    experts this rank owns. forward() takes this rank's tokens with GLOBAL
+    top-k ids and returns their (M, H) bf16 outputs. Every rank must call
+    forward() the same number of times (collectives)."""
+
+    def __init__(self, w13, w13_scale, w2, w2_scale, num_experts: int, rows_per_rank: int,
+                 group: Optional[dist.ProcessGroup] = None, ops=None, device=None):
+        self.group = group
+        self.G = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if num_experts % self.G:
+            raise ValueError("num_experts must be a multiple of the world size")
+        self.E = num_experts
+        self.E_local, self.I2, self.H = w13.shape
+        if self.E_local != num_experts // self.G:
+            raise ValueError("w13 must hold num_experts / world_size experts")
+        self.I = self.I2 // 2
+        self.w13, self.w13_scale, self.w2, self.w2_scale = w13, w13_scale.contiguous(), w2, w2_scale.contiguous()
+        self.cap = int(rows_per_rank)
+        self.ops = ops or CudaEPOps()
+        self.device = torch.device(device) if device is not None else w13.device
+        self._topk = None
+
+    def _buffers(self, topk: int):
+        if self._topk == topk:
+            return
+        G, cap, H, dev = self.G, self.cap, self.H, self.device
+        rb = self.ops.row_bytes(H, topk)
+        R = G * cap
+        self.row_bytes = rb
+        self.q = torch.empty(cap, H, dtype=FP8, device=dev)
+        self.s = torch.empty(cap, H // 128, dtype=torch.float32, device=dev)
+        self.send = torch.empty(R * rb, dtype=torch.uint8, device=dev)
+        self.recv = torch.empty(R * rb, dtype=torch.uint8, device=dev)
+        self.pos = torch.empty(cap * G, dtype=torch.int32, device=dev)
+        self.tok_of = torch.empty(R, dtype=torch.int32, device=dev)
+        self.counts = torch.empty(G, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.local_out = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+        self.returned = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+        self.ws = torch.empty(max(self.ops.workspace_bytes(R, H, self.I, self.E_local, topk), 256),
+                              dtype=torch.uint8, device=dev)
+        self.ws[:256].zero_()
+        self._topk = topk
+
+    def _all_to_all(self, out: torch.Tensor, inp: torch.Tensor):
+        if self.G == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, group=self.group)
+
+    STAGES = ("quant_dispatch", "all_to_all_dispatch", "layer_packed", "all_to_all_combine", "combine")
+
+    def forward(self, hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                out: Optional[torch.Tensor] = None, events=None) -> torch.Tensor:
+        """events: optional list of 6 CUDA events recorded at the STAGES boundaries."""
+        M, H = hidden.shape
+        topk = topk_ids.shape[1]
+        if M > self.cap:
+            raise ValueError(f"{M} tokens exceed rows_per_rank={self.cap}")
+        self._buffers(topk)
+        ids = topk_ids.to(torch.int32).contiguous()
+        tw = topk_weights.to(torch.float32).contiguous()
+        if out is None:
+            out = torch.empty(M, H, dtype=torch.bfloat16, device=self.device)
+        rec = (lambda i: events[i].record()) if events is not None else (lambda i: None)
+        q, s = self.q[:M], self.s[:M]
+        rec(0)
+        self.ops.quant(hidden.contiguous(), q, s)
+        self.ops.dispatch(q, s, ids, tw, self.E, self.G, self.cap, self.send, self.pos[: M * self.G],
+                          self.tok_of, self.counts, self.err)
+        rec(1)
+        self._all_to_all(self.recv, self.send)
+        rec(2)
+        R = self.G * self.cap
+        self.ops.layer_packed(self.recv, R, H, self.I, self.E_local, topk, self.w13, self.w13_scale, self.w2,
+                              self.w2_scale, self.local_out, self.ws)
+        rec(3)
+        self._all_to_all(self.returned.view(-1), self.local_out.view(-1))
+        rec(4)
+        self.ops.combine(self.returned, self.pos[: M * self.G], M, H, self.G, self.cap, out)
+        rec(5)
+        return out
+
+    __call__ = forward
+
+    def device_errors(self) -> int:
+        """OR of the dispatch and layer device error words (synchronises)."""
+        from .moe import read_device_error
+
+        return read_device_error(self.err) | read_device_error(self.ws[:4].view(torch.int32))
+
+
+def shard_experts(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """The slice of an (E, ...) expert tensor that rank `rank` owns."""
+    E = w.shape[0]
+    per = E // world
+    return w[rank * per:(rank + 1) * per].contiguous()

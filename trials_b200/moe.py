@@ -150,10 +150,14 @@ def per_block_quant_fp8(w: torch.Tensor, bn: int = 128, bk: int = 128):
 # ----------------------------------------------------------------------------
 # the layer
 # ----------------------------------------------------------------------------
-def _check_layer_args(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids):
+def _check_layer_args(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids, a1_scale=None):
     dev = _require_cuda(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids)
-    if hidden.dtype != torch.bfloat16:
-        raise NotImplementedError("hidden_states must be bf16 (pre-quantised fp8 input is not supported)")
+    if hidden.dtype == FP8:
+        if a1_scale is None or a1_scale.dim() != 2 or tuple(a1_scale.shape) != (hidden.shape[0], hidden.shape[1] // 128):
+            raise NotImplementedError("fp8 hidden_states need a1_scale of shape (M, H/128) (1x128 per-token-group "
+                                      "scales); per-token (M,) scales are not supported")
+    elif hidden.dtype != torch.bfloat16:
+        raise NotImplementedError("hidden_states must be bf16, or fp8 e4m3 with (M, H/128) a1_scale")
     if w13.dtype != FP8 or w2.dtype != FP8:
         raise NotImplementedError("weights must be float8_e4m3fn with 128x128 block scales")
     if w13_scale is None or w2_scale is None:
@@ -171,8 +175,9 @@ def _check_layer_args(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_i
     return dev, M, H, I, E
 
 
-def _run_layer(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids, expert_map, num_experts, out=None):
-    dev, M, H, I, E_w = _check_layer_args(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids)
+def _run_layer(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids, expert_map, num_experts, out=None,
+               a1_scale=None):
+    dev, M, H, I, E_w = _check_layer_args(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids, a1_scale)
     topk = topk_ids.shape[1]
     if out is None:
         out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
@@ -185,6 +190,13 @@ def _run_layer(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids, exp
     n_local = E_w
     ws_bytes = L.b200moe_layer_workspace_size(M, H, I, num_experts, n_local, topk)
     ws = _workspaces.get(dev, ws_bytes)
+    if hidden.dtype == FP8:
+        a1 = a1_scale.to(torch.float32).contiguous()
+        _lib.check(L.b200moe_layer_quantized(_ptr(hidden), _ptr(a1), M, H, I, num_experts, topk, _ptr(w13),
+                                             _ptr(w13_scale.contiguous()), _ptr(w2), _ptr(w2_scale.contiguous()),
+                                             _ptr(tw), _ptr(ids), _ptr(expert_map), n_local, _ptr(out), _ptr(ws),
+                                             ws.numel(), _stream(dev)), "b200moe_layer_quantized")
+        return out
     _lib.check(L.b200moe_layer(_ptr(hidden), M, H, I, num_experts, topk, _ptr(w13), _ptr(w13_scale.contiguous()),
                                _ptr(w2), _ptr(w2_scale.contiguous()), _ptr(tw), _ptr(ids), _ptr(expert_map),
                                n_local, _ptr(out), _ptr(ws), ws.numel(), _stream(dev)), "b200moe_layer")
@@ -196,11 +208,14 @@ def moe_decode_megakernel_full(hidden_states: torch.Tensor, w13_fp8: torch.Tenso
                                topk_ids: torch.Tensor, a1_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Full MoE layer, same arguments and result as the reference
     `_moe_decode_megakernel_full` (sglang_integration/aiter.py:74-177):
-    (M, H) bf16 = sum_j topk_weights[:, j] * W2[e] . silu_mul(W13[e] . h)."""
-    if a1_scale is not None:
-        raise NotImplementedError("pre-quantised activations (a1_scale) are not supported; pass bf16 hidden_states")
+    (M, H) bf16 = sum_j topk_weights[:, j] * W2[e] . silu_mul(W13[e] . h).
+    hidden_states may be bf16, or fp8 e4m3 already quantised 1x128 with
+    a1_scale (M, H/128); the reference's per-token (M,) a1_scale form
+    (aiter.py:126-130) cannot run there either and is rejected."""
+    if hidden_states.dtype != FP8 and a1_scale is not None:
+        raise ValueError("a1_scale is only meaningful with fp8 hidden_states")
     return _run_layer(hidden_states, w13_fp8, w13_scale, w2_fp8, w2_scale, topk_weights, topk_ids, None,
-                      w13_fp8.shape[0])
+                      w13_fp8.shape[0], a1_scale=a1_scale)
 
 
 _moe_decode_megakernel_full = moe_decode_megakernel_full
@@ -267,15 +282,17 @@ def fused_moe(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, t
         raise NotImplementedError("swiglu_limit is not supported")
     if extra:
         raise NotImplementedError(f"unsupported arguments: {sorted(extra)}")
-    if a1_scale is not None:
-        raise NotImplementedError("pre-quantised activations (a1_scale) are not supported")
+    if hidden_states.dtype != FP8 and a1_scale is not None:
+        raise NotImplementedError("static a1_scale with bf16 hidden_states is not supported (activations are "
+                                  "quantised per 1x128 group)")
     if hidden_states.shape[0] == 0:
-        return hidden_states
+        return hidden_states.new_empty((0, hidden_states.shape[1]), dtype=torch.bfloat16)
     if expert_mask is not None:
         emap = expert_map_from_mask(expert_mask.to(hidden_states.device))
         return _run_layer(hidden_states, w1, w1_scale, w2, w2_scale, topk_weight, topk_ids, emap,
-                          int(expert_mask.numel()))
-    return _run_layer(hidden_states, w1, w1_scale, w2, w2_scale, topk_weight, topk_ids, None, w1.shape[0])
+                          int(expert_mask.numel()), a1_scale=a1_scale)
+    return _run_layer(hidden_states, w1, w1_scale, w2, w2_scale, topk_weight, topk_ids, None, w1.shape[0],
+                      a1_scale=a1_scale)
 
 
 def moe_layer_ep_local(hidden_states, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids, expert_map,
