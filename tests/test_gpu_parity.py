@@ -186,12 +186,12 @@ def test_gather_and_gemm_stages(cuda_device, shape, tile):
     assert int(r.err.item()) == 0
 
 
-@pytest.mark.parametrize("grid", [1, 5, 37])
-def test_schedule_invariance_bit_exact(cuda_device, grid):
+@pytest.mark.parametrize("grid,tile", [(1, 32), (5, 32), (37, 32), (1, 128), (7, 128), (3, 64)])
+def test_schedule_invariance_bit_exact(cuda_device, grid, tile):
     """Any persistent grid gives bit-identical results (the reference's MODE 0/1
     equivalence check, phase3_blockscale.py:150-164)."""
     L, g = _tiny_layer(cuda_device, SMALL, seed=1)
-    r = stages.route(g["topk_ids"], SMALL.E, 32)
+    r = stages.route(g["topk_ids"], SMALL.E, tile)
     a1_q, a1_sT = stages.gather_quant(g["hidden"], SMALL.topk, r)
     ref_q, ref_s = stages.gemm1_silu(a1_q, a1_sT, g["w13"], g["w13_scale"], r, grid_ctas=0)
     q, s = stages.gemm1_silu(a1_q, a1_sT, g["w13"], g["w13_scale"], r, grid_ctas=grid)
@@ -231,7 +231,7 @@ def test_layer_tiny_vs_reference_golden(cuda_device):
     assert orc.rel_l2(out, ref) < LAYER_GATE
 
 
-@pytest.mark.parametrize("M,hot", [(64, 0), (256, 0), (1024, 16)])
+@pytest.mark.parametrize("M,hot", [(64, 0), (256, 0), (1024, 16), (2048, 0)])
 def test_layer_glm_shapes_vs_oracle(cuda_device, M, hot):
     shape = synth.glm(M, hot)
     L = synth.make_layer(shape, moe.per_block_quant_fp8, seed=0, device=cuda_device)

@@ -1,6 +1,7 @@
 // Instantiations and launcher of the persistent grouped GEMM.
 #include "launch.h"
 #include "moe_gemm.cuh"
+#include "moe_gemm_tok.cuh"
 
 namespace b200moe {
 
@@ -18,6 +19,16 @@ cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const G
 }
 
 template <int EPI>
+cudaError_t launch_tok(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p, int grid,
+                       cudaStream_t stream) {
+  auto kernel = moe_grouped_gemm_tok_kernel<EPI>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TokCfg::SMEM_BYTES);
+  if (err != cudaSuccess) return err;
+  kernel<<<grid, TokCfg::THREADS, TokCfg::SMEM_BYTES, stream>>>(tm_w, tm_a, p);
+  return cudaGetLastError();
+}
+
+template <int EPI>
 cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p,
                        int grid, cudaStream_t stream) {
   switch (tile_tokens) {
@@ -29,7 +40,8 @@ cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorM
       // combine epilogue: two slices (more warps hide its global stores).
       return launch_cfg<64, EPI == EPI_SILU ? 1 : 2, EPI>(tm_w, tm_a, p, grid, stream);
     case 128:
-      return launch_cfg<128, 2, EPI>(tm_w, tm_a, p, grid, stream);
+      // Many tokens per expert: routed rows on the MMA M side.
+      return launch_tok<EPI>(tm_w, tm_a, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }
