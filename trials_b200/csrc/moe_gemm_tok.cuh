@@ -55,6 +55,15 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(rd));
 }
 
+// Epilogue tuning: TMEM loads of 16 columns issued per wait (1, 2 or 4) and
+// packed f32x2 FMA (1) or scalar FMA (0) for the promotion. Same results.
+#ifndef B200MOE_TOK_LD_BATCH
+#define B200MOE_TOK_LD_BATCH 2
+#endif
+#ifndef B200MOE_TOK_FFMA2
+#define B200MOE_TOK_FFMA2 1
+#endif
+
 template <int EPI>
 __global__ void __launch_bounds__(TokCfg::THREADS, 1)
     moe_grouped_gemm_tok_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
@@ -248,14 +257,30 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
         if (live) {
           const float sc = ws * sscale[slot * C::TM + r];
           const uint32_t taddr = taddr0 + (uint32_t)(buf * C::UNIT_ROWS);
+          constexpr int LB = B200MOE_TOK_LD_BATCH;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint32_t v[16];
-            tmem_ld16(taddr + c * 16, v);
-            tmem_wait_ld16(v);
+          for (int c0 = 0; c0 < 8; c0 += LB) {
+            uint32_t v[LB][16];
 #pragma unroll
-            for (int i = 0; i < 16; i += 2)
-              ffma2(acc[c * 16 + i], acc[c * 16 + i + 1], __uint_as_float(v[i]), __uint_as_float(v[i + 1]), sc);
+            for (int b = 0; b < LB; ++b) tmem_ld16(taddr + (c0 + b) * 16, v[b]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int b = 0; b < LB; ++b)
+#pragma unroll
+              for (int i = 0; i < 16; ++i) tmem_reg_fence(v[b][i]);
+#pragma unroll
+            for (int b = 0; b < LB; ++b)
+#pragma unroll
+              for (int i = 0; i < 16; i += 2) {
+                float& d0 = acc[(c0 + b) * 16 + i];
+                float& d1 = acc[(c0 + b) * 16 + i + 1];
+#if B200MOE_TOK_FFMA2
+                ffma2(d0, d1, __uint_as_float(v[b][i]), __uint_as_float(v[b][i + 1]), sc);
+#else
+                d0 = fmaf(__uint_as_float(v[b][i]), sc, d0);
+                d1 = fmaf(__uint_as_float(v[b][i + 1]), sc, d1);
+#endif
+              }
           }
         }
         tc_fence_before();

@@ -193,6 +193,11 @@ __device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
                : "memory");
 }
 
+// Waits for this thread's outstanding tcgen05.ld; follow with tmem_reg_fence on
+// each destination register so no use moves above the wait.
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_reg_fence(uint32_t& r) { asm volatile("" : "+r"(r)); }
+
 // Named barrier among `nthreads` threads (a multiple of 32) with id `id` (1..15).
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
