@@ -83,6 +83,22 @@ B200MOE_API int b200moe_align(const int32_t* topk_ids, int64_t M, int topk, int 
                   int32_t* num_tokens_post_pad, int32_t* err_word, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Router: logits (M, E) f32 (logits_bf16 = 0) or bf16 (1) -> topk_ids and
+ * topk_weights (M, topk). Replaces the router kernel in front of the
+ * reference's MoE call (aiter topksoftmax, MBR/micro/glm52_fp8_moe.log) and
+ * GLM's sigmoid routing (measure_xcd_imbalance.py:50-55: ungrouped top-k of
+ * sigmoid(logits) + correction_bias).
+ * scoring 0 = softmax: select the top-k softmax probabilities; 1 = sigmoid:
+ * select the top-k of sigmoid + correction_bias (nullable). Weights are the
+ * unbiased probabilities of the selected experts, divided by their sum when
+ * renormalize != 0, times scaling. Ids in descending selection order, equal
+ * values broken by the lower id. E <= 1024, topk <= 16.
+ * ---------------------------------------------------------------------- */
+B200MOE_API int b200moe_router_topk(const void* logits, int logits_bf16, int64_t M, int num_experts, int topk,
+                                    int scoring, const float* correction_bias, int renormalize, float scaling,
+                                    float* topk_weights, int32_t* topk_ids, void* stream);
+
+/* ------------------------------------------------------------------------
  * Activation quantisation: per_token_group_quant_fp8(x, 128).
  * Replaces sglang's per_token_group_quant_fp8 called at
  * sglang_integration/aiter.py:132-133 and :151-152 (torch form of the same

@@ -285,3 +285,36 @@ def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
     a = a.double().cpu()
     b = b.double().cpu()
     return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+# ----------------------------------------------------------------------------
+# Router
+# ----------------------------------------------------------------------------
+def router_topk(logits, topk: int, scoring: str = "softmax", correction_bias=None, renormalize: bool = True,
+                scaling: float = 1.0):
+    """float64 restatement of the router (GLM sigmoid routing,
+    measure_xcd_imbalance.py:50-55; softmax top-k of the tiny configuration).
+    Returns (weights (M, k) f64, ids (M, k) int64, margin (M,) f64): ids in
+    descending selection value, ties -> lower id; margin = relative gap between
+    the k-th and (k+1)-th selection values (tiny margins are ambiguous in fp32)."""
+    x = np.asarray(logits, dtype=np.float64)
+    M, E = x.shape
+    if scoring == "softmax":
+        p = np.exp(x - x.max(axis=1, keepdims=True))
+        p /= p.sum(axis=1, keepdims=True)
+        sel = x
+    else:
+        p = 1.0 / (1.0 + np.exp(-x))
+        sel = p + (np.asarray(correction_bias, dtype=np.float64)[None, :] if correction_bias is not None else 0.0)
+    order = np.lexsort((np.broadcast_to(np.arange(E), (M, E)), -sel), axis=1)
+    ids = order[:, :topk]
+    w = np.take_along_axis(p, ids, axis=1)
+    if renormalize:
+        w = w / w.sum(axis=1, keepdims=True)
+    w = w * scaling
+    srt = np.take_along_axis(sel, order, axis=1)
+    if topk < E:
+        margin = np.abs(srt[:, topk - 1] - srt[:, topk]) / np.maximum(np.abs(srt[:, topk - 1]), 1e-30)
+    else:
+        margin = np.full(M, np.inf)
+    return w, ids, margin

@@ -16,6 +16,7 @@ from .moe import (  # noqa: F401
     per_block_quant_fp8,
     per_token_group_quant_fp8,
     read_device_error,
+    select_experts,
 )
 
 __version__ = "0.1.0"

@@ -35,6 +35,7 @@ SIGNATURES = {
     "b200moe_align_capacity_rows": (_L, [_L, _I, _I]),
     "b200moe_align_capacity_blocks": (_L, [_L, _I, _I]),
     "b200moe_align": (_I, [_P, _L, _I, _I, _I, _P, _I, _P, _L, _P, _L, _P, _P, _P]),
+    "b200moe_router_topk": (_I, [_P, _I, _L, _I, _I, _I, _P, _I, ctypes.c_float, _P, _P, _P]),
     "b200moe_quant_1x128": (_I, [_P, _L, _L, _L, _P, _L, _P, _L, _L, _P]),
     "b200moe_quant_block128": (_I, [_P, _L, _L, _L, _P, _P, _P]),
     "b200moe_layer_workspace_size": (_S, [_L, _L, _L, _I, _I, _I]),

@@ -555,6 +555,19 @@ int b200moe_ep_combine(const void* returned_rows, const int32_t* pos, int64_t M,
                      "ep_combine");
 }
 
+int b200moe_router_topk(const void* logits, int logits_bf16, int64_t M, int num_experts, int topk, int scoring,
+                        const float* correction_bias, int renormalize, float scaling, float* topk_weights,
+                        int32_t* topk_ids, void* stream) {
+  if (M < 0 || num_experts <= 0 || topk <= 0 || topk > num_experts || (scoring != 0 && scoring != 1) ||
+      (M > 0 && (!logits || !topk_weights || !topk_ids)) || (correction_bias && scoring != 1))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_router_topk: bad argument%s");
+  if (num_experts > 1024 || topk > 16)
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_router_topk: at most 1024 experts and top-16%s");
+  return cuda_status(launch_router_topk(logits, logits_bf16, M, num_experts, topk, scoring, correction_bias,
+                                        renormalize, scaling, topk_weights, topk_ids, (cudaStream_t)stream),
+                     "router_topk");
+}
+
 int b200moe_read_error(int32_t* err_word, int32_t* value, int clear, void* stream) {
   if (!err_word || !value) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_read_error: null pointer%s");
   cudaStream_t s = (cudaStream_t)stream;

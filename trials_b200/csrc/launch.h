@@ -75,6 +75,10 @@ cudaError_t launch_ep_unpack_meta(const uint8_t* rows, int64_t R, int64_t row_by
 cudaError_t launch_ep_combine(const void* comb, const int32_t* pos, int64_t M, int64_t H, int G,
                               int64_t rows_per_rank, void* out, cudaStream_t stream);
 
+cudaError_t launch_router_topk(const void* logits, int bf16, int64_t M, int E, int topk, int scoring,
+                               const float* bias, int renormalize, float scaling, float* out_w, int32_t* out_ids,
+                               cudaStream_t stream);
+
 cudaError_t launch_wait_timeout_selftest(int32_t* err, uint64_t timeout_ns, cudaStream_t stream);
 
 struct GemmParams;

@@ -114,6 +114,29 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
     return sorted_ids, expert_ids, ntp
 
 
+def select_experts(router_logits: torch.Tensor, top_k: int, scoring_func: str = "softmax",
+                   correction_bias: Optional[torch.Tensor] = None, renormalize: bool = True,
+                   routed_scaling_factor: float = 1.0):
+    """Router: (M, E) f32/bf16 logits -> (topk_weights (M, k) f32, topk_ids (M, k) int32).
+    softmax: top-k softmax probabilities; sigmoid: top-k of sigmoid + correction_bias
+    with the unbiased sigmoid as weights (GLM's routing). See b200moe_router_topk."""
+    dev = _require_cuda(router_logits)
+    if router_logits.dtype not in (torch.float32, torch.bfloat16):
+        raise NotImplementedError("router logits must be float32 or bfloat16")
+    scoring = {"softmax": 0, "sigmoid": 1}.get(scoring_func)
+    if scoring is None:
+        raise NotImplementedError(f"scoring_func {scoring_func!r}")
+    logits = router_logits.contiguous()
+    M, E = logits.shape
+    w = torch.empty(M, top_k, dtype=torch.float32, device=dev)
+    ids = torch.empty(M, top_k, dtype=torch.int32, device=dev)
+    bias = None if correction_bias is None else correction_bias.to(device=dev, dtype=torch.float32).contiguous()
+    _lib.check(_lib.lib().b200moe_router_topk(_ptr(logits), int(logits.dtype == torch.bfloat16), M, E, top_k,
+                                              scoring, _ptr(bias), int(renormalize), float(routed_scaling_factor),
+                                              _ptr(w), _ptr(ids), _stream(dev)), "select_experts")
+    return w, ids
+
+
 def per_token_group_quant_fp8(x: torch.Tensor, group_size: int = 128):
     """(M, K) bf16 -> (q e4m3 (M, K), s f32 (M, K/128))."""
     if group_size != 128:
