@@ -224,7 +224,7 @@ B200MOE_API int b200moe_layer_noalloc(const void* hidden, int64_t M, int64_t H, 
  * b200moe_route: the align above with block 16 into sorted_ids (capacity
  * rows_capacity >= b200moe_route_capacity_rows()), plus the GEMM work list:
  * each expert's padded rows cut into chunks of at most tile_tokens rows
- * (16, 32, 64 or 128); chunk_expert/chunk_row0/chunk_rows[chunks_capacity],
+ * (16, 32, 64, 128 or 256); chunk_expert/chunk_row0/chunk_rows[chunks_capacity],
  * n_chunks[1] and num_rows[1] (total padded rows) on the device.
  * ---------------------------------------------------------------------- */
 B200MOE_API int64_t b200moe_route_capacity_rows(int64_t numel, int num_local_experts);

@@ -137,7 +137,8 @@ def _tiny_layer(dev, shape=synth.TINY, seed=0):
 SMALL = synth.LayerShape(M=96, H=512, I=256, E=16, topk=4, scoring="sigmoid")
 
 
-@pytest.mark.parametrize("shape,tile", [(synth.TINY, 32), (SMALL, 32), (SMALL, 64), (SMALL, 128), (SMALL, 16)])
+@pytest.mark.parametrize("shape,tile", [(synth.TINY, 32), (SMALL, 32), (SMALL, 64), (SMALL, 128), (SMALL, 16),
+                                        (SMALL, 256), (synth.TINY, 256)])
 def test_gather_and_gemm_stages(cuda_device, shape, tile):
     L, g = _tiny_layer(cuda_device, shape)
     topk = shape.topk
@@ -186,7 +187,8 @@ def test_gather_and_gemm_stages(cuda_device, shape, tile):
     assert int(r.err.item()) == 0
 
 
-@pytest.mark.parametrize("grid,tile", [(1, 32), (5, 32), (37, 32), (1, 128), (7, 128), (3, 64)])
+@pytest.mark.parametrize("grid,tile", [(1, 32), (5, 32), (37, 32), (1, 128), (7, 128), (3, 64), (2, 256),
+                                       (6, 256)])
 def test_schedule_invariance_bit_exact(cuda_device, grid, tile):
     """Any persistent grid gives bit-identical results (the reference's MODE 0/1
     equivalence check, phase3_blockscale.py:150-164)."""
@@ -285,3 +287,14 @@ def test_bounded_wait_reports_timeout_and_context_survives(cuda_device):
     q, s = moe.per_token_group_quant_fp8(x)
     rq, rs = orc.per_token_group_quant_fp8(x.cpu())
     assert torch.equal(_u8(q), _u8(rq))
+
+
+def test_layer_glm_prefill_cta_pairs_vs_oracle(cuda_device):
+    """M=8192: 256 routed rows per expert, served by the CTA-pair kernel."""
+    shape = synth.glm(8192)
+    L = synth.make_layer(shape, moe.per_block_quant_fp8, seed=0, device=cuda_device)
+    out = moe.moe_decode_megakernel_full(L.hidden, L.w13, L.w13_scale, L.w2, L.w2_scale, L.topk_weights,
+                                         L.topk_ids)
+    ref = orc.moe_layer(L.hidden, L.w13, L.w13_scale, L.w2, L.w2_scale, L.topk_weights, L.topk_ids)
+    assert orc.rel_l2(out, ref) < EXACT_TOL
+    assert int(moe.read_device_error(moe.layer_error_word(cuda_device))) == 0

@@ -80,13 +80,13 @@ int sm_count() {
   return n;
 }
 
-bool valid_tile(int t) { return t == 16 || t == 32 || t == 64 || t == 128; }
+bool valid_tile(int t) { return t == 16 || t == 32 || t == 64 || t == 128 || t == 256; }
 
 int pick_tile_tokens(int64_t numel, int E_local) {
   const double avg = (double)numel / (double)(E_local > 0 ? E_local : 1);
   if (avg <= 20.0) return 32;
   if (avg <= 48.0) return 64;
-  return 128;
+  return 128;  // 256 (CTA pairs) is available to staged callers; measured slower so far
 }
 
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
@@ -103,7 +103,7 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
   p.tile_tokens = pick_tile_tokens(numel, E_local);
   p.rows_cap = b200moe_route_capacity_rows(numel, E_local);
   p.chunks_cap = b200moe_route_capacity_chunks(numel, E_local, p.tile_tokens);
-  p.as_ld = round_up(p.rows_cap + 128, 64);
+  p.as_ld = round_up(p.rows_cap + 256, 64);
   size_t off = 256;  // device error word
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -136,7 +136,7 @@ int run_gemm(int epi, const uint8_t* a_q, const float* a_sT, int64_t as_ld, int6
              const int32_t* crows, const int32_t* n_chunks, int64_t chunks_cap, int tile_tokens, GemmParams p,
              int grid_ctas, cudaStream_t stream) {
   CUtensorMap tm_w, tm_a;
-  int st = make_tmap_u8(&tm_w, w, (int64_t)E_local * Nw, K, 256);
+  int st = make_tmap_u8(&tm_w, w, (int64_t)E_local * Nw, K, gemm_weight_box_rows(tile_tokens));
   if (st) return st;
   st = make_tmap_u8(&tm_a, a_q, rows_cap, K, gemm_tile_rows(tile_tokens));
   if (st) return st;
@@ -329,7 +329,7 @@ int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, 
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 ||
-      a_s_ld < rows_capacity + gemm_tile_rows(tile_tokens) || a_s_ld % 4 != 0 || !a1_q || !a1_sT || !w13 ||
+      a_s_ld < rows_capacity + (tile_tokens < 32 ? 32 : tile_tokens) || a_s_ld % 4 != 0 || !a1_q || !a1_sT || !w13 ||
       !w13_scale || !chunk_expert || !chunk_row0 || !chunk_rows || !n_chunks || !a2_q || !a2_sT || !err_word)
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_gemm1_silu: bad argument%s");
   if (!aligned16(a1_q) || !aligned16(w13) || !aligned16(a1_sT) || !aligned16(a2_q))
@@ -354,7 +354,7 @@ int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_l
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 || M < 0 || topk <= 0 ||
-      a_s_ld < rows_capacity + gemm_tile_rows(tile_tokens) || a_s_ld % 4 != 0 || !a2_q || !a2_sT || !w2 ||
+      a_s_ld < rows_capacity + (tile_tokens < 32 ? 32 : tile_tokens) || a_s_ld % 4 != 0 || !a2_q || !a2_sT || !w2 ||
       !w2_scale || !chunk_expert || !chunk_row0 || !chunk_rows || !n_chunks || !sorted_ids || !topk_weights ||
       !out_pair || !err_word)
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_gemm2_combine: bad argument%s");

@@ -2,6 +2,7 @@
 #include "launch.h"
 #include "moe_gemm.cuh"
 #include "moe_gemm_tok.cuh"
+#include "moe_gemm_tok2.cuh"
 
 namespace b200moe {
 
@@ -29,6 +30,34 @@ cudaError_t launch_tok(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const G
 }
 
 template <int EPI>
+cudaError_t launch_tok2(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p, int grid,
+                        cudaStream_t stream) {
+  auto kernel = moe_grouped_gemm_tok2_kernel<EPI>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tok2Cfg::SMEM_BYTES);
+  if (err != cudaSuccess) return err;
+  // Pairs that can be resident at once (clusters must fit inside a GPC).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(Tok2Cfg::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Tok2Cfg::SMEM_BYTES;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int max_clusters = 0;
+  err = cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &cfg);
+  if (err != cudaSuccess) return err;
+  int pairs = grid / 2;
+  if (max_clusters > 0 && pairs > max_clusters) pairs = max_clusters;
+  if (pairs < 1) pairs = 1;
+  kernel<<<2 * pairs, Tok2Cfg::THREADS, Tok2Cfg::SMEM_BYTES, stream>>>(tm_w, tm_a, p);
+  return cudaGetLastError();
+}
+
+template <int EPI>
 cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p,
                        int grid, cudaStream_t stream) {
   switch (tile_tokens) {
@@ -42,6 +71,9 @@ cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorM
     case 128:
       // Many tokens per expert: routed rows on the MMA M side.
       return launch_tok<EPI>(tm_w, tm_a, p, grid, stream);
+    case 256:
+      // Even more: CTA pairs with a 256-row MMA.
+      return launch_tok2<EPI>(tm_w, tm_a, p, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -57,7 +89,8 @@ int gemm_tile_rows(int tile_tokens) {
     case 64:
       return 64;
     case 128:
-      return 128;
+    case 256:
+      return 128;  // per CTA for 256 (pairs)
     default:
       return 0;
   }
@@ -66,6 +99,7 @@ int gemm_tile_rows(int tile_tokens) {
 cudaError_t launch_grouped_gemm(int epi, int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a,
                                 const GemmParams& p, int grid, cudaStream_t stream) {
   if (grid <= 0) return cudaSuccess;
+  if (tile_tokens == 256 && grid < 2) grid = 2;
   if (epi == EPI_SILU) return launch_epi<EPI_SILU>(tile_tokens, tm_w, tm_a, p, grid, stream);
   return launch_epi<EPI_COMBINE>(tile_tokens, tm_w, tm_a, p, grid, stream);
 }

@@ -85,8 +85,10 @@ struct GemmParams;
 // epi: 0 = SiLU + requant (stage 1), 1 = weighted combine (stage 2).
 cudaError_t launch_grouped_gemm(int epi, int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a,
                                 const GemmParams& p, int grid, cudaStream_t stream);
-// Activation tile rows the kernel for this tile_tokens loads per stage.
+// Activation tile rows the kernel for this tile_tokens loads per stage (per CTA).
 int gemm_tile_rows(int tile_tokens);
+// Weight rows per TMA box (per CTA).
+inline int gemm_weight_box_rows(int tile_tokens) { return tile_tokens == 256 ? 128 : 256; }
 
 // Records a message for b200moe_last_error_message() and returns status.
 int record_error(int status, const char* message);

@@ -39,7 +39,7 @@ class Routing:
         return self.counts[1:2]
 
     def a_s_ld(self) -> int:
-        return (self.rows_cap + 128 + 63) // 64 * 64
+        return (self.rows_cap + 256 + 63) // 64 * 64
 
 
 def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map: Optional[torch.Tensor] = None,
@@ -157,7 +157,7 @@ class LayerPipeline:
         self.tile = tile_tokens or pick_tile_tokens(numel, self.E)
         self.rows_cap = L.b200moe_route_capacity_rows(numel, self.E)
         self.chunks_cap = L.b200moe_route_capacity_chunks(numel, self.E, self.tile)
-        self.ld = (self.rows_cap + 128 + 63) // 64 * 64
+        self.ld = (self.rows_cap + 256 + 63) // 64 * 64
         z = lambda n: torch.zeros(max(n, 1), dtype=torch.int32, device=device)  # noqa: E731
         self.sorted_ids, self.ce, self.cr0, self.crows = z(self.rows_cap), z(self.chunks_cap), z(self.chunks_cap), \
             z(self.chunks_cap)
