@@ -38,6 +38,24 @@
 #include "common.cuh"
 #include "ptx.cuh"
 
+// Weight tiles stream once per launch. An evict_first L2 hint on them measured
+// slower than no hint on a pure TMA read stream (6.9 vs 7.0 TB/s) and no faster
+// in this kernel, so it is off unless this is set to 1.
+#ifndef B200MOE_W_EVICT_FIRST
+#define B200MOE_W_EVICT_FIRST 0
+#endif
+// K blocks the epilogue promotes per round when a thread holds 32 token
+// columns: the TMEM loads of a round share one wait, and the barrier waits and
+// releases of a round follow each other, so the epilogue's fixed latency per
+// K block shrinks by this factor.
+#ifndef B200MOE_EPI_KR
+#define B200MOE_EPI_KR 2
+#endif
+// SiLU with the fast (2 ulp) division; 0 selects IEEE division.
+#ifndef B200MOE_FAST_SILU
+#define B200MOE_FAST_SILU 1
+#endif
+
 namespace b200moe {
 
 enum { EPI_SILU = 0, EPI_COMBINE = 1 };
@@ -79,6 +97,7 @@ struct GemmCfg {
   static constexpr int UNIT_ROWS = 128 * NSUB; // weight rows per unit
   static constexpr int THREADS = 64 + 32 * EW;
   static constexpr int TC = T / CS;            // token columns per epilogue thread
+  static constexpr int KR = (TC <= 32 && CS == 1) ? B200MOE_EPI_KR : 1;  // K blocks per epilogue round
   static constexpr int W_BYTES = UNIT_ROWS * 128;
   static constexpr int A_BYTES = T * 128;
   static constexpr int TILE_BYTES = W_BYTES + A_BYTES;  // multiple of 1024
@@ -101,11 +120,21 @@ struct GemmCfg {
   static_assert(T % 16 == 0 && T >= 16 && T <= 256, "MMA N must be a multiple of 16 in [16, 256]");
   static_assert(TC % 32 == 0, "columns per epilogue thread must be a multiple of 32");
   static_assert(NBUF >= 2, "need at least two TMEM buffers");
+  static_assert(KR >= 1 && 2 * KR <= NBUF, "epilogue round must leave the MMA TMEM buffers to fill");
   static_assert(NSTAGE >= 2, "shared memory too small");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
 };
 
-__device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + __expf(-g)); }
+__device__ __forceinline__ float silu_f32(float g) {
+#if B200MOE_FAST_SILU
+  // __fdividef is accurate to 2 ulp for divisors below 2^126; above that
+  // (g < -87) silu(g) rounds to -0 anyway.
+  const float d = 1.0f + __expf(-g);
+  return d < 1e30f ? __fdividef(g, d) : -0.0f;
+#else
+  return g / (1.0f + __expf(-g));
+#endif
+}
 
 // Column maxima for values spread over lane pairs: lane l holds, for m < 16,
 // |value| of column 2m + (l & 1). Returns, in lane l, the max over the 16
@@ -195,11 +224,20 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
       uint32_t phase = 0, sphase = 0;
       long issued = 0;
       bool ok = true;
+      // Chunk metadata is loaded one unit ahead, off the critical path.
+      int e_n = 0, p0_n = 0;
+      if (blockIdx.x < n_units) {
+        e_n = __ldg(&p.chunk_expert[blockIdx.x / NT]);
+        p0_n = __ldg(&p.chunk_row0[blockIdx.x / NT]);
+      }
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const int chunk = u / NT;
         const int nt = u - chunk * NT;
-        const int e = __ldg(&p.chunk_expert[chunk]);
-        const int p0 = __ldg(&p.chunk_row0[chunk]);
+        const int e = e_n, p0 = p0_n;
+        if (u + (int)gridDim.x < n_units) {
+          e_n = __ldg(&p.chunk_expert[(u + gridDim.x) / NT]);
+          p0_n = __ldg(&p.chunk_row0[(u + gridDim.x) / NT]);
+        }
         const int wrow = e * p.Nw + nt * C::UNIT_ROWS;
         for (int kb = 0; kb < NKB; ++kb) {
           if (*abort_flag || !mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns) ||
@@ -209,7 +247,11 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
           }
           uint8_t* tile = tiles + stage * C::TILE_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::TILE_BYTES);
+#if B200MOE_W_EVICT_FIRST
           tma_load_2d(tile, &tm_w, &full[stage], kb * 128, wrow, pol_w);
+#else
+          tma_load_2d(tile, &tm_w, &full[stage], kb * 128, wrow);
+#endif
           tma_load_2d(tile + C::W_BYTES, &tm_a, &full[stage], kb * 128, p0, pol_a);
           mbar_arrive_expect_tx(&sfull[slot], C::S_BYTES);
           bulk_load(sscale + slot * T, p.a_sT + (int64_t)kb * p.as_ld + p0, C::S_BYTES, &sfull[slot]);
@@ -245,9 +287,10 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
       int last_buf = 0;
       uint32_t last_bphase = 0;
       bool ok = true;
+      int rows_n = blockIdx.x < n_units ? __ldg(&p.chunk_rows[blockIdx.x / NT]) : 0;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const int chunk = u / NT;
-        const int rows = __ldg(&p.chunk_rows[chunk]);
+        const int rows = rows_n;
+        if (u + (int)gridDim.x < n_units) rows_n = __ldg(&p.chunk_rows[(u + gridDim.x) / NT]);
         const uint32_t idesc = idesc_e4m3_f32(128, rows);
         for (int kb = 0; kb < NKB; ++kb) {
           if (*abort_flag || !mbar_wait_bounded(&tempty[buf], bphase ^ 1, p.timeout_ns)) {
@@ -303,61 +346,121 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
     int slot = 0, buf = 0;
     uint32_t sphase = 0, bphase = 0;
     bool ok = true;
+    // Chunk metadata is loaded one unit ahead, and the unit's weight block
+    // scales (one per K block of this 128-row half) are spread over the lanes
+    // (K blocks lane and lane + 32) and loaded before the previous unit's
+    // final epilogue, so no global load sits on the per-K-block path.
+    auto ws_row = [&](int e, int nt) { return p.w_scale + ((int64_t)e * (p.Nw >> 7) + nt * 2 + hs) * NKB; };
+    int e_n = 0, p0_n = 0, rows_n = 0;
+    float wl0 = 0.f, wl1 = 0.f;
+    if (blockIdx.x < n_units) {
+      const int c = blockIdx.x / NT;
+      e_n = __ldg(&p.chunk_expert[c]);
+      p0_n = __ldg(&p.chunk_row0[c]);
+      rows_n = __ldg(&p.chunk_rows[c]);
+      const float* w = ws_row(e_n, blockIdx.x - c * NT);
+      wl0 = lane < NKB ? __ldg(w + lane) : 0.f;
+      wl1 = lane + 32 < NKB ? __ldg(w + lane + 32) : 0.f;
+    }
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int chunk = u / NT;
       const int nt = u - chunk * NT;
-      const int e = __ldg(&p.chunk_expert[chunk]);
-      const int p0 = __ldg(&p.chunk_row0[chunk]);
-      const int rows = __ldg(&p.chunk_rows[chunk]);
-      const float* wsp = p.w_scale + ((int64_t)e * (p.Nw >> 7) + nt * 2 + hs) * NKB;
+      const int e = e_n, p0 = p0_n, rows = rows_n;
+      const float ws0 = wl0, ws1 = wl1;
+      const float* wsp = ws_row(e, nt);
+      const int un = u + gridDim.x;
+      const int cn = un / NT;
+      if (un < n_units) {
+        e_n = __ldg(&p.chunk_expert[cn]);
+        p0_n = __ldg(&p.chunk_row0[cn]);
+        rows_n = __ldg(&p.chunk_rows[cn]);
+      }
 
       float acc[C::TC];
 #pragma unroll
       for (int j = 0; j < C::TC; ++j) acc[j] = 0.f;
 
-      float ws = __ldg(wsp);
-      for (int kb = 0; kb < NKB && ok; ++kb) {
-        const float wsn = (kb + 1 < NKB) ? __ldg(wsp + kb + 1) : 0.f;
-        if (*abort_flag || !mbar_wait_bounded(&tfull[buf], bphase, p.timeout_ns)) {
+      constexpr int KR = C::KR;
+      for (int kb = 0; kb < NKB && ok; kb += KR) {
+        const int nr = NKB - kb < KR ? NKB - kb : KR;
+        float wsr[KR];
+        int bufr[KR], slotr[KR];
+        bool good = *abort_flag == 0;
+#pragma unroll
+        for (int r = 0; r < KR; ++r) {
+          int b = buf + r, sl = slot + r;
+          uint32_t bp = bphase, sp = sphase;
+          if (b >= C::NBUF) {
+            b -= C::NBUF;
+            bp ^= 1;
+          }
+          if (sl >= C::NSLOT) {
+            sl -= C::NSLOT;
+            sp ^= 1;
+          }
+          bufr[r] = b;
+          slotr[r] = sl;
+          const int k = kb + r;
+          const float wsh = __shfl_sync(0xffffffffu, k < 32 ? ws0 : ws1, k & 31);
+          wsr[r] = k < 64 ? wsh : (k < NKB ? __ldg(wsp + k) : 0.f);
+          if (r < nr && good)
+            good = mbar_wait_bounded(&tfull[b], bp, p.timeout_ns) && mbar_wait_bounded(&sfull[sl], sp, p.timeout_ns);
+        }
+        if (!good) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (!mbar_wait_bounded(&sfull[slot], sphase, p.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        const float* ss = sscale + slot * T + col0;
 #pragma unroll
         for (int cc = 0; cc < C::TC / 16; ++cc) {
           if (col0 + cc * 16 < rows) {  // warp-uniform
-            uint32_t r[16];
-            tmem_ld16(tmem_base + lane_base + (uint32_t)(buf * 2 * T + hs * T + col0 + cc * 16), r);
-            tmem_wait_ld16(r);
+            uint32_t v[KR][16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              acc[cc * 16 + i] = fmaf(__uint_as_float(r[i]), ws * ss[cc * 16 + i], acc[cc * 16 + i]);
+            for (int r = 0; r < KR; ++r)
+              if (r < nr)
+                tmem_ld16(tmem_base + lane_base + (uint32_t)(bufr[r] * 2 * T + hs * T + col0 + cc * 16), v[r]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int r = 0; r < KR; ++r)
+              if (r < nr) {
+                const float* ss = sscale + slotr[r] * T + col0 + cc * 16;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  tmem_reg_fence(v[r][i]);
+                  acc[cc * 16 + i] = fmaf(__uint_as_float(v[r][i]), wsr[r] * ss[i], acc[cc * 16 + i]);
+                }
+              }
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&tempty[buf]);
-          mbar_arrive(&sempty[slot]);
+#pragma unroll
+          for (int r = 0; r < KR; ++r)
+            if (r < nr) {
+              mbar_arrive(&tempty[bufr[r]]);
+              mbar_arrive(&sempty[slotr[r]]);
+            }
         }
-        ws = wsn;
-        if (++slot == C::NSLOT) {
-          slot = 0;
-          sphase ^= 1;
-        }
-        if (++buf == C::NBUF) {
-          buf = 0;
+        buf += nr;
+        if (buf >= C::NBUF) {
+          buf -= C::NBUF;
           bphase ^= 1;
+        }
+        slot += nr;
+        if (slot >= C::NSLOT) {
+          slot -= C::NSLOT;
+          sphase ^= 1;
         }
       }
       if (!ok) {
         atomicOr(p.err, ERR_DEV_TIMEOUT);
         *abort_flag = 1;
+      }
+      if (un < n_units) {
+        const float* w = ws_row(e_n, un - cn * NT);
+        wl0 = lane < NKB ? __ldg(w + lane) : 0.f;
+        wl1 = lane + 32 < NKB ? __ldg(w + lane + 32) : 0.f;
       }
 
       if constexpr (EPI == EPI_SILU) {

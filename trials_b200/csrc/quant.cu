@@ -7,17 +7,23 @@ namespace b200moe {
 
 // ---------------------------------------------------------------------------
 // 1 x 128 per-token-group quantisation (per_token_group_quant_fp8,
-// phase5_orchestrator.py:26-32). One warp per output row; each lane converts 8
-// consecutive bf16 (one 16-byte load), a half-warp covers one 128-column
-// group, so a warp step handles 256 columns.
+// phase5_orchestrator.py:26-32). One warp per (output row, 1024-column
+// segment): each lane converts 8 consecutive bf16 per 16-byte load, a
+// half-warp covers one 128-column group, and the warp issues the loads of its
+// four 256-column steps before it reduces any of them, so a row's latency is
+// one load round trip rather than K/256 of them.
 // ---------------------------------------------------------------------------
 constexpr int kQuantWarps = 8;
+constexpr int kQuantSegSteps = 4;
+constexpr int kQuantSegCols = 256 * kQuantSegSteps;
 
 __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const QuantArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
   const int64_t n_rows = a.num_rows ? (int64_t)(*a.num_rows) : a.rows;
   if (row >= n_rows || row >= a.rows) return;
+  const int64_t seg0 = (int64_t)blockIdx.y * kQuantSegCols;
+  const int64_t seg_end = seg0 + kQuantSegCols < a.K ? seg0 + kQuantSegCols : a.K;
   int64_t src = row;
   if (a.sorted_ids) {
     const int f = __ldg(&a.sorted_ids[row]);
@@ -26,50 +32,58 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
   uint8_t* qr = a.q + row * a.ldq;
   if (a.xq != nullptr) {
     // Copy mode: the input is already quantised.
-    const int64_t n16 = a.K / 16;
-    uint4* dq = reinterpret_cast<uint4*>(qr);
     if (src >= 0) {
-      const uint4* sq = reinterpret_cast<const uint4*>(a.xq + src * a.ldxq);
-      for (int64_t i = lane; i < n16; i += 32) dq[i] = __ldg(&sq[i]);
-      for (int64_t g = lane; g < a.K / 128; g += 32) a.s[row * a.s_row + g * a.s_grp] = __ldg(&a.xs[src * a.ldxs + g]);
+      const uint8_t* sq = a.xq + src * a.ldxq;
+      for (int64_t b = seg0 + lane * 16; b < seg_end; b += 512)
+        *reinterpret_cast<uint4*>(qr + b) = __ldg(reinterpret_cast<const uint4*>(sq + b));
+      const int64_t g = (seg0 >> 7) + lane;
+      if (lane < kQuantSegCols / 128 && g * 128 < seg_end)
+        a.s[row * a.s_row + g * a.s_grp] = __ldg(&a.xs[src * a.ldxs + g]);
     } else {
-      for (int64_t i = lane; i < n16; i += 32) dq[i] = make_uint4(0, 0, 0, 0);
-      for (int64_t g = lane; g < a.K / 128; g += 32) a.s[row * a.s_row + g * a.s_grp] = 0.f;
+      for (int64_t b = seg0 + lane * 16; b < seg_end; b += 512)
+        *reinterpret_cast<uint4*>(qr + b) = make_uint4(0, 0, 0, 0);
+      const int64_t g = (seg0 >> 7) + lane;
+      if (lane < kQuantSegCols / 128 && g * 128 < seg_end) a.s[row * a.s_row + g * a.s_grp] = 0.f;
     }
     return;
   }
   const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
-  for (int64_t c0 = 0; c0 < a.K; c0 += 256) {
-    const int64_t c = c0 + lane * 8;
-    const bool in = c < a.K;
-    float v[8];
-    if (src >= 0 && in) {
+  float v[kQuantSegSteps][8];
+#pragma unroll
+  for (int i = 0; i < kQuantSegSteps; ++i) {
+    const int64_t c = seg0 + i * 256 + lane * 8;
+    if (src >= 0 && c < seg_end) {
       const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + c));
       const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f2 = __bfloat1622float2(h2[i]);
-        v[2 * i] = f2.x;
-        v[2 * i + 1] = f2.y;
+      for (int j = 0; j < 4; ++j) {
+        const float2 f2 = __bfloat1622float2(h2[j]);
+        v[i][2 * j] = f2.x;
+        v[i][2 * j + 1] = f2.y;
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
     }
+  }
+#pragma unroll
+  for (int i = 0; i < kQuantSegSteps; ++i) {
+    if (seg0 + i * 256 >= seg_end) break;  // warp-uniform
+    const int64_t c = seg0 + i * 256 + lane * 8;
     float m = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
 #pragma unroll
     for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (!in) continue;
+    if (c >= seg_end) continue;
     uint32_t lo = 0, hi = 0;
     float scale = 0.f;
     if (src >= 0) {
       scale = group_scale(m);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) lo |= (uint32_t)quant_e4m3(v[i], scale) << (8 * i);
+      for (int j = 0; j < 4; ++j) lo |= (uint32_t)quant_e4m3(v[i][j], scale) << (8 * j);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) hi |= (uint32_t)quant_e4m3(v[4 + i], scale) << (8 * i);
+      for (int j = 0; j < 4; ++j) hi |= (uint32_t)quant_e4m3(v[i][4 + j], scale) << (8 * j);
     }
     *reinterpret_cast<uint2*>(qr + c) = make_uint2(lo, hi);
     if ((lane & 15) == 0) a.s[row * a.s_row + (c >> 7) * a.s_grp] = scale;
@@ -77,9 +91,10 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
 }
 
 cudaError_t launch_quant_1x128(const QuantArgs& a, cudaStream_t stream) {
-  if (a.rows <= 0) return cudaSuccess;
+  if (a.rows <= 0 || a.K <= 0) return cudaSuccess;
   const int64_t blocks = (a.rows + kQuantWarps - 1) / kQuantWarps;
-  quant_1x128_kernel<<<(unsigned)blocks, kQuantWarps * 32, 0, stream>>>(a);
+  const dim3 grid((unsigned)blocks, (unsigned)((a.K + kQuantSegCols - 1) / kQuantSegCols));
+  quant_1x128_kernel<<<grid, kQuantWarps * 32, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
