@@ -53,6 +53,7 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-sample-experts", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--split", action="store_true", help="the two GEMM stages as two launches (default: one)")
     return ap.parse_args(argv)
 
 
@@ -175,6 +176,14 @@ def layer_bytes(shape, active, pairs):
 
     w = active * (synth.weight_bytes_per_expert(shape.H, shape.I) + synth.scale_bytes_per_expert(shape.H, shape.I))
     return w + shape.M * shape.H * 2 * 2
+
+
+def gemm2_bytes(shape, active, pairs):
+    """Algorithmic bytes of one GEMM2 launch: w2 + its scales of every active
+    expert, the fp8 inter rows and scales read, the fp32 weighted rows written."""
+    H, I = shape.H, shape.I
+    w = active * (H * I + 4 * (H // 128) * (I // 128))
+    return w + pairs * (I + 4 * I // 128) + pairs * H * 4
 
 
 def gemm1_bytes(shape, active, pairs):
@@ -396,7 +405,8 @@ def run_ours(args, shape, config):
     L = synth.make_layer(shape, moe.per_block_quant_fp8, seed=args.seed + rank, device=dev)
     active = synth.active_experts(L.topk_ids, shape.E)
     pairs = int(((L.topk_ids >= 0) & (L.topk_ids < shape.E)).sum().item())
-    pipe = stages.LayerPipeline(shape.M, shape.H, shape.I, shape.E, shape.topk, dev, tile_tokens=args.tile)
+    pipe = stages.LayerPipeline(shape.M, shape.H, shape.I, shape.E, shape.topk, dev, tile_tokens=args.tile,
+                                split=args.split)
     args_run = (L.hidden, L.topk_ids, L.topk_weights, L.w13, L.w13_scale, L.w2, L.w2_scale)
 
     def barrier():
@@ -414,7 +424,7 @@ def run_ours(args, shape, config):
     # ---- device-resident timing (value)
     for _ in range(args.warmup):
         pipe.run(*args_run)
-    n_ev = 6
+    n_ev = len(pipe.stages) + 1
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
@@ -429,7 +439,7 @@ def run_ours(args, shape, config):
     clocks.window(t0, clocks.mark())
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
     stage_ms = {name: statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(args.steps))
-                for i, name in enumerate(stages.LayerPipeline.STAGES)}
+                for i, name in enumerate(pipe.stages)}
     err = int(pipe.err.item())
     if err:
         raise RuntimeError(f"device error word {err} after the timed steps")
@@ -479,10 +489,18 @@ def run_ours(args, shape, config):
             dist.destroy_process_group()
         return 0
     peak, peak_kind = measured_peaks()
-    g1_bytes = gemm1_bytes(shape, active, pairs)
-    g1_ms = stage_ms["gemm1_silu"]
-    achieved = g1_bytes / (g1_ms / 1e3) / 1e9
-    traffic_name = f"gemm1_silu_glm_decode_m{shape.M}" + (f"_hot{shape.hot_experts}" if shape.hot_experts else "")
+    hot = f"_hot{shape.hot_experts}" if shape.hot_experts else ""
+    if "experts" in stage_ms:
+        # Both GEMM stages in one launch (two launches for token-major tiles).
+        k_name, k_bytes, k_ms = "experts (grouped GEMM, both stages)", \
+            gemm1_bytes(shape, active, pairs) + gemm2_bytes(shape, active, pairs), stage_ms["experts"]
+        traffic_name = f"experts_glm_decode_m{shape.M}{hot}"
+    else:
+        k_name, k_bytes, k_ms = "gemm1_silu (grouped GEMM stage 1)", gemm1_bytes(shape, active, pairs), \
+            stage_ms["gemm1_silu"]
+        traffic_name = f"gemm1_silu_glm_decode_m{shape.M}{hot}"
+    achieved = k_bytes / (k_ms / 1e3) / 1e9
+    launches = len(pipe.stages) + (1 if not args.split and pipe.tile > 64 else 0)
     step_bytes = layer_bytes(shape, active, pairs)
     line = {
         "metric": METRIC,
@@ -502,11 +520,11 @@ def run_ours(args, shape, config):
         "hbm_frac": step_bytes / (ms / 1e3) / 1e9 / peak,
         "active_experts": active,
         "stage_ms": stage_ms,
-        "roofline": {"kernel": "gemm1_silu (grouped GEMM stage 1)", "bound": "hbm", "achieved": achieved,
+        "roofline": {"kernel": k_name, "bound": "hbm", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": f"{peak_kind} HBM copy bandwidth",
-                     "algorithmic_bytes_per_launch": g1_bytes, "traffic": ncu_traffic(traffic_name)},
-        "gpu_launches": 5 * args.steps,
+                     "algorithmic_bytes_per_launch": k_bytes, "traffic": ncu_traffic(traffic_name)},
+        "gpu_launches": launches * args.steps,
         "clocks": clk,
     }
     if e2e is not None:

@@ -225,14 +225,16 @@ B200MOE_API int b200moe_layer_noalloc(const void* hidden, int64_t M, int64_t H, 
  * rows_capacity >= b200moe_route_capacity_rows()), plus the GEMM work list:
  * each expert's padded rows cut into chunks of at most tile_tokens rows
  * (16, 32, 64, 128 or 256); chunk_expert/chunk_row0/chunk_rows[chunks_capacity],
- * n_chunks[1] and num_rows[1] (total padded rows) on the device.
+ * n_chunks[1] and num_rows[1] (total padded rows) on the device. chunk_ready
+ * (nullable, chunks_capacity entries) is zeroed for b200moe_experts.
  * ---------------------------------------------------------------------- */
 B200MOE_API int64_t b200moe_route_capacity_rows(int64_t numel, int num_local_experts);
 B200MOE_API int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_experts, int tile_tokens);
 B200MOE_API int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
                   int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
                   int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
-                  int32_t* n_chunks, int32_t* num_rows, int32_t* err_word, void* stream);
+                  int32_t* n_chunks, int32_t* num_rows, int32_t* chunk_ready, int32_t* err_word,
+                  void* stream);
 
 /* Quantise hidden rows into the sorted layout: row p of a_q (ld = H) holds
  * q(hidden[sorted_ids[p] / topk]) or zeros for a padding row; scales go to
@@ -260,6 +262,23 @@ B200MOE_API int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, i
                           const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
                           const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
                           float* out_pair, int32_t* err_word, int grid_ctas, void* stream);
+
+/* Stage 1 and stage 2 in one persistent launch (the reference's fused
+ * stage-1 / stage-2 launcher pair, moe_decode_megakernel_fused.py:125-157,
+ * as one kernel): same arguments and results as b200moe_gemm1_silu followed
+ * by b200moe_gemm2_combine, bit for bit. A stage-2 work unit of a chunk
+ * starts as soon as the stage-1 units of that chunk have written their rows,
+ * which they count in chunk_ready (zeroed by b200moe_route for this call), so
+ * the weight stream does not stop between the stages. Tiles of 16..64 tokens
+ * run fused (cooperative launch, one CTA per SM); 128 and 256 run the two
+ * stage kernels back to back. */
+B200MOE_API int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
+                    const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                    int num_local_experts, int64_t H, int64_t I, const int32_t* chunk_expert,
+                    const int32_t* chunk_row0, const int32_t* chunk_rows, const int32_t* n_chunks,
+                    int64_t chunks_capacity, int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
+                    const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, float* out_pair,
+                    int32_t* err_word, int grid_ctas, void* stream);
 
 /* out[t, :] = bf16( sum_{j valid} out_pair[t*topk + j, :] ), slots summed in
  * order j = 0..topk-1; a slot is valid when its id is in [0, num_experts)

@@ -203,6 +203,27 @@ def test_schedule_invariance_bit_exact(cuda_device, grid, tile):
     assert torch.equal(p0, p1)
 
 
+@pytest.mark.parametrize("shape,tile,grid", [(synth.TINY, 32, 0), (SMALL, 16, 0), (SMALL, 32, 0), (SMALL, 64, 0),
+                                             (SMALL, 32, 1), (SMALL, 32, 5), (SMALL, 64, 37), (SMALL, 32, 148),
+                                             (SMALL, 128, 0)])
+def test_fused_experts_bit_identical_to_split(cuda_device, shape, tile, grid):
+    """Both GEMM stages in one launch (stage-2 units wait per chunk on the
+    stage-1 units) give exactly the two-launch results, for any grid."""
+    L, g = _tiny_layer(cuda_device, shape, seed=2)
+    r = stages.route(g["topk_ids"], shape.E, tile)
+    a1_q, a1_sT = stages.gather_quant(g["hidden"], shape.topk, r)
+    q1, s1 = stages.gemm1_silu(a1_q, a1_sT, g["w13"], g["w13_scale"], r)
+    p1 = stages.gemm2_combine(q1, s1, g["w2"], g["w2_scale"], r, g["topk_weights"])
+    q2, s2, p2 = stages.experts(a1_q, a1_sT, g["w13"], g["w13_scale"], g["w2"], g["w2_scale"], r,
+                                g["topk_weights"], grid_ctas=grid)
+    torch.cuda.synchronize()
+    assert torch.equal(_u8(q1), _u8(q2)) and torch.equal(s1, s2) and torch.equal(p1, p2)
+    assert int(r.err.item()) == 0
+    if tile <= 64:
+        nc = int(r.counts[0].item())
+        assert (r.chunk_ready[:nc] == 2 * shape.I // 256).all()
+
+
 # ----------------------------------------------------------------------------
 # full layer
 # ----------------------------------------------------------------------------

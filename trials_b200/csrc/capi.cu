@@ -94,7 +94,8 @@ constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
 struct LayerPlan {
   int tile_tokens;
   int64_t rows_cap, chunks_cap, as_ld;
-  size_t off_sorted, off_ce, off_cr0, off_crows, off_counts, off_a1, off_a1s, off_a2, off_a2s, off_pair, total;
+  size_t off_sorted, off_ce, off_cr0, off_crows, off_ready, off_counts, off_a1, off_a1s, off_a2, off_a2s, off_pair,
+      total;
 };
 
 LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
@@ -114,6 +115,7 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
   p.off_ce = take(sizeof(int32_t) * p.chunks_cap);
   p.off_cr0 = take(sizeof(int32_t) * p.chunks_cap);
   p.off_crows = take(sizeof(int32_t) * p.chunks_cap);
+  p.off_ready = take(sizeof(int32_t) * p.chunks_cap);
   p.off_counts = take(sizeof(int32_t) * 4);
   p.off_a1 = take((size_t)p.rows_cap * H);
   p.off_a1s = take(sizeof(float) * (size_t)(H / 128) * p.as_ld);
@@ -131,11 +133,11 @@ int check_gemm_shapes(int64_t H, int64_t I) {
   return B200MOE_OK;
 }
 
-int run_gemm(int epi, const uint8_t* a_q, const float* a_sT, int64_t as_ld, int64_t rows_cap, const uint8_t* w,
-             const float* w_scale, int E_local, int64_t Nw, int64_t K, const int32_t* ce, const int32_t* cr0,
-             const int32_t* crows, const int32_t* n_chunks, int64_t chunks_cap, int tile_tokens, GemmParams p,
-             int grid_ctas, cudaStream_t stream) {
-  CUtensorMap tm_w, tm_a;
+// Tensor maps and the operand / work-list fields of one grouped GEMM stage.
+int prep_gemm(const uint8_t* a_q, const float* a_sT, int64_t as_ld, int64_t rows_cap, const uint8_t* w,
+              const float* w_scale, int E_local, int64_t Nw, int64_t K, const int32_t* ce, const int32_t* cr0,
+              const int32_t* crows, const int32_t* n_chunks, int tile_tokens, GemmParams& p, CUtensorMap& tm_w,
+              CUtensorMap& tm_a) {
   int st = make_tmap_u8(&tm_w, w, (int64_t)E_local * Nw, K, gemm_weight_box_rows(tile_tokens));
   if (st) return st;
   st = make_tmap_u8(&tm_a, a_q, rows_cap, K, gemm_tile_rows(tile_tokens));
@@ -150,6 +152,17 @@ int run_gemm(int epi, const uint8_t* a_q, const float* a_sT, int64_t as_ld, int6
   p.K = (int)K;
   p.Nw = (int)Nw;
   p.timeout_ns = kTimeoutNs;
+  return B200MOE_OK;
+}
+
+int run_gemm(int epi, const uint8_t* a_q, const float* a_sT, int64_t as_ld, int64_t rows_cap, const uint8_t* w,
+             const float* w_scale, int E_local, int64_t Nw, int64_t K, const int32_t* ce, const int32_t* cr0,
+             const int32_t* crows, const int32_t* n_chunks, int64_t chunks_cap, int tile_tokens, GemmParams p,
+             int grid_ctas, cudaStream_t stream) {
+  CUtensorMap tm_w, tm_a;
+  int st = prep_gemm(a_q, a_sT, as_ld, rows_cap, w, w_scale, E_local, Nw, K, ce, cr0, crows, n_chunks, tile_tokens,
+                     p, tm_w, tm_a);
+  if (st) return st;
   const int64_t units_cap = chunks_cap * (Nw / 256);
   int64_t grid = grid_ctas > 0 ? grid_ctas : sm_count();
   if (grid > units_cap) grid = units_cap;
@@ -263,7 +276,7 @@ int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_experts, int 
 int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
                   int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
                   int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
-                  int32_t* n_chunks, int32_t* num_rows, int32_t* err_word, void* stream) {
+                  int32_t* n_chunks, int32_t* num_rows, int32_t* chunk_ready, int32_t* err_word, void* stream) {
   if (M < 0 || topk <= 0 || num_experts <= 0 || !valid_tile(tile_tokens) || !sorted_ids || !chunk_expert ||
       !chunk_row0 || !chunk_rows || !n_chunks || !num_rows || !err_word || (M > 0 && !topk_ids))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_route: bad argument%s");
@@ -292,6 +305,7 @@ int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts,
   a.chunk_rows = chunk_rows;
   a.chunks_cap = chunks_capacity;
   a.n_chunks = n_chunks;
+  a.chunk_ready = chunk_ready;
   a.err = err_word;
   return cuda_status(launch_align(a, (cudaStream_t)stream), "route");
 }
@@ -371,6 +385,60 @@ int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_l
                   (cudaStream_t)stream);
 }
 
+int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
+                    const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                    int num_local_experts, int64_t H, int64_t I, const int32_t* chunk_expert,
+                    const int32_t* chunk_row0, const int32_t* chunk_rows, const int32_t* n_chunks,
+                    int64_t chunks_capacity, int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
+                    const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, float* out_pair,
+                    int32_t* err_word, int grid_ctas, void* stream) {
+  if (tile_tokens > 64) {
+    // Token-major tiles: the two stages as two launches.
+    int st = b200moe_gemm1_silu(a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, H, I,
+                                chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, a2_q,
+                                a2_sT, err_word, grid_ctas, stream);
+    if (st) return st;
+    return b200moe_gemm2_combine(a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I,
+                                 chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens,
+                                 sorted_ids, topk_weights, M, topk, out_pair, err_word, grid_ctas, stream);
+  }
+  int st = check_gemm_shapes(H, I);
+  if (st) return st;
+  if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 || M < 0 || topk <= 0 ||
+      a_s_ld < rows_capacity + (tile_tokens < 32 ? 32 : tile_tokens) || a_s_ld % 4 != 0 || !a1_q || !a1_sT ||
+      !w13 || !w13_scale || !w2 || !w2_scale || !chunk_expert || !chunk_row0 || !chunk_rows || !n_chunks ||
+      !chunk_ready || !a2_q || !a2_sT || !sorted_ids || !topk_weights || !out_pair || !err_word)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_experts: bad argument%s");
+  if (!aligned16(a1_q) || !aligned16(w13) || !aligned16(a1_sT) || !aligned16(a2_q) || !aligned16(w2) ||
+      !aligned16(a2_sT))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_experts: 16-byte alignment required%s");
+  GemmParams p1{}, p2{};
+  CUtensorMap tw1, ta1, tw2, ta2;
+  st = prep_gemm(a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, 2 * I, H, chunk_expert,
+                 chunk_row0, chunk_rows, n_chunks, tile_tokens, p1, tw1, ta1);
+  if (st) return st;
+  st = prep_gemm(a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I, chunk_expert, chunk_row0,
+                 chunk_rows, n_chunks, tile_tokens, p2, tw2, ta2);
+  if (st) return st;
+  p1.out_q = a2_q;
+  p1.out_q_ld = I;
+  p1.out_sT = a2_sT;
+  p1.out_s_ld = a_s_ld;
+  p1.chunk_ready = chunk_ready;
+  p1.err = err_word;
+  p2.sorted_ids = sorted_ids;
+  p2.topk_w = topk_weights;
+  p2.sentinel = (int32_t)(M * topk);
+  p2.out_pair = out_pair;
+  p2.err = err_word;
+  const int64_t units_cap = chunks_capacity * ((2 * I) / 256 + H / 256);
+  int64_t grid = grid_ctas > 0 ? grid_ctas : sm_count();
+  if (grid > units_cap) grid = units_cap;
+  return cuda_status(launch_grouped_gemm_fused(tile_tokens, tw1, ta1, p1, tw2, ta2, p2, (int)grid,
+                                               (cudaStream_t)stream),
+                     "experts");
+}
+
 int b200moe_combine_reduce(const float* out_pair, const int32_t* topk_ids, const int32_t* expert_map,
                            int num_experts, int64_t M, int topk, int64_t H, void* out, void* stream) {
   if (M < 0 || topk <= 0 || H <= 0 || H % 8 != 0 || num_experts <= 0 ||
@@ -428,6 +496,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   int32_t* ce = reinterpret_cast<int32_t*>(wl + pl.off_ce);
   int32_t* cr0 = reinterpret_cast<int32_t*>(wl + pl.off_cr0);
   int32_t* crows = reinterpret_cast<int32_t*>(wl + pl.off_crows);
+  int32_t* ready = reinterpret_cast<int32_t*>(wl + pl.off_ready);
   int32_t* counts = reinterpret_cast<int32_t*>(wl + pl.off_counts);  // [0] n_chunks, [1] num_rows
   uint8_t* a1 = wl + pl.off_a1;
   float* a1s = reinterpret_cast<float*>(wl + pl.off_a1s);
@@ -436,7 +505,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   float* pair = reinterpret_cast<float*>(wl + pl.off_pair);
 
   st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,
-                     crows, pl.chunks_cap, counts, counts + 1, err, stream);
+                     crows, pl.chunks_cap, counts, counts + 1, ready, err, stream);
   if (st) return st;
   if (in.hidden) {
     st = b200moe_gather_quant(in.hidden, M, H, topk, sorted, counts + 1, pl.rows_cap, a1, a1s, pl.as_ld, stream);
@@ -462,11 +531,9 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
     st = cuda_status(launch_quant_1x128(a, (cudaStream_t)stream), "gather rows");
   }
   if (st) return st;
-  st = b200moe_gemm1_silu(a1, a1s, pl.as_ld, pl.rows_cap, w13, w13_scale, E, H, I, ce, cr0, crows, counts,
-                          pl.chunks_cap, pl.tile_tokens, a2, a2s, err, 0, stream);
-  if (st) return st;
-  st = b200moe_gemm2_combine(a2, a2s, pl.as_ld, pl.rows_cap, w2, w2_scale, E, H, I, ce, cr0, crows, counts,
-                             pl.chunks_cap, pl.tile_tokens, sorted, topk_weights, M, topk, pair, err, 0, stream);
+  st = b200moe_experts(a1, a1s, pl.as_ld, pl.rows_cap, w13, w13_scale, w2, w2_scale, E, H, I, ce, cr0, crows, counts,
+                       pl.chunks_cap, ready, pl.tile_tokens, a2, a2s, sorted, topk_weights, M, topk, pair, err, 0,
+                       stream);
   if (st) return st;
   return b200moe_combine_reduce(pair, topk_ids, expert_map, num_experts, M, topk, H, out, stream);
 }

@@ -8,15 +8,48 @@ namespace b200moe {
 
 namespace {
 
+int sm_count_cached() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int cache[64] = {0};
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
 template <int T, int CS, int EPI>
-cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p, int grid,
+cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p,
+                       const CUtensorMap& tm_w2, const CUtensorMap& tm_a2, const GemmParams& p2, int grid,
                        cudaStream_t stream) {
   using C = GemmCfg<T, CS>;
   auto kernel = moe_grouped_gemm_kernel<T, CS, EPI>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (err != cudaSuccess) return err;
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_a, p);
-  return cudaGetLastError();
+  if (EPI != EPI_FUSED) {
+    kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_a, p, tm_w2, tm_a2, p2);
+    return cudaGetLastError();
+  }
+  // Stage-2 units wait for stage-1 units of other CTAs: the whole grid must
+  // be resident at once, which a cooperative launch guarantees (or refuses).
+  int per_sm = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, C::THREADS + 32, C::SMEM_BYTES);
+  if (err != cudaSuccess) return err;
+  const int resident = per_sm * sm_count_cached();
+  if (resident <= 0) return cudaErrorCooperativeLaunchTooLarge;
+  if (grid > resident) grid = resident;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(C::THREADS + 32, 1, 1);  // + the publisher warp
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeCooperative;
+  attr.val.cooperative = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, tm_w, tm_a, p, tm_w2, tm_a2, p2);
 }
 
 template <int EPI>
@@ -63,11 +96,11 @@ cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorM
   switch (tile_tokens) {
     case 16:
     case 32:
-      return launch_cfg<32, 1, EPI>(tm_w, tm_a, p, grid, stream);
+      return launch_cfg<32, 1, EPI>(tm_w, tm_a, p, tm_w, tm_a, p, grid, stream);
     case 64:
       // SiLU epilogue: one column slice (no register spills, measured faster);
       // combine epilogue: two slices (more warps hide its global stores).
-      return launch_cfg<64, EPI == EPI_SILU ? 1 : 2, EPI>(tm_w, tm_a, p, grid, stream);
+      return launch_cfg<64, EPI == EPI_SILU ? 1 : 2, EPI>(tm_w, tm_a, p, tm_w, tm_a, p, grid, stream);
     case 128:
       // Many tokens per expert: routed rows on the MMA M side.
       return launch_tok<EPI>(tm_w, tm_a, p, grid, stream);
@@ -93,6 +126,21 @@ int gemm_tile_rows(int tile_tokens) {
       return 128;  // per CTA for 256 (pairs)
     default:
       return 0;
+  }
+}
+
+cudaError_t launch_grouped_gemm_fused(int tile_tokens, const CUtensorMap& tm_w1, const CUtensorMap& tm_a1,
+                                      const GemmParams& p1, const CUtensorMap& tm_w2, const CUtensorMap& tm_a2,
+                                      const GemmParams& p2, int grid, cudaStream_t stream) {
+  if (grid <= 0) return cudaSuccess;
+  switch (tile_tokens) {
+    case 16:
+    case 32:
+      return launch_cfg<32, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
+    case 64:
+      return launch_cfg<64, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
+    default:
+      return cudaErrorInvalidValue;
   }
 }
 

@@ -28,6 +28,7 @@ struct AlignArgs {
   int32_t* chunk_rows;
   int64_t chunks_cap;
   int32_t* n_chunks;
+  int32_t* chunk_ready;    // nullable: zeroed over chunks_cap entries
   int32_t* err;
 };
 
@@ -83,6 +84,12 @@ cudaError_t launch_wait_timeout_selftest(int32_t* err, uint64_t timeout_ns, cuda
 
 struct GemmParams;
 // epi: 0 = SiLU + requant (stage 1), 1 = weighted combine (stage 2).
+// Both stages in one cooperative persistent launch (tiles of 16..64 tokens):
+// stage-2 units of a chunk start once its stage-1 units released
+// p1.chunk_ready (zeroed by the route kernel).
+cudaError_t launch_grouped_gemm_fused(int tile_tokens, const CUtensorMap& tm_w1, const CUtensorMap& tm_a1,
+                                      const GemmParams& p1, const CUtensorMap& tm_w2, const CUtensorMap& tm_a2,
+                                      const GemmParams& p2, int grid, cudaStream_t stream);
 cudaError_t launch_grouped_gemm(int epi, int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a,
                                 const GemmParams& p, int grid, cudaStream_t stream);
 // Activation tile rows the kernel for this tile_tokens loads per stage (per CTA).

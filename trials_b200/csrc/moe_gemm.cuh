@@ -58,7 +58,7 @@
 
 namespace b200moe {
 
-enum { EPI_SILU = 0, EPI_COMBINE = 1 };
+enum { EPI_SILU = 0, EPI_COMBINE = 1, EPI_FUSED = 2 };
 
 struct GemmParams {
   // routing: chunk list produced by the route kernel (device memory)
@@ -83,6 +83,8 @@ struct GemmParams {
   const float* topk_w;
   int32_t sentinel;   // M * topk
   float* out_pair;    // (M*topk, Nw) fp32
+  // EPI_FUSED: per-chunk count of finished stage-1 units (zeroed by routing)
+  int32_t* chunk_ready;
   // diagnostics
   int32_t* err;
   uint64_t timeout_ns;
@@ -157,12 +159,59 @@ __device__ __forceinline__ float warp_pair_transpose_max(const float* vals, int 
   return m[0];
 }
 
+// Acquire load of a counter another CTA releases.
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+// Waits until *counter >= target (bounded like every wait in this library);
+// then orders the following async-proxy (TMA) reads after the acquire.
+__device__ __forceinline__ bool wait_count_bounded(const int32_t* counter, int target, uint64_t limit_ns,
+                                                   volatile int* abort_flag) {
+  bool ok = ld_acquire_gpu(counter) >= target;
+  if (!ok) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!ok) {
+      __nanosleep(128);
+      ok = ld_acquire_gpu(counter) >= target;
+      if (!ok && (*abort_flag || globaltimer_ns() - t0 > limit_ns)) return false;
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
+// mbarrier wait that gives up after limit_ns or once the CTA's abort flag is set.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                                   volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (*abort_flag || globaltimer_ns() - t0 > limit_ns) return false;
+  return true;
+}
+
+// The kernel runs one stage (EPI_SILU / EPI_COMBINE: parameters p, tensor
+// maps tm_w / tm_a; the *2 copies are unused) or both (EPI_FUSED): units
+// [0, n1) are stage-1 units with p, units [n1, n1 + n2) stage-2 units with
+// p2, in one persistent grid. A stage-2 unit of chunk c reads the stage-1
+// output rows of c, so its producer first waits until all NT1 stage-1 units
+// of c have released p.chunk_ready[c]. Every CTA finishes issuing its stage-1
+// units before it waits on any chunk, and the grid is co-resident (one CTA
+// per SM, cooperative launch), so the waits always end. The count is released
+// by an extra "publisher" warp: the epilogue warps hand it each finished
+// stage-1 unit through an mbarrier, and its GPU-scope fence (which waits for
+// the stores to land) stays off the epilogue's path.
 template <int T, int CS, int EPI>
-__global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
+__global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 32 : 0), 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
-                            const GemmParams p) {
+                            const __grid_constant__ GemmParams p, const __grid_constant__ CUtensorMap tm_w2,
+                            const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ GemmParams p2) {
   using C = GemmCfg<T, CS>;
   constexpr int EW = C::EW;
+  constexpr bool FUSED = EPI == EPI_FUSED;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled TMA tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -178,11 +227,17 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
   uint64_t* sempty = sfull + C::NSLOT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + C::NSLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // The epilogue's stop decision for a unit, written by one thread before the
+  // unit's first named barrier so that every epilogue warp reads the same value.
+  volatile int* stop_sh = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  // EPI_FUSED hand-off of finished stage-1 units to the publisher warp:
+  // pub[0..1] filled by the epilogue warps, pub[2..3] released by the publisher.
+  uint64_t* pub = reinterpret_cast<uint64_t*>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int NKB = p.K >> 7;
-  const int NT = p.Nw / C::UNIT_ROWS;
+  const int NT1 = p.Nw / C::UNIT_ROWS, NKB1 = p.K >> 7;
+  const int NT2 = FUSED ? p2.Nw / C::UNIT_ROWS : 1, NKB2 = FUSED ? p2.K >> 7 : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
@@ -198,6 +253,12 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
       mbar_init(&sempty[s], EW);  // released by every epilogue warp
     }
     *abort_flag = 0;
+    if (FUSED) {
+      mbar_init(&pub[0], EW);
+      mbar_init(&pub[1], EW);
+      mbar_init(&pub[2], 1);
+      mbar_init(&pub[3], 1);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -207,38 +268,63 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_a);
+    if (FUSED) {
+      prefetch_tmap(&tm_w2);
+      prefetch_tmap(&tm_a2);
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int n_units = (*p.n_chunks) * NT;
+  const int n_chunks = *p.n_chunks;
+  const int n1 = n_chunks * NT1;
+  const int n_units = n1 + (FUSED ? n_chunks * NT2 : 0);
+  // unit -> (stage 2?, chunk, weight-row tile)
+  auto unit_of = [&](int u, bool& s2, int& chunk, int& nt) {
+    s2 = FUSED && u >= n1;
+    const int v = s2 ? u - n1 : u;
+    const int NT = s2 ? NT2 : NT1;
+    chunk = v / NT;
+    nt = v - chunk * NT;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
+      (void)pol_w;
       int stage = 0, slot = 0;
       uint32_t phase = 0, sphase = 0;
       long issued = 0;
       bool ok = true;
       // Chunk metadata is loaded one unit ahead, off the critical path.
       int e_n = 0, p0_n = 0;
-      if (blockIdx.x < n_units) {
-        e_n = __ldg(&p.chunk_expert[blockIdx.x / NT]);
-        p0_n = __ldg(&p.chunk_row0[blockIdx.x / NT]);
-      }
+      auto meta = [&](int u) {
+        bool s2;
+        int c, nt;
+        unit_of(u, s2, c, nt);
+        e_n = __ldg(&p.chunk_expert[c]);
+        p0_n = __ldg(&p.chunk_row0[c]);
+      };
+      if (blockIdx.x < n_units) meta(blockIdx.x);
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const int chunk = u / NT;
-        const int nt = u - chunk * NT;
+        bool s2;
+        int chunk, nt;
+        unit_of(u, s2, chunk, nt);
         const int e = e_n, p0 = p0_n;
-        if (u + (int)gridDim.x < n_units) {
-          e_n = __ldg(&p.chunk_expert[(u + gridDim.x) / NT]);
-          p0_n = __ldg(&p.chunk_row0[(u + gridDim.x) / NT]);
+        if (u + (int)gridDim.x < n_units) meta(u + gridDim.x);
+        const GemmParams& q = s2 ? p2 : p;
+        const CUtensorMap* tw = s2 ? &tm_w2 : &tm_w;
+        const CUtensorMap* ta = s2 ? &tm_a2 : &tm_a;
+        const int NKB = s2 ? NKB2 : NKB1;
+        const int wrow = e * q.Nw + nt * C::UNIT_ROWS;
+        if (FUSED && s2 && !wait_count_bounded(p.chunk_ready + chunk, NT1, p.timeout_ns, abort_flag)) {
+          ok = false;
+          break;
         }
-        const int wrow = e * p.Nw + nt * C::UNIT_ROWS;
         for (int kb = 0; kb < NKB; ++kb) {
           if (*abort_flag || !mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns) ||
               !mbar_wait_bounded(&sempty[slot], sphase ^ 1, p.timeout_ns)) {
@@ -248,13 +334,13 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
           uint8_t* tile = tiles + stage * C::TILE_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::TILE_BYTES);
 #if B200MOE_W_EVICT_FIRST
-          tma_load_2d(tile, &tm_w, &full[stage], kb * 128, wrow, pol_w);
+          tma_load_2d(tile, tw, &full[stage], kb * 128, wrow, pol_w);
 #else
-          tma_load_2d(tile, &tm_w, &full[stage], kb * 128, wrow);
+          tma_load_2d(tile, tw, &full[stage], kb * 128, wrow);
 #endif
-          tma_load_2d(tile + C::W_BYTES, &tm_a, &full[stage], kb * 128, p0, pol_a);
+          tma_load_2d(tile + C::W_BYTES, ta, &full[stage], kb * 128, p0, pol_a);
           mbar_arrive_expect_tx(&sfull[slot], C::S_BYTES);
-          bulk_load(sscale + slot * T, p.a_sT + (int64_t)kb * p.as_ld + p0, C::S_BYTES, &sfull[slot]);
+          bulk_load(sscale + slot * T, q.a_sT + (int64_t)kb * q.as_ld + p0, C::S_BYTES, &sfull[slot]);
           ++issued;
           if (++stage == C::NSTAGE) {
             stage = 0;
@@ -287,10 +373,17 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
       int last_buf = 0;
       uint32_t last_bphase = 0;
       bool ok = true;
-      int rows_n = blockIdx.x < n_units ? __ldg(&p.chunk_rows[blockIdx.x / NT]) : 0;
+      auto rows_of = [&](int u) {
+        bool s2;
+        int c, nt;
+        unit_of(u, s2, c, nt);
+        return __ldg(&p.chunk_rows[c]);
+      };
+      int rows_n = blockIdx.x < n_units ? rows_of(blockIdx.x) : 0;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const int rows = rows_n;
-        if (u + (int)gridDim.x < n_units) rows_n = __ldg(&p.chunk_rows[(u + gridDim.x) / NT]);
+        if (u + (int)gridDim.x < n_units) rows_n = rows_of(u + gridDim.x);
+        const int NKB = (FUSED && u >= n1) ? NKB2 : NKB1;
         const uint32_t idesc = idesc_e4m3_f32(128, rows);
         for (int kb = 0; kb < NKB; ++kb) {
           if (*abort_flag || !mbar_wait_bounded(&tempty[buf], bphase ^ 1, p.timeout_ns)) {
@@ -336,7 +429,7 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
       // The tensor core must be done with TMEM before it is released.
       if (committed > 0) mbar_wait_bounded(&tfull[last_buf], last_bphase, p.timeout_ns);
     }
-  } else {
+  } else if (warp < 2 + EW) {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;                 // 0..EW-1
     const int q = warp & 3;                  // TMEM lane quarter
@@ -350,27 +443,41 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
     // scales (one per K block of this 128-row half) are spread over the lanes
     // (K blocks lane and lane + 32) and loaded before the previous unit's
     // final epilogue, so no global load sits on the per-K-block path.
-    auto ws_row = [&](int e, int nt) { return p.w_scale + ((int64_t)e * (p.Nw >> 7) + nt * 2 + hs) * NKB; };
+    auto ws_row = [&](bool s2, int e, int nt) {
+      const GemmParams& g = s2 ? p2 : p;
+      return g.w_scale + ((int64_t)e * (g.Nw >> 7) + nt * 2 + hs) * (g.K >> 7);
+    };
     int e_n = 0, p0_n = 0, rows_n = 0;
     float wl0 = 0.f, wl1 = 0.f;
+    auto load_ws = [&](bool s2, int e, int nt) {
+      const float* w = ws_row(s2, e, nt);
+      const int nkb = s2 ? NKB2 : NKB1;
+      wl0 = lane < nkb ? __ldg(w + lane) : 0.f;
+      wl1 = lane + 32 < nkb ? __ldg(w + lane + 32) : 0.f;
+    };
+    int n_pub = 0;  // stage-1 units handed to the publisher (EPI_FUSED)
     if (blockIdx.x < n_units) {
-      const int c = blockIdx.x / NT;
+      bool s2;
+      int c, nt;
+      unit_of(blockIdx.x, s2, c, nt);
       e_n = __ldg(&p.chunk_expert[c]);
       p0_n = __ldg(&p.chunk_row0[c]);
       rows_n = __ldg(&p.chunk_rows[c]);
-      const float* w = ws_row(e_n, blockIdx.x - c * NT);
-      wl0 = lane < NKB ? __ldg(w + lane) : 0.f;
-      wl1 = lane + 32 < NKB ? __ldg(w + lane + 32) : 0.f;
+      load_ws(s2, e_n, nt);
     }
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-      const int chunk = u / NT;
-      const int nt = u - chunk * NT;
+      bool s2;
+      int chunk, nt;
+      unit_of(u, s2, chunk, nt);
+      const int NKB = s2 ? NKB2 : NKB1;
       const int e = e_n, p0 = p0_n, rows = rows_n;
       const float ws0 = wl0, ws1 = wl1;
-      const float* wsp = ws_row(e, nt);
+      const float* wsp = ws_row(s2, e, nt);
       const int un = u + gridDim.x;
-      const int cn = un / NT;
+      bool s2n = false;
+      int cn = 0, ntn = 0;
       if (un < n_units) {
+        unit_of(un, s2n, cn, ntn);
         e_n = __ldg(&p.chunk_expert[cn]);
         p0_n = __ldg(&p.chunk_row0[cn]);
         rows_n = __ldg(&p.chunk_rows[cn]);
@@ -457,13 +564,9 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
         atomicOr(p.err, ERR_DEV_TIMEOUT);
         *abort_flag = 1;
       }
-      if (un < n_units) {
-        const float* w = ws_row(e_n, un - cn * NT);
-        wl0 = lane < NKB ? __ldg(w + lane) : 0.f;
-        wl1 = lane + 32 < NKB ? __ldg(w + lane + 32) : 0.f;
-      }
+      if (un < n_units) load_ws(s2n, e_n, ntn);
 
-      if constexpr (EPI == EPI_SILU) {
+      if (EPI == EPI_SILU || (FUSED && !s2)) {
         // Lane pair (2k, 2k+1) holds weight rows 2k (gate) and 2k+1 (up) of
         // this half for every token column. The even lane produces inter for
         // the even token columns and the odd lane for the odd ones; inter
@@ -491,9 +594,12 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
 #pragma unroll
         for (int g = 0; g < NG; ++g)
           if (g < live) red[(hs * 4 + q) * T + col0 + g * 32 + lane] = warp_pair_transpose_max(v + g * 16, lane);
+        const int tid = threadIdx.x - 64;
+        if (tid == 0) *stop_sh = *abort_flag;
         named_bar_sync(1, EW * 32);
-        const bool stop = *abort_flag != 0;
-        if (stop) break;
+        // The previous read of stop_sh happened before this unit's second
+        // barrier, the write above after it: one slot suffices.
+        if (*stop_sh) break;
         float colscale[NG];
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
@@ -515,14 +621,25 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
         }
         named_bar_sync(1, EW * 32);
         // Coalesced copy of the quantised rows: 8 x 16 B per row.
-        const int tid = threadIdx.x - 64;
         for (int idx = tid; idx < rows * 8; idx += EW * 32) {
           const int c = idx >> 3, part = idx & 7;
           const uint4 val = *reinterpret_cast<const uint4*>(staging + c * 128 + part * 16);
           *reinterpret_cast<uint4*>(p.out_q + (int64_t)(p0 + c) * p.out_q_ld + nt * 128 + part * 16) = val;
         }
+        if (FUSED) {
+          // The warp's stores are ordered before lane 0's arrive (release) by
+          // __syncwarp; the publisher's acquire and GPU-scope fence follow.
+          const int sl = n_pub & 1;
+          bool free_slot = true;
+          if (n_pub >= 2 && lane == 0)
+            free_slot = mbar_wait_or_abort(&pub[2 + sl], ((n_pub >> 1) & 1) ^ 1, p.timeout_ns, abort_flag);
+          __syncwarp();
+          if (lane == 0 && free_slot) mbar_arrive(&pub[sl]);
+          ++n_pub;
+        }
       } else {
         if (!ok) break;
+        const GemmParams& pc = FUSED ? p2 : p;
         // Lane l fetches the slot id and router weight of column l of each
         // 32-column group once; the stores below broadcast them by shuffle.
         constexpr int NG = C::TC / 32;
@@ -531,18 +648,36 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS, 1)
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
           const int c = col0 + g * 32 + lane;
-          fl[g] = c < rows ? __ldg(&p.sorted_ids[p0 + c]) : p.sentinel;
-          wl[g] = fl[g] < p.sentinel ? __ldg(&p.topk_w[fl[g]]) : 0.f;
+          fl[g] = c < rows ? __ldg(&pc.sorted_ids[p0 + c]) : pc.sentinel;
+          wl[g] = fl[g] < pc.sentinel ? __ldg(&pc.topk_w[fl[g]]) : 0.f;
         }
-        float* dst = p.out_pair + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane;
+        float* dst = pc.out_pair + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane;
 #pragma unroll
         for (int j = 0; j < C::TC; ++j) {
           if (col0 + (j & ~31) < rows) {  // warp-uniform
             const int f = __shfl_sync(0xffffffffu, fl[j / 32], j % 32);
             const float w = __shfl_sync(0xffffffffu, wl[j / 32], j % 32);
-            if (f < p.sentinel) dst[(int64_t)f * p.Nw] = w * acc[j];
+            if (f < pc.sentinel) dst[(int64_t)f * pc.Nw] = w * acc[j];
           }
         }
+      }
+    }
+  } else if (FUSED) {
+    // ------------------------------------------------------------ publisher
+    if (lane == 0) {
+      int k = 0;
+      for (int u = blockIdx.x; u < n1; u += gridDim.x, ++k) {
+        const int sl = k & 1;
+        if (!mbar_wait_or_abort(&pub[sl], (k >> 1) & 1, p.timeout_ns, abort_flag)) {
+          if (!*abort_flag) {
+            atomicOr(p.err, ERR_DEV_TIMEOUT);
+            *abort_flag = 1;
+          }
+          break;
+        }
+        __threadfence();
+        atomicAdd(p.chunk_ready + u / NT1, 1);
+        mbar_arrive(&pub[2 + sl]);
       }
     }
   }

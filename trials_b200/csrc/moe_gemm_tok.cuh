@@ -83,6 +83,9 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
   uint64_t* sempty = sfull + C::NSLOT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + C::NSLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // The epilogue's stop decision for a unit, written by one thread before the
+  // unit's first named barrier so that every epilogue warp reads the same value.
+  volatile int* stop_sh = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -315,10 +318,11 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
         }
         float* rb = red + parity * 2 * C::TM;
         rb[h * C::TM + r] = m;
+        if (threadIdx.x == 64) *stop_sh = *abort_flag;
         named_bar_sync(1, EW * 32);
-        // Every warp reads the abort flag between the two barriers; a warp can
-        // only set it in a later wait, after the second one.
-        const bool stop = *abort_flag != 0;
+        // All epilogue warps read the value one thread stored before the
+        // barrier; the store for the next unit comes after the second barrier.
+        const bool stop = *stop_sh != 0;
         const float scale = group_scale(fmaxf(rb[r], rb[C::TM + r]));
         named_bar_sync(1, EW * 32);
         if (stop) break;

@@ -1,5 +1,6 @@
 """Stage-level calls of the layer (route -> gather/quantise -> GEMM1+SiLU ->
-GEMM2+combine -> top-k reduce) on explicit torch buffers.
+GEMM2+combine -> top-k reduce, or the two GEMM stages as one launch) on
+explicit torch buffers.
 
 These mirror the reference's kernel launchers (moe_decode_megakernel_stage1,
 ..._stage1_fused with fused_silu, ..._stage2_fused:
@@ -29,6 +30,7 @@ class Routing:
     chunk_rows: torch.Tensor
     counts: torch.Tensor        # [n_chunks, num_rows] int32
     err: torch.Tensor           # (1,) int32
+    chunk_ready: torch.Tensor   # (chunks_cap,) int32, zeroed by route for experts()
 
     @property
     def n_chunks(self):
@@ -54,13 +56,13 @@ def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map
     z = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=dev)  # noqa: E731
     r = Routing(tile_tokens, rows_cap, chunks_cap, z(rows_cap), z(chunks_cap), z(chunks_cap), z(chunks_cap),
                 torch.zeros(2, dtype=torch.int32, device=dev),
-                err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev))
+                err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev), z(chunks_cap))
     if expert_map is not None:
         expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
     _lib.check(L.b200moe_route(_ptr(ids), M, topk, num_experts, _ptr(expert_map), E, tile_tokens,
                                _ptr(r.sorted_ids), rows_cap, _ptr(r.chunk_expert), _ptr(r.chunk_row0),
-                               _ptr(r.chunk_rows), chunks_cap, _ptr(r.n_chunks), _ptr(r.num_rows), _ptr(r.err),
-                               _stream(dev)), "route")
+                               _ptr(r.chunk_rows), chunks_cap, _ptr(r.n_chunks), _ptr(r.num_rows),
+                               _ptr(r.chunk_ready), _ptr(r.err), _stream(dev)), "route")
     return r
 
 
@@ -109,6 +111,29 @@ def gemm2_combine(a2_q, a2_sT, w2, w2_scale, r: Routing, topk_weights: torch.Ten
     return out_pair
 
 
+def experts(a1_q, a1_sT, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights: torch.Tensor,
+            grid_ctas: int = 0, out_pair: Optional[torch.Tensor] = None):
+    """Both GEMM stages in one launch -> (a2_q, a2_sT, out_pair), the same
+    values as gemm1_silu followed by gemm2_combine. Needs the chunk_ready
+    counters as zeroed by route() for this routing."""
+    dev = _require_cuda(a1_q, w13, w2)
+    E, N2, H = w13.shape
+    I = N2 // 2
+    M, topk = topk_weights.shape
+    ld = r.a_s_ld()
+    a2_q = torch.zeros(r.rows_cap, I, dtype=FP8, device=dev)
+    a2_sT = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
+    tw = topk_weights.to(torch.float32).contiguous()
+    if out_pair is None:
+        out_pair = torch.zeros(M * topk, H, dtype=torch.float32, device=dev)
+    _lib.check(_lib.lib().b200moe_experts(
+        _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13), _ptr(w13_scale.contiguous()), _ptr(w2),
+        _ptr(w2_scale.contiguous()), E, H, I, _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows),
+        _ptr(r.n_chunks), r.chunks_cap, _ptr(r.chunk_ready), r.tile_tokens, _ptr(a2_q), _ptr(a2_sT),
+        _ptr(r.sorted_ids), _ptr(tw), M, topk, _ptr(out_pair), _ptr(r.err), grid_ctas, _stream(dev)), "experts")
+    return a2_q, a2_sT, out_pair
+
+
 def combine_reduce(out_pair: torch.Tensor, topk_ids: torch.Tensor, num_experts: int,
                    expert_map: Optional[torch.Tensor] = None) -> torch.Tensor:
     dev = _require_cuda(out_pair, topk_ids)
@@ -139,14 +164,18 @@ def pick_tile_tokens(numel: int, num_local_experts: int) -> int:
 
 
 class LayerPipeline:
-    """The five launches of the layer on preallocated buffers, with optional
-    CUDA events between stages (used by the benchmark to time each kernel on
-    the launching stream). Same kernels and order as b200moe_layer."""
+    """The launches of the layer on preallocated buffers, with optional CUDA
+    events between stages (used by the benchmark to time each kernel on the
+    launching stream). Same kernels and order as b200moe_layer: route,
+    gather_quant, experts (both GEMM stages in one launch), combine_reduce;
+    with split=True the GEMM stages run as two launches instead."""
 
-    STAGES = ("route", "gather_quant", "gemm1_silu", "gemm2_combine", "combine_reduce")
+    FUSED_STAGES = ("route", "gather_quant", "experts", "combine_reduce")
+    SPLIT_STAGES = ("route", "gather_quant", "gemm1_silu", "gemm2_combine", "combine_reduce")
 
     def __init__(self, M: int, H: int, I: int, num_experts: int, topk: int, device, tile_tokens: int = 0,
-                 expert_map: Optional[torch.Tensor] = None, num_local_experts: Optional[int] = None):
+                 expert_map: Optional[torch.Tensor] = None, num_local_experts: Optional[int] = None,
+                 split: bool = False):
         self.M, self.H, self.I, self.topk = M, H, I, topk
         self.num_experts = num_experts
         self.E = num_local_experts if expert_map is not None else num_experts
@@ -161,6 +190,9 @@ class LayerPipeline:
         z = lambda n: torch.zeros(max(n, 1), dtype=torch.int32, device=device)  # noqa: E731
         self.sorted_ids, self.ce, self.cr0, self.crows = z(self.rows_cap), z(self.chunks_cap), z(self.chunks_cap), \
             z(self.chunks_cap)
+        self.ready = z(self.chunks_cap)
+        self.split = split
+        self.stages = self.SPLIT_STAGES if split else self.FUSED_STAGES
         self.counts = z(2)
         self.err = z(1)
         self.a1 = torch.zeros(self.rows_cap, H, dtype=FP8, device=device)
@@ -173,7 +205,7 @@ class LayerPipeline:
     def run(self, hidden, topk_ids, topk_weights, w13, w13_scale, w2, w2_scale, events=None, grid_ctas: int = 0):
         L = _lib.lib()
         st = _stream(self.device)
-        ev = events or [None] * 6
+        ev = events or [None] * (len(self.stages) + 1)
         rec = lambda i: ev[i].record() if ev[i] is not None else None  # noqa: E731
         M, H, I, topk, E = self.M, self.H, self.I, self.topk, self.E
         cnt = _ptr(self.counts)
@@ -181,11 +213,24 @@ class LayerPipeline:
         rec(0)
         _lib.check(L.b200moe_route(_ptr(topk_ids), M, topk, self.num_experts, _ptr(self.expert_map), E, self.tile,
                                    _ptr(self.sorted_ids), self.rows_cap, _ptr(self.ce), _ptr(self.cr0),
-                                   _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.err), st), "route")
+                                   _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.ready), _ptr(self.err),
+                                   st), "route")
         rec(1)
         _lib.check(L.b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(self.sorted_ids), rows, self.rows_cap,
                                           _ptr(self.a1), _ptr(self.a1s), self.ld, st), "gather_quant")
         rec(2)
+        if not self.split:
+            _lib.check(L.b200moe_experts(_ptr(self.a1), _ptr(self.a1s), self.ld, self.rows_cap, _ptr(w13),
+                                         _ptr(w13_scale), _ptr(w2), _ptr(w2_scale), E, H, I, _ptr(self.ce),
+                                         _ptr(self.cr0), _ptr(self.crows), cnt, self.chunks_cap, _ptr(self.ready),
+                                         self.tile, _ptr(self.a2), _ptr(self.a2s), _ptr(self.sorted_ids),
+                                         _ptr(topk_weights), M, topk, _ptr(self.pair), _ptr(self.err), grid_ctas,
+                                         st), "experts")
+            rec(3)
+            _lib.check(L.b200moe_combine_reduce(_ptr(self.pair), _ptr(topk_ids), _ptr(self.expert_map),
+                                                self.num_experts, M, topk, H, _ptr(self.out), st), "combine_reduce")
+            rec(4)
+            return self.out
         _lib.check(L.b200moe_gemm1_silu(_ptr(self.a1), _ptr(self.a1s), self.ld, self.rows_cap, _ptr(w13),
                                         _ptr(w13_scale), E, H, I, _ptr(self.ce), _ptr(self.cr0), _ptr(self.crows),
                                         cnt, self.chunks_cap, self.tile, _ptr(self.a2), _ptr(self.a2s),
