@@ -148,12 +148,11 @@ def test_gather_and_gemm_stages(cuda_device, shape, tile):
     n_rows = int(r.counts[1].item())
     sorted_ids = r.sorted_ids[:n_rows].cpu().numpy()
     valid = sorted_ids < shape.M * topk
-    # gather + quantise: bit-exact rows, zero padding rows
+    # gather + quantise: bit-exact routed rows (padding rows are not written)
     hq, hs = orc.per_token_group_quant_fp8(L.hidden)
     tok = torch.as_tensor(sorted_ids[valid] // topk, dtype=torch.long)
     assert torch.equal(_u8(a1_q[:n_rows][torch.as_tensor(valid)]), _u8(hq[tok]))
     assert torch.equal(a1_sT[:, :n_rows].T.cpu()[torch.as_tensor(valid)], hs[tok])
-    assert int(_u8(a1_q[:n_rows][torch.as_tensor(~valid)]).abs().sum()) == 0
 
     # stage 1 vs oracle (fp32 gate/up -> SiLU*up -> 1x128 requant)
     a2_q, a2_sT = stages.gemm1_silu(a1_q, a1_sT, g["w13"], g["w13_scale"], r)
@@ -187,6 +186,23 @@ def test_gather_and_gemm_stages(cuda_device, shape, tile):
     assert int(r.err.item()) == 0
 
 
+@pytest.mark.parametrize("M,tile", [(16, 32), (300, 64), (600, 128)])
+def test_gather_rows_equals_gather_quant(cuda_device, M, tile):
+    """Quantise each token once + copy rows (the large-batch path) gives the
+    same routed rows and scales as quantising every routed copy."""
+    shape = synth.LayerShape(M=M, H=512, I=256, E=16, topk=4, scoring="sigmoid")
+    L, g = _tiny_layer(cuda_device, shape, seed=3)
+    r = stages.route(g["topk_ids"], shape.E, tile)
+    a_q, a_sT = stages.gather_quant(g["hidden"], shape.topk, r)
+    tq, ts = moe.per_token_group_quant_fp8(g["hidden"])
+    b_q, b_sT = stages.gather_rows(tq, ts, shape.topk, r)
+    torch.cuda.synchronize()
+    n_rows = int(r.counts[1].item())
+    valid = torch.as_tensor(r.sorted_ids[:n_rows].cpu().numpy() < M * shape.topk)
+    assert torch.equal(_u8(a_q[:n_rows][valid]), _u8(b_q[:n_rows][valid]))
+    assert torch.equal(a_sT[:, :n_rows].T.cpu()[valid], b_sT[:, :n_rows].T.cpu()[valid])
+
+
 @pytest.mark.parametrize("grid,tile", [(1, 32), (5, 32), (37, 32), (1, 128), (7, 128), (3, 64), (2, 256),
                                        (6, 256)])
 def test_schedule_invariance_bit_exact(cuda_device, grid, tile):
@@ -197,7 +213,8 @@ def test_schedule_invariance_bit_exact(cuda_device, grid, tile):
     a1_q, a1_sT = stages.gather_quant(g["hidden"], SMALL.topk, r)
     ref_q, ref_s = stages.gemm1_silu(a1_q, a1_sT, g["w13"], g["w13_scale"], r, grid_ctas=0)
     q, s = stages.gemm1_silu(a1_q, a1_sT, g["w13"], g["w13_scale"], r, grid_ctas=grid)
-    assert torch.equal(_u8(q), _u8(ref_q)) and torch.equal(s, ref_s)
+    # bit patterns (rows of padding tokens may hold NaN from unwritten inputs)
+    assert torch.equal(_u8(q), _u8(ref_q)) and torch.equal(s.view(torch.int32), ref_s.view(torch.int32))
     p0 = stages.gemm2_combine(ref_q, ref_s, g["w2"], g["w2_scale"], r, g["topk_weights"], grid_ctas=0)
     p1 = stages.gemm2_combine(ref_q, ref_s, g["w2"], g["w2_scale"], r, g["topk_weights"], grid_ctas=grid)
     assert torch.equal(p0, p1)
@@ -217,7 +234,8 @@ def test_fused_experts_bit_identical_to_split(cuda_device, shape, tile, grid):
     q2, s2, p2 = stages.experts(a1_q, a1_sT, g["w13"], g["w13_scale"], g["w2"], g["w2_scale"], r,
                                 g["topk_weights"], grid_ctas=grid)
     torch.cuda.synchronize()
-    assert torch.equal(_u8(q1), _u8(q2)) and torch.equal(s1, s2) and torch.equal(p1, p2)
+    assert torch.equal(_u8(q1), _u8(q2)) and torch.equal(s1.view(torch.int32), s2.view(torch.int32))
+    assert torch.equal(p1, p2)
     assert int(r.err.item()) == 0
     if tile <= 64:
         nc = int(r.counts[0].item())

@@ -91,11 +91,28 @@ int pick_tile_tokens(int64_t numel, int E_local) {
 
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
 
+// Chunks per unit group (unit_coords): token-major tiles have several chunks
+// per expert at prefill, whose CTAs then share weight tiles through L2.
+#ifndef B200MOE_CHUNK_GROUP_TOK
+#define B200MOE_CHUNK_GROUP_TOK 4
+#endif
+#ifndef B200MOE_CHUNK_GROUP_SWAP
+#define B200MOE_CHUNK_GROUP_SWAP 1
+#endif
+
+// From this many routed (token, slot) pairs on, the layer quantises each token
+// once and copies its fp8 row into the routed positions (two launches),
+// instead of quantising every routed copy (one launch): topk-fold less
+// conversion work, which outweighs the extra launch at prefill sizes.
+constexpr int64_t kTokenQuantMinPairs = 2048;
+bool token_quant_first(int64_t numel) { return numel >= kTokenQuantMinPairs; }
+
 struct LayerPlan {
   int tile_tokens;
   int64_t rows_cap, chunks_cap, as_ld;
   size_t off_sorted, off_ce, off_cr0, off_crows, off_ready, off_counts, off_a1, off_a1s, off_a2, off_a2s, off_pair,
-      total;
+      off_tq, off_ts, total;
+  bool token_quant;  // quantise each token once, then copy rows (large batches)
 };
 
 LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
@@ -122,6 +139,11 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
   p.off_a2 = take((size_t)p.rows_cap * I);
   p.off_a2s = take(sizeof(float) * (size_t)(I / 128) * p.as_ld);
   p.off_pair = take(sizeof(float) * (size_t)numel * H);
+  p.token_quant = token_quant_first(numel);
+  if (p.token_quant) {
+    p.off_tq = take((size_t)M * H);
+    p.off_ts = take(sizeof(float) * (size_t)M * (H / 128));
+  }
   p.total = off;
   return p;
 }
@@ -152,6 +174,7 @@ int prep_gemm(const uint8_t* a_q, const float* a_sT, int64_t as_ld, int64_t rows
   p.K = (int)K;
   p.Nw = (int)Nw;
   p.timeout_ns = kTimeoutNs;
+  p.chunk_group = tile_tokens > 64 ? B200MOE_CHUNK_GROUP_TOK : B200MOE_CHUNK_GROUP_SWAP;
   return B200MOE_OK;
 }
 
@@ -335,6 +358,33 @@ int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, con
   return cuda_status(launch_quant_1x128(a, (cudaStream_t)stream), "gather_quant");
 }
 
+int b200moe_gather_rows(const uint8_t* xq, const float* xs, int64_t ldxq, int64_t ldxs, int64_t M, int64_t H, int topk,
+                        const int32_t* sorted_ids, const int32_t* num_rows, int64_t rows_capacity, uint8_t* a_q,
+                        float* a_sT, int64_t a_s_ld, void* stream) {
+  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || rows_capacity < 0 || a_s_ld < rows_capacity ||
+      ldxq < H || ldxs < H / 128 || (rows_capacity > 0 && (!xq || !xs || !sorted_ids || !num_rows || !a_q || !a_sT)))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_gather_rows: bad argument%s");
+  if (!aligned16(xq) || ldxq % 16 != 0 || !aligned16(a_q) || H % 16 != 0)
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_gather_rows: fp8 rows must be 16-byte aligned%s");
+  QuantArgs a{};
+  a.xq = xq;
+  a.ldxq = ldxq;
+  a.xs = xs;
+  a.ldxs = ldxs;
+  a.K = H;
+  a.rows = rows_capacity;
+  a.num_rows = num_rows;
+  a.sorted_ids = sorted_ids;
+  a.topk = topk;
+  a.sentinel = (int32_t)(M * topk);
+  a.q = a_q;
+  a.ldq = H;
+  a.s = a_sT;
+  a.s_row = 1;
+  a.s_grp = a_s_ld;
+  return cuda_status(launch_quant_1x128(a, (cudaStream_t)stream), "gather_rows");
+}
+
 int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
                        const uint8_t* w13, const float* w13_scale, int num_local_experts, int64_t H, int64_t I,
                        const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
@@ -507,16 +557,24 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,
                      crows, pl.chunks_cap, counts, counts + 1, ready, err, stream);
   if (st) return st;
-  if (in.hidden) {
+  LayerInput src = in;
+  if (in.hidden && pl.token_quant) {
+    uint8_t* tq = wl + pl.off_tq;
+    float* ts = reinterpret_cast<float*>(wl + pl.off_ts);
+    st = b200moe_quant_1x128(in.hidden, M, H, H, tq, H, ts, H / 128, 1, stream);
+    if (st) return st;
+    src = LayerInput{nullptr, tq, H, ts, H / 128};
+  }
+  if (src.hidden) {
     st = b200moe_gather_quant(in.hidden, M, H, topk, sorted, counts + 1, pl.rows_cap, a1, a1s, pl.as_ld, stream);
   } else {
-    if (!aligned16(in.q) || in.ldq % 16 != 0 || in.ldq < H || in.lds < H / 128 || !in.s)
+    if (!aligned16(src.q) || src.ldq % 16 != 0 || src.ldq < H || src.lds < H / 128 || !src.s)
       return fail(B200MOE_ERR_UNSUPPORTED, "%s: fp8 rows must be 16-byte aligned with scales per row", name);
     QuantArgs a{};
-    a.xq = in.q;
-    a.ldxq = in.ldq;
-    a.xs = in.s;
-    a.ldxs = in.lds;
+    a.xq = src.q;
+    a.ldxq = src.ldq;
+    a.xs = src.s;
+    a.ldxs = src.lds;
     a.K = H;
     a.rows = pl.rows_cap;
     a.num_rows = counts + 1;

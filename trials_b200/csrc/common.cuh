@@ -27,4 +27,21 @@ __device__ __forceinline__ uint8_t quant_e4m3(float x, float scale) {
 // Group scale: max(amax / 448, 1e-12) in fp32 (phase5_orchestrator.py:29-30).
 __device__ __forceinline__ float group_scale(float amax) { return fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f); }
 
+// Work-unit order of the grouped GEMMs. A unit is (chunk, weight tile nt).
+// Chunks are taken in groups of `group` consecutive chunks, and inside a group
+// weight-tile-major: (c0, 0), (c1, 0), ..., (c0, 1), (c1, 1), ... CTAs running
+// at the same time then share the weight tile of an expert that has several
+// chunks (one HBM read, the rest from L2) and reuse the group's activation rows
+// from L2. group = 1 is plain chunk-major order. A bijection of
+// [0, n_chunks * NT) for every group >= 1.
+__device__ __forceinline__ void unit_coords(int u, int n_chunks, int NT, int group, int& chunk, int& nt) {
+  const int span = group * NT;
+  const int g = u / span;
+  const int r = u - g * span;
+  const int first = g * group;
+  const int gc = n_chunks - first < group ? n_chunks - first : group;
+  nt = r / gc;
+  chunk = first + (r - nt * gc);
+}
+
 }  // namespace b200moe

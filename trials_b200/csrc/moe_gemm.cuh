@@ -85,6 +85,8 @@ struct GemmParams {
   float* out_pair;    // (M*topk, Nw) fp32
   // EPI_FUSED: per-chunk count of finished stage-1 units (zeroed by routing)
   int32_t* chunk_ready;
+  // unit order: chunks per group (see unit_coords); 1 = chunk-major
+  int chunk_group;
   // diagnostics
   int32_t* err;
   uint64_t timeout_ns;
@@ -284,10 +286,7 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
   // unit -> (stage 2?, chunk, weight-row tile)
   auto unit_of = [&](int u, bool& s2, int& chunk, int& nt) {
     s2 = FUSED && u >= n1;
-    const int v = s2 ? u - n1 : u;
-    const int NT = s2 ? NT2 : NT1;
-    chunk = v / NT;
-    nt = v - chunk * NT;
+    unit_coords(s2 ? u - n1 : u, n_chunks, s2 ? NT2 : NT1, p.chunk_group, chunk, nt);
   };
 
   if (warp == 0) {
@@ -675,8 +674,11 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
           }
           break;
         }
+        bool s2;
+        int chunk, nt;
+        unit_of(u, s2, chunk, nt);
         __threadfence();
-        atomicAdd(p.chunk_ready + u / NT1, 1);
+        atomicAdd(p.chunk_ready + chunk, 1);
         mbar_arrive(&pub[2 + sl]);
       }
     }

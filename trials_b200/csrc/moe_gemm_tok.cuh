@@ -120,7 +120,8 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int n_units = (*p.n_chunks) * NT;
+  const int n_chunks = *p.n_chunks;
+  const int n_units = n_chunks * NT;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -132,8 +133,8 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
       long issued = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const int chunk = u / NT;
-        const int nt = u - chunk * NT;
+        int chunk, nt;
+        unit_coords(u, n_chunks, NT, p.chunk_group, chunk, nt);
         const int e = __ldg(&p.chunk_expert[chunk]);
         const int p0 = __ldg(&p.chunk_row0[chunk]);
         const int wrow = e * p.Nw + nt * C::UNIT_ROWS;
@@ -233,8 +234,8 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
     bool ok = true;
     int parity = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, parity ^= 1) {
-      const int chunk = u / NT;
-      const int nt = u - chunk * NT;
+      int chunk, nt;
+      unit_coords(u, n_chunks, NT, p.chunk_group, chunk, nt);
       const int e = __ldg(&p.chunk_expert[chunk]);
       const int p0 = __ldg(&p.chunk_row0[chunk]);
       const int rows = __ldg(&p.chunk_rows[chunk]);

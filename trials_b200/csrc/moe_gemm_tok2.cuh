@@ -104,7 +104,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tok2Cfg::THREADS, 1)
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int n_units = (*p.n_chunks) * NT;
+  const int n_chunks = *p.n_chunks;
+  const int n_units = n_chunks * NT;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producers (both CTAs)
@@ -118,8 +119,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tok2Cfg::THREADS, 1)
       long issued = 0;
       bool ok = true;
       for (int u = pair; u < n_units && ok; u += n_pairs) {
-        const int chunk = u / NT;
-        const int nt = u - chunk * NT;
+        int chunk, nt;
+        unit_coords(u, n_chunks, NT, p.chunk_group, chunk, nt);
         const int e = __ldg(&p.chunk_expert[chunk]);
         const int p0 = __ldg(&p.chunk_row0[chunk]) + (int)rank * C::TM;
         const int wrow = e * p.Nw + nt * C::UNIT_ROWS + (int)rank * C::W_ROWS;
@@ -223,8 +224,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tok2Cfg::THREADS, 1)
     bool ok = true;
     int parity = 0;
     for (int u = pair; u < n_units; u += n_pairs, parity ^= 1) {
-      const int chunk = u / NT;
-      const int nt = u - chunk * NT;
+      int chunk, nt;
+      unit_coords(u, n_chunks, NT, p.chunk_group, chunk, nt);
       const int e = __ldg(&p.chunk_expert[chunk]);
       const int p0 = __ldg(&p.chunk_row0[chunk]) + (int)rank * C::TM;
       const int chunk_rows = __ldg(&p.chunk_rows[chunk]);

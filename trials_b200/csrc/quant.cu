@@ -28,23 +28,18 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
   if (a.sorted_ids) {
     const int f = __ldg(&a.sorted_ids[row]);
     src = (f >= 0 && f < a.sentinel) ? (int64_t)(f / a.topk) : -1;
+    // Padding rows are not written: a padding row only feeds its own MMA
+    // column (or row), whose results no epilogue keeps.
+    if (src < 0) return;
   }
   uint8_t* qr = a.q + row * a.ldq;
   if (a.xq != nullptr) {
     // Copy mode: the input is already quantised.
-    if (src >= 0) {
-      const uint8_t* sq = a.xq + src * a.ldxq;
-      for (int64_t b = seg0 + lane * 16; b < seg_end; b += 512)
-        *reinterpret_cast<uint4*>(qr + b) = __ldg(reinterpret_cast<const uint4*>(sq + b));
-      const int64_t g = (seg0 >> 7) + lane;
-      if (lane < kQuantSegCols / 128 && g * 128 < seg_end)
-        a.s[row * a.s_row + g * a.s_grp] = __ldg(&a.xs[src * a.ldxs + g]);
-    } else {
-      for (int64_t b = seg0 + lane * 16; b < seg_end; b += 512)
-        *reinterpret_cast<uint4*>(qr + b) = make_uint4(0, 0, 0, 0);
-      const int64_t g = (seg0 >> 7) + lane;
-      if (lane < kQuantSegCols / 128 && g * 128 < seg_end) a.s[row * a.s_row + g * a.s_grp] = 0.f;
-    }
+    const uint8_t* sq = a.xq + src * a.ldxq;
+    for (int64_t b = seg0 + lane * 16; b < seg_end; b += 512)
+      *reinterpret_cast<uint4*>(qr + b) = __ldg(reinterpret_cast<const uint4*>(sq + b));
+    const int64_t g = (seg0 >> 7) + lane;
+    if (lane < kQuantSegCols / 128 && g * 128 < seg_end) a.s[row * a.s_row + g * a.s_grp] = __ldg(&a.xs[src * a.ldxs + g]);
     return;
   }
   const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
@@ -52,7 +47,7 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
 #pragma unroll
   for (int i = 0; i < kQuantSegSteps; ++i) {
     const int64_t c = seg0 + i * 256 + lane * 8;
-    if (src >= 0 && c < seg_end) {
+    if (c < seg_end) {
       const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + c));
       const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
@@ -77,14 +72,11 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
     for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (c >= seg_end) continue;
     uint32_t lo = 0, hi = 0;
-    float scale = 0.f;
-    if (src >= 0) {
-      scale = group_scale(m);
+    const float scale = group_scale(m);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) lo |= (uint32_t)quant_e4m3(v[i][j], scale) << (8 * j);
+    for (int j = 0; j < 4; ++j) lo |= (uint32_t)quant_e4m3(v[i][j], scale) << (8 * j);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) hi |= (uint32_t)quant_e4m3(v[i][4 + j], scale) << (8 * j);
-    }
+    for (int j = 0; j < 4; ++j) hi |= (uint32_t)quant_e4m3(v[i][4 + j], scale) << (8 * j);
     *reinterpret_cast<uint2*>(qr + c) = make_uint2(lo, hi);
     if ((lane & 15) == 0) a.s[row * a.s_row + (c >> 7) * a.s_grp] = scale;
   }

@@ -79,6 +79,21 @@ def gather_quant(hidden: torch.Tensor, topk: int, r: Routing):
     return a_q, a_sT
 
 
+def gather_rows(xq: torch.Tensor, xs: torch.Tensor, topk: int, r: Routing):
+    """Already quantised token rows (xq (M, H) e4m3, xs (M, H/128) f32) ->
+    (a_q (rows_cap, H), a_sT (H/128, ld)) in sorted row order."""
+    dev = _require_cuda(xq, xs)
+    M, H = xq.shape
+    xq, xs = xq.contiguous(), xs.contiguous()
+    ld = r.a_s_ld()
+    a_q = torch.empty(r.rows_cap, H, dtype=FP8, device=dev)
+    a_sT = torch.empty(H // 128, ld, dtype=torch.float32, device=dev)
+    _lib.check(_lib.lib().b200moe_gather_rows(_ptr(xq), _ptr(xs), H, xs.shape[1], M, H, topk, _ptr(r.sorted_ids),
+                                              _ptr(r.num_rows), r.rows_cap, _ptr(a_q), _ptr(a_sT), ld, _stream(dev)),
+               "gather_rows")
+    return a_q, a_sT
+
+
 def gemm1_silu(a1_q, a1_sT, w13, w13_scale, r: Routing, grid_ctas: int = 0):
     """-> (a2_q (rows_cap, I) e4m3, a2_sT (I/128, ld) f32)."""
     dev = _require_cuda(a1_q, w13)
@@ -153,6 +168,11 @@ def selftest_wait_timeout(err: torch.Tensor, timeout_us: int = 20000) -> None:
     _lib.check(_lib.lib().b200moe_selftest_wait_timeout(_ptr(err), timeout_us, _stream(dev)), "selftest")
 
 
+# From this many routed pairs on, hidden rows are quantised once per token and
+# then copied into the sorted layout (the same rule as the C layer, capi.cu).
+TOKEN_QUANT_MIN_PAIRS = 2048
+
+
 def pick_tile_tokens(numel: int, num_local_experts: int) -> int:
     """Token columns per GEMM unit; the same rule as the C layer (capi.cu)."""
     avg = numel / max(num_local_experts, 1)
@@ -200,6 +220,10 @@ class LayerPipeline:
         self.a2 = torch.zeros(self.rows_cap, I, dtype=FP8, device=device)
         self.a2s = torch.zeros(I // 128, self.ld, dtype=torch.float32, device=device)
         self.pair = torch.zeros(max(numel, 1), H, dtype=torch.float32, device=device)
+        self.token_quant = numel >= TOKEN_QUANT_MIN_PAIRS
+        if self.token_quant:
+            self.tq = torch.zeros(M, H, dtype=FP8, device=device)
+            self.ts = torch.zeros(M, H // 128, dtype=torch.float32, device=device)
         self.out = torch.zeros(M, H, dtype=torch.bfloat16, device=device)
 
     def run(self, hidden, topk_ids, topk_weights, w13, w13_scale, w2, w2_scale, events=None, grid_ctas: int = 0):
@@ -216,8 +240,15 @@ class LayerPipeline:
                                    _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.ready), _ptr(self.err),
                                    st), "route")
         rec(1)
-        _lib.check(L.b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(self.sorted_ids), rows, self.rows_cap,
-                                          _ptr(self.a1), _ptr(self.a1s), self.ld, st), "gather_quant")
+        if self.token_quant:
+            _lib.check(L.b200moe_quant_1x128(_ptr(hidden), M, H, H, _ptr(self.tq), H, _ptr(self.ts), H // 128, 1, st),
+                       "quant_1x128")
+            _lib.check(L.b200moe_gather_rows(_ptr(self.tq), _ptr(self.ts), H, H // 128, M, H, topk,
+                                             _ptr(self.sorted_ids), rows, self.rows_cap, _ptr(self.a1), _ptr(self.a1s),
+                                             self.ld, st), "gather_rows")
+        else:
+            _lib.check(L.b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(self.sorted_ids), rows, self.rows_cap,
+                                              _ptr(self.a1), _ptr(self.a1s), self.ld, st), "gather_quant")
         rec(2)
         if not self.split:
             _lib.check(L.b200moe_experts(_ptr(self.a1), _ptr(self.a1s), self.ld, self.rows_cap, _ptr(w13),
