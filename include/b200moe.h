@@ -225,7 +225,9 @@ B200MOE_API int b200moe_layer_noalloc(const void* hidden, int64_t M, int64_t H, 
  * rows_capacity >= b200moe_route_capacity_rows()), plus the GEMM work list:
  * each expert's padded rows cut into chunks of at most tile_tokens rows
  * (16, 32, 64, 128 or 256); chunk_expert/chunk_row0/chunk_rows[chunks_capacity],
- * n_chunks[1] and num_rows[1] (total padded rows) on the device. chunk_ready
+ * n_chunks[1] and num_rows[1] (total padded rows) on the device. slot_pos
+ * (nullable, M*topk entries) receives the sorted row of every flat slot
+ * t*topk+j, or -1 for a dropped slot (for b200moe_combine_reduce). chunk_ready
  * (nullable, chunks_capacity entries) is zeroed for b200moe_experts.
  * ---------------------------------------------------------------------- */
 B200MOE_API int64_t b200moe_route_capacity_rows(int64_t numel, int num_local_experts);
@@ -233,8 +235,8 @@ B200MOE_API int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_e
 B200MOE_API int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
                   int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
                   int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
-                  int32_t* n_chunks, int32_t* num_rows, int32_t* chunk_ready, int32_t* err_word,
-                  void* stream);
+                  int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
+                  int32_t* err_word, void* stream);
 
 /* Quantise hidden rows into the sorted layout: row p of a_q (ld = H) holds
  * q(hidden[sorted_ids[p] / topk]); scales go to a_sT[g * a_s_ld + p]
@@ -263,9 +265,11 @@ B200MOE_API int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int6
                        const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens, uint8_t* a2_q,
                        float* a2_sT, int32_t* err_word, int grid_ctas, void* stream);
 
-/* Stage 2: out_pair[f, :] = topk_weights[f] * (a2 . w2^T)[p, :] for every
- * sorted row p with f = sorted_ids[p] < M*topk. out_pair is (M*topk, H) f32;
- * rows of dropped slots are not written. */
+/* Stage 2: topk_weights[f] * (a2 . w2^T)[p, :] for every sorted row p with
+ * f = sorted_ids[p] < M*topk, as an f32 row of H. Tiles of 16..64 tokens
+ * write it to row f of out_pair (M*topk, H); token-major tiles (128, 256) to
+ * row p of out_pair (rows_capacity, H), which keeps a unit's rows together in
+ * memory. Padding rows and dropped slots are not written. */
 B200MOE_API int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, int64_t rows_capacity,
                           const uint8_t* w2, const float* w2_scale, int num_local_experts, int64_t H, int64_t I,
                           const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
@@ -290,12 +294,13 @@ B200MOE_API int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t
                     const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, float* out_pair,
                     int32_t* err_word, int grid_ctas, void* stream);
 
-/* out[t, :] = bf16( sum_{j valid} out_pair[t*topk + j, :] ), slots summed in
- * order j = 0..topk-1; a slot is valid when its id is in [0, num_experts)
- * and (expert_map == NULL or expert_map[id] >= 0). Replaces the unpermute of
+/* out[t, :] = bf16( sum_j row_j ) over the slots j with slot_pos[t*topk + j]
+ * >= 0 (from b200moe_route), summed in order j = 0..topk-1; row_j is
+ * out_pair[slot_pos[t*topk + j]] when sorted_rows is non-zero (token-major
+ * tiles), else out_pair[t*topk + j]. Replaces the unpermute of
  * sglang_integration/aiter.py:164-177. */
-B200MOE_API int b200moe_combine_reduce(const float* out_pair, const int32_t* topk_ids, const int32_t* expert_map,
-                           int num_experts, int64_t M, int topk, int64_t H, void* out, void* stream);
+B200MOE_API int b200moe_combine_reduce(const float* out_pair, const int32_t* slot_pos, int sorted_rows, int64_t M,
+                           int topk, int64_t H, void* out, void* stream);
 
 /* ------------------------------------------------------------------------
  * Diagnostics.

@@ -176,12 +176,22 @@ def test_gather_and_gemm_stages(cuda_device, shape, tile):
                     for i, e in enumerate(experts)])
     w = L.topk_weights.reshape(-1)[torch.as_tensor(sorted_ids[valid], dtype=torch.long)].double()
     ref_pair = g2 * w[:, None]
-    got_pair = pair.cpu()[torch.as_tensor(sorted_ids[valid], dtype=torch.long)]
+    if r.sorted_rows:
+        got_pair = pair.cpu()[:n_rows][torch.as_tensor(valid)]
+    else:
+        got_pair = pair.cpu()[torch.as_tensor(sorted_ids[valid], dtype=torch.long)]
     assert orc.rel_l2(got_pair, ref_pair) < 1e-5
 
-    # top-k reduce
-    out = stages.combine_reduce(pair, g["topk_ids"], shape.E)
-    ref_out = pair.cpu().view(shape.M, topk, shape.H).sum(1).to(torch.bfloat16)
+    # slot positions: the inverse of the routed part of sorted_ids
+    pos = r.slot_pos.cpu().numpy()
+    assert (pos[sorted_ids[valid]] == np.nonzero(valid)[0]).all()
+    assert np.count_nonzero(pos >= 0) == int(valid.sum())
+
+    # top-k reduce: slot rows gathered by position, summed in slot order
+    out = stages.combine_reduce(pair, r, shape.M, topk)
+    by_slot = torch.zeros(shape.M * topk, shape.H, dtype=torch.float32)
+    by_slot[torch.as_tensor(sorted_ids[valid], dtype=torch.long)] = got_pair
+    ref_out = by_slot.view(shape.M, topk, shape.H).sum(1).to(torch.bfloat16)
     assert orc.rel_l2(out, ref_out) < 1e-2 ** 2
     assert int(r.err.item()) == 0
 

@@ -107,11 +107,15 @@ constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
 constexpr int64_t kTokenQuantMinPairs = 2048;
 bool token_quant_first(int64_t numel) { return numel >= kTokenQuantMinPairs; }
 
+// Stage-2 output row layout of a tile size: token-major tiles (128, 256)
+// write rows in sorted order, the swap-AB tiles one row per slot.
+int pair_sorted_rows(int tile_tokens) { return tile_tokens > 64 ? 1 : 0; }
+
 struct LayerPlan {
   int tile_tokens;
   int64_t rows_cap, chunks_cap, as_ld;
-  size_t off_sorted, off_ce, off_cr0, off_crows, off_ready, off_counts, off_a1, off_a1s, off_a2, off_a2s, off_pair,
-      off_tq, off_ts, total;
+  size_t off_sorted, off_pos, off_ce, off_cr0, off_crows, off_ready, off_counts, off_a1, off_a1s, off_a2, off_a2s,
+      off_pair, off_tq, off_ts, total;
   bool token_quant;  // quantise each token once, then copy rows (large batches)
 };
 
@@ -129,6 +133,7 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
     return o;
   };
   p.off_sorted = take(sizeof(int32_t) * p.rows_cap);
+  p.off_pos = take(sizeof(int32_t) * (numel > 0 ? numel : 1));
   p.off_ce = take(sizeof(int32_t) * p.chunks_cap);
   p.off_cr0 = take(sizeof(int32_t) * p.chunks_cap);
   p.off_crows = take(sizeof(int32_t) * p.chunks_cap);
@@ -138,7 +143,8 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
   p.off_a1s = take(sizeof(float) * (size_t)(H / 128) * p.as_ld);
   p.off_a2 = take((size_t)p.rows_cap * I);
   p.off_a2s = take(sizeof(float) * (size_t)(I / 128) * p.as_ld);
-  p.off_pair = take(sizeof(float) * (size_t)numel * H);
+  // Token-major tiles write sorted rows (rows_cap of them), the others slot rows.
+  p.off_pair = take(sizeof(float) * (size_t)(pair_sorted_rows(p.tile_tokens) ? p.rows_cap : numel) * H);
   p.token_quant = token_quant_first(numel);
   if (p.token_quant) {
     p.off_tq = take((size_t)M * H);
@@ -299,7 +305,8 @@ int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_experts, int 
 int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
                   int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
                   int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
-                  int32_t* n_chunks, int32_t* num_rows, int32_t* chunk_ready, int32_t* err_word, void* stream) {
+                  int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready, int32_t* err_word,
+                  void* stream) {
   if (M < 0 || topk <= 0 || num_experts <= 0 || !valid_tile(tile_tokens) || !sorted_ids || !chunk_expert ||
       !chunk_row0 || !chunk_rows || !n_chunks || !num_rows || !err_word || (M > 0 && !topk_ids))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_route: bad argument%s");
@@ -329,6 +336,7 @@ int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts,
   a.chunks_cap = chunks_capacity;
   a.n_chunks = n_chunks;
   a.chunk_ready = chunk_ready;
+  a.slot_pos = slot_pos;
   a.err = err_word;
   return cuda_status(launch_align(a, (cudaStream_t)stream), "route");
 }
@@ -489,16 +497,14 @@ int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int
                      "experts");
 }
 
-int b200moe_combine_reduce(const float* out_pair, const int32_t* topk_ids, const int32_t* expert_map,
-                           int num_experts, int64_t M, int topk, int64_t H, void* out, void* stream) {
-  if (M < 0 || topk <= 0 || H <= 0 || H % 8 != 0 || num_experts <= 0 ||
-      (M > 0 && (!out_pair || !topk_ids || !out)))
+int b200moe_combine_reduce(const float* out_pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
+                           int64_t H, void* out, void* stream) {
+  if (M < 0 || topk <= 0 || H <= 0 || H % 8 != 0 || (M > 0 && (!out_pair || !slot_pos || !out)))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_combine_reduce: bad argument%s");
   if (!aligned16(out_pair) || !aligned16(out))
     return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_combine_reduce: 16-byte alignment required%s");
-  return cuda_status(
-      launch_combine_reduce(out_pair, topk_ids, expert_map, num_experts, M, topk, H, out, (cudaStream_t)stream),
-      "combine_reduce");
+  return cuda_status(launch_combine_reduce(out_pair, slot_pos, sorted_rows, M, topk, H, out, (cudaStream_t)stream),
+                     "combine_reduce");
 }
 
 size_t b200moe_layer_workspace_size(int64_t M, int64_t H, int64_t I, int num_experts, int num_local_experts,
@@ -543,6 +549,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   int32_t* err = reinterpret_cast<int32_t*>(ws);
   uint8_t* wl = ws + workspace_offset;  // layer regions (the error word stays at offset 0)
   int32_t* sorted = reinterpret_cast<int32_t*>(wl + pl.off_sorted);
+  int32_t* pos = reinterpret_cast<int32_t*>(wl + pl.off_pos);
   int32_t* ce = reinterpret_cast<int32_t*>(wl + pl.off_ce);
   int32_t* cr0 = reinterpret_cast<int32_t*>(wl + pl.off_cr0);
   int32_t* crows = reinterpret_cast<int32_t*>(wl + pl.off_crows);
@@ -555,7 +562,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   float* pair = reinterpret_cast<float*>(wl + pl.off_pair);
 
   st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,
-                     crows, pl.chunks_cap, counts, counts + 1, ready, err, stream);
+                     crows, pl.chunks_cap, counts, counts + 1, pos, ready, err, stream);
   if (st) return st;
   LayerInput src = in;
   if (in.hidden && pl.token_quant) {
@@ -593,7 +600,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
                        pl.chunks_cap, ready, pl.tile_tokens, a2, a2s, sorted, topk_weights, M, topk, pair, err, 0,
                        stream);
   if (st) return st;
-  return b200moe_combine_reduce(pair, topk_ids, expert_map, num_experts, M, topk, H, out, stream);
+  return b200moe_combine_reduce(pair, pos, pair_sorted_rows(pl.tile_tokens), M, topk, H, out, stream);
 }
 
 }  // namespace

@@ -29,6 +29,7 @@ struct AlignArgs {
   int64_t chunks_cap;
   int32_t* n_chunks;
   int32_t* chunk_ready;    // nullable: zeroed over chunks_cap entries
+  int32_t* slot_pos;       // nullable: sorted position of each flat slot (n entries), -1 if dropped
   int32_t* err;
 };
 
@@ -64,8 +65,8 @@ cudaError_t launch_quant_1x128(const QuantArgs& a, cudaStream_t stream);
 cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K, uint8_t* q, float* s,
                                   cudaStream_t stream);
 
-cudaError_t launch_combine_reduce(const float* pair, const int32_t* ids, const int32_t* expert_map,
-                                  int num_experts, int64_t M, int topk, int64_t H, void* out, cudaStream_t stream);
+cudaError_t launch_combine_reduce(const float* pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
+                                  int64_t H, void* out, cudaStream_t stream);
 
 cudaError_t launch_ep_dispatch(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t M,
                                int64_t H, int topk, int num_experts, int G, int64_t rows_per_rank, uint8_t* send,

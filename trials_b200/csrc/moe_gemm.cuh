@@ -82,7 +82,7 @@ struct GemmParams {
   const int32_t* sorted_ids;
   const float* topk_w;
   int32_t sentinel;   // M * topk
-  float* out_pair;    // (M*topk, Nw) fp32
+  float* out_pair;    // fp32 rows of Nw: row f = slot (tiles <= 64) or sorted row p (tiles >= 128)
   // EPI_FUSED: per-chunk count of finished stage-1 units (zeroed by routing)
   int32_t* chunk_ready;
   // unit order: chunks per group (see unit_coords); 1 = chunk-major
@@ -650,6 +650,7 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
           fl[g] = c < rows ? __ldg(&pc.sorted_ids[p0 + c]) : pc.sentinel;
           wl[g] = fl[g] < pc.sentinel ? __ldg(&pc.topk_w[fl[g]]) : 0.f;
         }
+        // Row f (the slot) of out_pair; one 128-byte store per column.
         float* dst = pc.out_pair + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane;
 #pragma unroll
         for (int j = 0; j < C::TC; ++j) {

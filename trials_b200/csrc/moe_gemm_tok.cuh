@@ -45,6 +45,7 @@ struct TokCfg {
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
 };
 
+
 // d = a * s + d on two fp32 lanes at once (IEEE fma on each).
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float s) {
   uint64_t rd, ra, rs;
@@ -233,22 +234,37 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
     uint32_t sphase = 0, bphase = 0;
     bool ok = true;
     int parity = 0;
+    // The unit's weight block scales (one per K block of this 128-row half)
+    // are spread over the lanes (K blocks lane and lane + 32) and loaded
+    // before the previous unit's final epilogue, so no global load sits on
+    // the per-K-block path.
+    auto ws_row = [&](int e, int nt) { return p.w_scale + ((int64_t)e * (p.Nw >> 7) + nt * 2 + h) * NKB; };
+    float wl0 = 0.f, wl1 = 0.f;
+    auto load_ws = [&](int u) {
+      int c, t;
+      unit_coords(u, n_chunks, NT, p.chunk_group, c, t);
+      const float* w = ws_row(__ldg(&p.chunk_expert[c]), t);
+      wl0 = lane < NKB ? __ldg(w + lane) : 0.f;
+      wl1 = lane + 32 < NKB ? __ldg(w + lane + 32) : 0.f;
+    };
+    if (blockIdx.x < n_units) load_ws(blockIdx.x);
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, parity ^= 1) {
       int chunk, nt;
       unit_coords(u, n_chunks, NT, p.chunk_group, chunk, nt);
       const int e = __ldg(&p.chunk_expert[chunk]);
       const int p0 = __ldg(&p.chunk_row0[chunk]);
       const int rows = __ldg(&p.chunk_rows[chunk]);
+      const float ws0 = wl0, ws1 = wl1;
       const bool live = q * 32 < rows;  // warp-uniform
-      const float* wsp = p.w_scale + ((int64_t)e * (p.Nw >> 7) + nt * 2 + h) * NKB;
+      const float* wsp = ws_row(e, nt);
 
       float acc[128];
 #pragma unroll
       for (int j = 0; j < 128; ++j) acc[j] = 0.f;
 
-      float ws = __ldg(wsp);
       for (int kb = 0; kb < NKB && ok; ++kb) {
-        const float wsn = (kb + 1 < NKB) ? __ldg(wsp + kb + 1) : 0.f;
+        const float wsh = __shfl_sync(0xffffffffu, kb < 32 ? ws0 : ws1, kb & 31);
+        const float ws = kb < 64 ? wsh : __ldg(wsp + kb);
         if (*abort_flag || !mbar_wait_bounded(&tfull[buf], bphase, p.timeout_ns)) {
           ok = false;
           break;
@@ -293,7 +309,6 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
           mbar_arrive(&tempty[buf]);
           mbar_arrive(&sempty[slot]);
         }
-        ws = wsn;
         if (++slot == C::NSLOT) {
           slot = 0;
           sphase ^= 1;
@@ -307,6 +322,7 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
         atomicOr(p.err, ERR_DEV_TIMEOUT);
         *abort_flag = 1;
       }
+      if (u + (int)gridDim.x < n_units) load_ws(u + gridDim.x);
 
       if constexpr (EPI == EPI_SILU) {
         // inter column i of this half = silu(acc[2i]) * acc[2i+1]; group of 128
@@ -347,7 +363,10 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
           const int f = __ldg(&p.sorted_ids[p0 + r]);
           if (f < p.sentinel) {
             const float w = __ldg(&p.topk_w[f]);
-            float4* dst = reinterpret_cast<float4*>(p.out_pair + (int64_t)f * p.Nw + nt * C::UNIT_ROWS + h * 128);
+            // Row p of out_pair = sorted row p: a unit's rows are neighbours in
+            // memory (rows by slot id scatter them over the whole buffer, and the
+            // stores then cost more than the unit's MMAs at prefill sizes).
+            float4* dst = reinterpret_cast<float4*>(p.out_pair + (int64_t)(p0 + r) * p.Nw + nt * C::UNIT_ROWS + h * 128);
 #pragma unroll
             for (int k = 0; k < 32; ++k)
               dst[k] = make_float4(w * acc[4 * k], w * acc[4 * k + 1], w * acc[4 * k + 2], w * acc[4 * k + 3]);

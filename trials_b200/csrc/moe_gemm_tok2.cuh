@@ -238,9 +238,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tok2Cfg::THREADS, 1)
 #pragma unroll
       for (int j = 0; j < 128; ++j) acc[j] = 0.f;
 
-      float ws = __ldg(wsp);
+      // The unit's weight block scales spread over the lanes (K blocks lane
+      // and lane + 32), read by shuffle: no global load per K block.
+      const float ws0 = lane < NKB ? __ldg(wsp + lane) : 0.f;
+      const float ws1 = lane + 32 < NKB ? __ldg(wsp + lane + 32) : 0.f;
       for (int kb = 0; kb < NKB && ok; ++kb) {
-        const float wsn = (kb + 1 < NKB) ? __ldg(wsp + kb + 1) : 0.f;
+        const float wsh = __shfl_sync(0xffffffffu, kb < 32 ? ws0 : ws1, kb & 31);
+        const float ws = kb < 64 ? wsh : __ldg(wsp + kb);
         if (*abort_flag || !mbar_wait_bounded(&tfull[buf], bphase, p.timeout_ns)) {
           ok = false;
           break;
@@ -277,7 +281,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tok2Cfg::THREADS, 1)
           mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
           mbar_arrive(&sempty[slot]);
         }
-        ws = wsn;
         if (++slot == C::NSLOT) {
           slot = 0;
           sphase ^= 1;
@@ -329,7 +332,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tok2Cfg::THREADS, 1)
           const int f = __ldg(&p.sorted_ids[p0 + r]);
           if (f < p.sentinel) {
             const float w = __ldg(&p.topk_w[f]);
-            float4* dst = reinterpret_cast<float4*>(p.out_pair + (int64_t)f * p.Nw + nt * C::UNIT_ROWS + h * 128);
+            // Row p of out_pair = sorted row p: a unit's rows are neighbours in
+            // memory (rows by slot id scatter them over the whole buffer, and the
+            // stores then cost more than the unit's MMAs at prefill sizes).
+            float4* dst = reinterpret_cast<float4*>(p.out_pair + (int64_t)(p0 + r) * p.Nw + nt * C::UNIT_ROWS + h * 128);
 #pragma unroll
             for (int k = 0; k < 32; ++k)
               dst[k] = make_float4(w * acc[4 * k], w * acc[4 * k + 1], w * acc[4 * k + 2], w * acc[4 * k + 3]);

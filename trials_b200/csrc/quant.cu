@@ -150,14 +150,14 @@ cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K
 }
 
 // ---------------------------------------------------------------------------
-// Top-k combine: out[t, n] = bf16(sum_j pair[t*topk + j, n]) over valid slots,
-// summed in slot order (the view(M, k, K).sum(1) of
+// Top-k combine: out[t, n] = bf16(sum_j pair[pos(t, j), n]) over the routed
+// slots, summed in slot order j (the view(M, k, K).sum(1) of
 // sglang_integration/aiter.py:176-177, on fp32 rows that already carry the
-// router weight). One thread per 8 output columns.
+// router weight). pos = slot_pos[t*topk+j] (-1: slot dropped); the slot's row
+// of pair is pos (sorted_rows) or t*topk+j. One thread per 8 output columns.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __restrict__ pair,
-                                                             const int32_t* __restrict__ ids,
-                                                             const int32_t* __restrict__ emap, int num_experts,
+                                                             const int32_t* __restrict__ slot_pos, int sorted_rows,
                                                              int64_t M, int topk, int64_t H,
                                                              __nv_bfloat16* __restrict__ out) {
   const int64_t per_row = H / 8;
@@ -169,11 +169,10 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __rest
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   for (int j = 0; j < topk; ++j) {
-    const int id = __ldg(&ids[t * topk + j]);
-    bool valid = id >= 0 && id < num_experts;
-    if (valid && emap) valid = __ldg(&emap[id]) >= 0;
-    if (!valid) continue;
-    const float4* src = reinterpret_cast<const float4*>(pair + (t * topk + j) * H + c);
+    const int pos = __ldg(&slot_pos[t * topk + j]);
+    if (pos < 0) continue;
+    const int64_t row = sorted_rows ? (int64_t)pos : t * topk + j;
+    const float4* src = reinterpret_cast<const float4*>(pair + row * H + c);
     const float4 a = __ldg(src), b = __ldg(src + 1);
     acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
     acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
@@ -184,12 +183,12 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __rest
   *reinterpret_cast<uint4*>(out + t * H + c) = *reinterpret_cast<const uint4*>(o);
 }
 
-cudaError_t launch_combine_reduce(const float* pair, const int32_t* ids, const int32_t* expert_map,
-                                  int num_experts, int64_t M, int topk, int64_t H, void* out, cudaStream_t stream) {
+cudaError_t launch_combine_reduce(const float* pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
+                                  int64_t H, void* out, cudaStream_t stream) {
   const int64_t n = M * (H / 8);
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = (n + 255) / 256;
-  combine_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pair, ids, expert_map, num_experts, M, topk, H,
+  combine_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, M, topk, H,
                                                               reinterpret_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }

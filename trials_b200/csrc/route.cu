@@ -129,8 +129,11 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
     *a.ntp = overflow ? 0 : total_rows;
     if (a.n_chunks) *a.n_chunks = overflow ? 0 : total_chunks;
   }
-  // Defined contents everywhere: sentinel ids first, then the scatter below.
+  // Defined contents everywhere: sentinel ids (and no position for any slot)
+  // first, then the scatter below.
   for (int64_t i = tid; i < a.sorted_cap; i += kRouteThreads) a.sorted_ids[i] = a.sentinel;
+  if (a.slot_pos)
+    for (int64_t i = tid; i < a.n; i += kRouteThreads) a.slot_pos[i] = -1;
   __syncthreads();
   if (overflow) return;
 
@@ -143,7 +146,9 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
     int step = 0;
     if (e >= 0) {
       const int rank = __popc(peers & lt_mask);
-      a.sorted_ids[base[e] + cnt[warp * E + e] + rank] = (int32_t)i;
+      const int32_t pos = base[e] + cnt[warp * E + e] + rank;
+      a.sorted_ids[pos] = (int32_t)i;
+      if (a.slot_pos) a.slot_pos[i] = pos;
       step = __popc(peers);
     }
     __syncwarp();

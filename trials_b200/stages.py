@@ -31,6 +31,7 @@ class Routing:
     counts: torch.Tensor        # [n_chunks, num_rows] int32
     err: torch.Tensor           # (1,) int32
     chunk_ready: torch.Tensor   # (chunks_cap,) int32, zeroed by route for experts()
+    slot_pos: torch.Tensor      # (M*topk,) int32: sorted row of each flat slot, -1 if dropped
 
     @property
     def n_chunks(self):
@@ -42,6 +43,14 @@ class Routing:
 
     def a_s_ld(self) -> int:
         return (self.rows_cap + 256 + 63) // 64 * 64
+
+    @property
+    def sorted_rows(self) -> int:
+        """Stage-2 output layout: 1 = row p (sorted, token-major tiles), 0 = row of the slot."""
+        return 1 if self.tile_tokens > 64 else 0
+
+    def pair_rows(self, M: int, topk: int) -> int:
+        return self.rows_cap if self.sorted_rows else M * topk
 
 
 def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map: Optional[torch.Tensor] = None,
@@ -56,12 +65,12 @@ def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map
     z = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=dev)  # noqa: E731
     r = Routing(tile_tokens, rows_cap, chunks_cap, z(rows_cap), z(chunks_cap), z(chunks_cap), z(chunks_cap),
                 torch.zeros(2, dtype=torch.int32, device=dev),
-                err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev), z(chunks_cap))
+                err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev), z(chunks_cap), z(M * topk))
     if expert_map is not None:
         expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
     _lib.check(L.b200moe_route(_ptr(ids), M, topk, num_experts, _ptr(expert_map), E, tile_tokens,
                                _ptr(r.sorted_ids), rows_cap, _ptr(r.chunk_expert), _ptr(r.chunk_row0),
-                               _ptr(r.chunk_rows), chunks_cap, _ptr(r.n_chunks), _ptr(r.num_rows),
+                               _ptr(r.chunk_rows), chunks_cap, _ptr(r.n_chunks), _ptr(r.num_rows), _ptr(r.slot_pos),
                                _ptr(r.chunk_ready), _ptr(r.err), _stream(dev)), "route")
     return r
 
@@ -111,13 +120,14 @@ def gemm1_silu(a1_q, a1_sT, w13, w13_scale, r: Routing, grid_ctas: int = 0):
 
 def gemm2_combine(a2_q, a2_sT, w2, w2_scale, r: Routing, topk_weights: torch.Tensor, grid_ctas: int = 0,
                   out_pair: Optional[torch.Tensor] = None):
-    """-> out_pair (M*topk, H) f32 (rows of dropped slots untouched)."""
+    """-> out_pair f32 rows of H: row p = sorted row p for token-major tiles (rows_cap
+    rows), else row f = slot (M*topk rows). Padding rows / dropped slots untouched."""
     dev = _require_cuda(a2_q, w2)
     E, H, I = w2.shape
     M, topk = topk_weights.shape
     tw = topk_weights.to(torch.float32).contiguous()
     if out_pair is None:
-        out_pair = torch.zeros(M * topk, H, dtype=torch.float32, device=dev)
+        out_pair = torch.zeros(r.pair_rows(M, topk), H, dtype=torch.float32, device=dev)
     _lib.check(_lib.lib().b200moe_gemm2_combine(
         _ptr(a2_q), _ptr(a2_sT), r.a_s_ld(), r.rows_cap, _ptr(w2), _ptr(w2_scale.contiguous()), E, H, I,
         _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows), _ptr(r.n_chunks), r.chunks_cap,
@@ -140,7 +150,7 @@ def experts(a1_q, a1_sT, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights:
     a2_sT = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
     tw = topk_weights.to(torch.float32).contiguous()
     if out_pair is None:
-        out_pair = torch.zeros(M * topk, H, dtype=torch.float32, device=dev)
+        out_pair = torch.zeros(r.pair_rows(M, topk), H, dtype=torch.float32, device=dev)
     _lib.check(_lib.lib().b200moe_experts(
         _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13), _ptr(w13_scale.contiguous()), _ptr(w2),
         _ptr(w2_scale.contiguous()), E, H, I, _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows),
@@ -149,17 +159,13 @@ def experts(a1_q, a1_sT, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights:
     return a2_q, a2_sT, out_pair
 
 
-def combine_reduce(out_pair: torch.Tensor, topk_ids: torch.Tensor, num_experts: int,
-                   expert_map: Optional[torch.Tensor] = None) -> torch.Tensor:
-    dev = _require_cuda(out_pair, topk_ids)
-    ids = topk_ids.to(torch.int32).contiguous()
-    M, topk = ids.shape
+def combine_reduce(out_pair: torch.Tensor, r: Routing, M: int, topk: int) -> torch.Tensor:
+    """out[t] = bf16(sum over the routed slots j of the slot's stage-2 row)."""
+    dev = _require_cuda(out_pair)
     H = out_pair.shape[1]
     out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
-    if expert_map is not None:
-        expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
-    _lib.check(_lib.lib().b200moe_combine_reduce(_ptr(out_pair), _ptr(ids), _ptr(expert_map), num_experts, M,
-                                                 topk, H, _ptr(out), _stream(dev)), "combine_reduce")
+    _lib.check(_lib.lib().b200moe_combine_reduce(_ptr(out_pair), _ptr(r.slot_pos), r.sorted_rows, M, topk, H,
+                                                 _ptr(out), _stream(dev)), "combine_reduce")
     return out
 
 
@@ -211,6 +217,7 @@ class LayerPipeline:
         self.sorted_ids, self.ce, self.cr0, self.crows = z(self.rows_cap), z(self.chunks_cap), z(self.chunks_cap), \
             z(self.chunks_cap)
         self.ready = z(self.chunks_cap)
+        self.slot_pos = z(numel)
         self.split = split
         self.stages = self.SPLIT_STAGES if split else self.FUSED_STAGES
         self.counts = z(2)
@@ -219,7 +226,9 @@ class LayerPipeline:
         self.a1s = torch.zeros(H // 128, self.ld, dtype=torch.float32, device=device)
         self.a2 = torch.zeros(self.rows_cap, I, dtype=FP8, device=device)
         self.a2s = torch.zeros(I // 128, self.ld, dtype=torch.float32, device=device)
-        self.pair = torch.zeros(max(numel, 1), H, dtype=torch.float32, device=device)
+        self.sorted_rows = 1 if self.tile > 64 else 0
+        self.pair = torch.zeros(max(self.rows_cap if self.sorted_rows else numel, 1), H, dtype=torch.float32,
+                                device=device)
         self.token_quant = numel >= TOKEN_QUANT_MIN_PAIRS
         if self.token_quant:
             self.tq = torch.zeros(M, H, dtype=FP8, device=device)
@@ -237,8 +246,8 @@ class LayerPipeline:
         rec(0)
         _lib.check(L.b200moe_route(_ptr(topk_ids), M, topk, self.num_experts, _ptr(self.expert_map), E, self.tile,
                                    _ptr(self.sorted_ids), self.rows_cap, _ptr(self.ce), _ptr(self.cr0),
-                                   _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.ready), _ptr(self.err),
-                                   st), "route")
+                                   _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.slot_pos),
+                                   _ptr(self.ready), _ptr(self.err), st), "route")
         rec(1)
         if self.token_quant:
             _lib.check(L.b200moe_quant_1x128(_ptr(hidden), M, H, H, _ptr(self.tq), H, _ptr(self.ts), H // 128, 1, st),
@@ -258,8 +267,9 @@ class LayerPipeline:
                                          _ptr(topk_weights), M, topk, _ptr(self.pair), _ptr(self.err), grid_ctas,
                                          st), "experts")
             rec(3)
-            _lib.check(L.b200moe_combine_reduce(_ptr(self.pair), _ptr(topk_ids), _ptr(self.expert_map),
-                                                self.num_experts, M, topk, H, _ptr(self.out), st), "combine_reduce")
+            _lib.check(L.b200moe_combine_reduce(_ptr(self.pair), _ptr(self.slot_pos), self.sorted_rows, M, topk, H,
+                                                _ptr(self.out), st),
+                       "combine_reduce")
             rec(4)
             return self.out
         _lib.check(L.b200moe_gemm1_silu(_ptr(self.a1), _ptr(self.a1s), self.ld, self.rows_cap, _ptr(w13),
@@ -273,7 +283,8 @@ class LayerPipeline:
                                            _ptr(topk_weights), M, topk, _ptr(self.pair), _ptr(self.err), grid_ctas,
                                            st), "gemm2_combine")
         rec(4)
-        _lib.check(L.b200moe_combine_reduce(_ptr(self.pair), _ptr(topk_ids), _ptr(self.expert_map),
-                                            self.num_experts, M, topk, H, _ptr(self.out), st), "combine_reduce")
+        _lib.check(L.b200moe_combine_reduce(_ptr(self.pair), _ptr(self.slot_pos), self.sorted_rows, M, topk, H,
+                                                _ptr(self.out), st),
+                   "combine_reduce")
         rec(5)
         return self.out
