@@ -36,7 +36,8 @@ struct TokCfg {
   static constexpr int RED = 2 * 2 * TM * 4;     // amax exchange, double-buffered by unit parity
   static constexpr int SMEM_LIMIT = 232448;
   static constexpr int MAX_STAGE = 6;
-  static constexpr int FIXED = 1024 + RED + (MAX_STAGE + NBUF) * S_BYTES + 1024;
+  static constexpr int XPOSE = EW * 32 * 20 * 4;  // stage-2 store transpose blocks
+  static constexpr int FIXED = 1024 + RED + (MAX_STAGE + NBUF) * S_BYTES + 1024 + XPOSE;
   static constexpr int NSTAGE_RAW = (SMEM_LIMIT - FIXED) / TILE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > MAX_STAGE ? MAX_STAGE : NSTAGE_RAW;
   static constexpr int NSLOT = NSTAGE + NBUF;
@@ -45,6 +46,34 @@ struct TokCfg {
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
 };
 
+
+// Router-weighted fp32 rows of a token-major unit, in sorted row order. The
+// calling warp holds rows row0 .. row0+31 of the unit (lane = row) x 128
+// output columns in acc. They pass through tb (this warp's 32 x 20 floats of
+// shared memory) 16 columns at a time, so that every store instruction writes
+// 64 contiguous bytes of 8 rows (whole 32-byte sectors) instead of 16 bytes of
+// 32 rows. Only rows whose bit is set in `valid` (bit i = row row0 + i, a
+// routed slot) are written; w_l is the lane's router weight.
+__device__ __forceinline__ void store_sorted_rows(const float (&acc)[128], float w_l, unsigned valid, float* tb,
+                                                  int lane, int row0, float* out, int64_t ld) {
+#pragma unroll
+  for (int cb = 0; cb < 8; ++cb) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      *reinterpret_cast<float4*>(tb + lane * 20 + 4 * k) =
+          make_float4(w_l * acc[cb * 16 + 4 * k], w_l * acc[cb * 16 + 4 * k + 1], w_l * acc[cb * 16 + 4 * k + 2],
+                      w_l * acc[cb * 16 + 4 * k + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const int row = rr * 8 + (lane >> 2);
+      const float4 v = *reinterpret_cast<const float4*>(tb + row * 20 + 4 * (lane & 3));
+      if ((valid >> row) & 1u)
+        *reinterpret_cast<float4*>(out + (int64_t)(row0 + row) * ld + cb * 16 + 4 * (lane & 3)) = v;
+    }
+    __syncwarp();
+  }
+}
 
 // d = a * s + d on two fp32 lanes at once (IEEE fma on each).
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float s) {
@@ -87,6 +116,7 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
   // The epilogue's stop decision for a unit, written by one thread before the
   // unit's first named barrier so that every epilogue warp reads the same value.
   volatile int* stop_sh = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  float* xpose = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 1024);  // EW x 32 x 20
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -359,18 +389,15 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
         }
       } else {
         if (!ok) break;
-        if (r < rows) {
-          const int f = __ldg(&p.sorted_ids[p0 + r]);
-          if (f < p.sentinel) {
-            const float w = __ldg(&p.topk_w[f]);
-            // Row p of out_pair = sorted row p: a unit's rows are neighbours in
-            // memory (rows by slot id scatter them over the whole buffer, and the
-            // stores then cost more than the unit's MMAs at prefill sizes).
-            float4* dst = reinterpret_cast<float4*>(p.out_pair + (int64_t)(p0 + r) * p.Nw + nt * C::UNIT_ROWS + h * 128);
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-              dst[k] = make_float4(w * acc[4 * k], w * acc[4 * k + 1], w * acc[4 * k + 2], w * acc[4 * k + 3]);
-          }
+        // Row p of out_pair = sorted row p: a unit's rows are neighbours in
+        // memory (rows by slot id scatter them over the whole buffer, and the
+        // stores then cost more than the unit's MMAs at prefill sizes).
+        if (live) {
+          const int f = r < rows ? __ldg(&p.sorted_ids[p0 + r]) : p.sentinel;
+          const float w = f < p.sentinel ? __ldg(&p.topk_w[f]) : 0.f;
+          const unsigned valid = __ballot_sync(0xffffffffu, f < p.sentinel);
+          store_sorted_rows(acc, w, valid, xpose + ew * (32 * 20), lane, q * 32,
+                            p.out_pair + (int64_t)p0 * p.Nw + nt * C::UNIT_ROWS + h * 128, p.Nw);
         }
       }
     }

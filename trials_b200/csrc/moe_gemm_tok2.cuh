@@ -40,7 +40,8 @@ struct Tok2Cfg {
   static constexpr int RED = 2 * 2 * TM * 4;
   static constexpr int SMEM_LIMIT = 232448;
   static constexpr int MAX_STAGE = 6;
-  static constexpr int FIXED = 1024 + RED + (MAX_STAGE + NBUF) * S_BYTES + 1024;
+  static constexpr int XPOSE = EW * 32 * 20 * 4;  // stage-2 store transpose blocks
+  static constexpr int FIXED = 1024 + RED + (MAX_STAGE + NBUF) * S_BYTES + 1024 + XPOSE;
   static constexpr int NSTAGE_RAW = (SMEM_LIMIT - FIXED) / TILE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > MAX_STAGE ? MAX_STAGE : NSTAGE_RAW;
   static constexpr int NSLOT = NSTAGE + NBUF;
@@ -71,6 +72,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tok2Cfg::THREADS, 1)
   // The epilogue's stop decision for a unit, written by one thread before the
   // unit's first named barrier so that every epilogue warp reads the same value.
   volatile int* stop_sh = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  float* xpose = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 1024);  // EW x 32 x 20
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -328,18 +330,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tok2Cfg::THREADS, 1)
         }
       } else {
         if (!ok) break;
-        if (r < rows) {
-          const int f = __ldg(&p.sorted_ids[p0 + r]);
-          if (f < p.sentinel) {
-            const float w = __ldg(&p.topk_w[f]);
-            // Row p of out_pair = sorted row p: a unit's rows are neighbours in
-            // memory (rows by slot id scatter them over the whole buffer, and the
-            // stores then cost more than the unit's MMAs at prefill sizes).
-            float4* dst = reinterpret_cast<float4*>(p.out_pair + (int64_t)(p0 + r) * p.Nw + nt * C::UNIT_ROWS + h * 128);
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-              dst[k] = make_float4(w * acc[4 * k], w * acc[4 * k + 1], w * acc[4 * k + 2], w * acc[4 * k + 3]);
-          }
+        // Row p of out_pair = sorted row p (see the one-CTA kernel).
+        if (live) {
+          const int f = r < rows ? __ldg(&p.sorted_ids[p0 + r]) : p.sentinel;
+          const float w = f < p.sentinel ? __ldg(&p.topk_w[f]) : 0.f;
+          const unsigned valid = __ballot_sync(0xffffffffu, f < p.sentinel);
+          store_sorted_rows(acc, w, valid, xpose + ew * (32 * 20), lane, q * 32,
+                            p.out_pair + (int64_t)p0 * p.Nw + nt * C::UNIT_ROWS + h * 128, p.Nw);
         }
       }
     }
