@@ -24,6 +24,7 @@ namespace b200moe {
 
 constexpr int kRouteWarps = 32;
 constexpr int kRouteThreads = kRouteWarps * 32;
+constexpr int kRouteBatch = 8;  // 32-id steps whose loads a warp issues together
 
 // Maps a raw id to the weight index, -1 = drop. Reports bad ids when `report`.
 __device__ __forceinline__ int map_expert(const AlignArgs& a, int raw, bool report) {
@@ -88,12 +89,21 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
   const int64_t beg = warp * seg;
   const int64_t end = beg + seg < n ? beg + seg : n;
 
-  // Pass 1: per-(warp, expert) counts.
-  for (int64_t i0 = beg; i0 < end; i0 += 32) {
-    const int64_t i = i0 + lane;
-    const int e = (i < end) ? map_expert(a, __ldg(&a.topk_ids[i]), true) : -2;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+  // Pass 1: per-(warp, expert) counts. Each warp loads kRouteBatch steps of
+  // ids before it counts any (one load round trip per batch, not per step).
+  for (int64_t i0 = beg; i0 < end; i0 += 32 * kRouteBatch) {
+    int ev[kRouteBatch];
+#pragma unroll
+    for (int u = 0; u < kRouteBatch; ++u) {
+      const int64_t i = i0 + u * 32 + lane;
+      ev[u] = (i < end) ? map_expert(a, __ldg(&a.topk_ids[i]), true) : -2;
+    }
+#pragma unroll
+    for (int u = 0; u < kRouteBatch; ++u) {
+      const unsigned peers = __match_any_sync(0xffffffffu, ev[u]);
+      if (ev[u] >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + ev[u]] += __popc(peers);
+      __syncwarp();
+    }
   }
   __syncthreads();
 
@@ -139,21 +149,30 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
 
   // Pass 2: stable scatter.
   const unsigned lt_mask = (1u << lane) - 1u;
-  for (int64_t i0 = beg; i0 < end; i0 += 32) {
-    const int64_t i = i0 + lane;
-    const int e = (i < end) ? map_expert(a, __ldg(&a.topk_ids[i]), false) : -2;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    int step = 0;
-    if (e >= 0) {
-      const int rank = __popc(peers & lt_mask);
-      const int32_t pos = base[e] + cnt[warp * E + e] + rank;
-      a.sorted_ids[pos] = (int32_t)i;
-      if (a.slot_pos) a.slot_pos[i] = pos;
-      step = __popc(peers);
+  for (int64_t i0 = beg; i0 < end; i0 += 32 * kRouteBatch) {
+    int ev[kRouteBatch];
+#pragma unroll
+    for (int u = 0; u < kRouteBatch; ++u) {
+      const int64_t i = i0 + u * 32 + lane;
+      ev[u] = (i < end) ? map_expert(a, __ldg(&a.topk_ids[i]), false) : -2;
     }
-    __syncwarp();
-    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += step;
-    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < kRouteBatch; ++u) {
+      const int64_t i = i0 + u * 32 + lane;
+      const int e = ev[u];
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      int step = 0;
+      if (e >= 0) {
+        const int rank = __popc(peers & lt_mask);
+        const int32_t pos = base[e] + cnt[warp * E + e] + rank;
+        a.sorted_ids[pos] = (int32_t)i;
+        if (a.slot_pos) a.slot_pos[i] = pos;
+        step = __popc(peers);
+      }
+      __syncwarp();
+      if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += step;
+      __syncwarp();
+    }
   }
 
   // Expert id of every block_m block; -1 past the routed rows.
