@@ -48,16 +48,17 @@ struct TokCfg {
 
 
 // Router-weighted fp32 rows of a token-major unit, in sorted row order. The
-// calling warp holds rows row0 .. row0+31 of the unit (lane = row) x 128
+// calling warp holds rows row0 .. row0+31 of the unit (lane = row) x NC
 // output columns in acc. They pass through tb (this warp's 32 x 20 floats of
 // shared memory) 16 columns at a time, so that every store instruction writes
 // 64 contiguous bytes of 8 rows (whole 32-byte sectors) instead of 16 bytes of
 // 32 rows. Only rows whose bit is set in `valid` (bit i = row row0 + i, a
 // routed slot) are written; w_l is the lane's router weight.
-__device__ __forceinline__ void store_sorted_rows(const float (&acc)[128], float w_l, unsigned valid, float* tb,
+template <int NC>
+__device__ __forceinline__ void store_sorted_rows(const float (&acc)[NC], float w_l, unsigned valid, float* tb,
                                                   int lane, int row0, float* out, int64_t ld) {
 #pragma unroll
-  for (int cb = 0; cb < 8; ++cb) {
+  for (int cb = 0; cb < NC / 16; ++cb) {
 #pragma unroll
     for (int k = 0; k < 4; ++k)
       *reinterpret_cast<float4*>(tb + lane * 20 + 4 * k) =
