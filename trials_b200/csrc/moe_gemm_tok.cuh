@@ -91,6 +91,10 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
 #ifndef B200MOE_TOK_LD_BATCH
 #define B200MOE_TOK_LD_BATCH 2
 #endif
+// L2 hint on token-major weight tiles: 0 none, 1 evict_first, 2 evict_last.
+#ifndef B200MOE_TOK_W_POLICY
+#define B200MOE_TOK_W_POLICY 0
+#endif
 #ifndef B200MOE_TOK_FFMA2
 #define B200MOE_TOK_FFMA2 1
 #endif
@@ -158,7 +162,10 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
+      // Weight tiles of a group's chunks are shared through L2 by units that
+      // run at the same time (unit_coords), activation tiles by the 2I/256 or
+      // H/256 units of a chunk: neither may be evicted first.
+      const uint64_t pol_w = B200MOE_TOK_W_POLICY == 2 ? policy_evict_last() : policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
       int stage = 0, slot = 0;
       uint32_t phase = 0, sphase = 0;
@@ -179,7 +186,10 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
           uint8_t* tile = tiles + stage * C::TILE_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::TILE_BYTES);
           tma_load_2d(tile, &tm_a, &full[stage], kb * 128, p0, pol_a);
-          tma_load_2d(tile + C::A_BYTES, &tm_w, &full[stage], kb * 128, wrow, pol_w);
+          if (B200MOE_TOK_W_POLICY == 1 || B200MOE_TOK_W_POLICY == 2)
+            tma_load_2d(tile + C::A_BYTES, &tm_w, &full[stage], kb * 128, wrow, pol_w);
+          else
+            tma_load_2d(tile + C::A_BYTES, &tm_w, &full[stage], kb * 128, wrow);
           mbar_arrive_expect_tx(&sfull[slot], C::S_BYTES);
           bulk_load(sscale + slot * C::TM, p.a_sT + (int64_t)kb * p.as_ld + p0, C::S_BYTES, &sfull[slot]);
           ++issued;
