@@ -8,13 +8,15 @@ synthetic GLM-5-like decode batch (M=64 tokens by default: H=6144, I=2048,
 E=256 experts, top-8 sigmoid router, FP8 e4m3 weights with fp32 128x128 block
 scales, 1x128 activation scales, bf16 in/out).
 
-  value       tokens/s over all ranks, inputs resident in HBM, the five kernels
-              of the layer (route, gather+quant, GEMM1+SiLU+requant,
-              GEMM2+combine, top-k reduce) timed with CUDA events on their stream;
+  value       tokens/s over all ranks, inputs resident in HBM, the launches of
+              the layer (route, gather+quant, both grouped-GEMM stages in one
+              launch, top-k reduce) timed with CUDA events on their stream;
   e2e         the same metric through the public API moe_decode_megakernel_full
-              with host (pinned) inputs copied in and the output copied out
-              inside the timed region;
-  roofline    the dominant kernel (GEMM1) against measured HBM bandwidth;
+              with host (pinned) inputs copied in (one copy of the packed
+              hidden rows, ids and weights) and the output copied out inside
+              the timed region;
+  roofline    the dominant kernel (the grouped GEMMs) against measured HBM
+              bandwidth;
   cpu_baseline the fp32 CPU oracle on a bounded sample of experts (rank 0, N=1).
 --impl reference times that CPU path alone (the reference is a Python/Triton
 package for AMD GPUs; its algorithm is restated by the oracle).
@@ -178,6 +180,26 @@ def layer_bytes(shape, active, pairs):
     return w + shape.M * shape.H * 2 * 2
 
 
+def packed_inputs(*tensors):
+    """One pinned host buffer and one device buffer holding the step's input
+    tensors back to back (16-byte aligned), so that each step copies its inputs
+    in with a single host-to-device copy. -> (host, device, device views)."""
+    import torch
+
+    offs, off = [], 0
+    for t in tensors:
+        offs.append(off)
+        off += (t.numel() * t.element_size() + 15) // 16 * 16
+    host = torch.empty(off, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(off, dtype=torch.uint8, device=tensors[0].device)
+    views = []
+    for t, o in zip(tensors, offs):
+        n = t.numel() * t.element_size()
+        host[o:o + n].copy_(t.contiguous().view(-1).view(torch.uint8).cpu())
+        views.append(dev[o:o + n].view(t.dtype).view(t.shape))
+    return host, dev, views
+
+
 def gemm2_bytes(shape, active, pairs):
     """Algorithmic bytes of one GEMM2 launch: w2 + its scales of every active
     expert, the fp8 inter rows and scales read, the fp32 weighted rows written."""
@@ -339,14 +361,11 @@ def run_ep(args, shape, config):
 
     e2e = None
     if not args.no_e2e:
-        h_host, ids_host, tw_host = hidden.cpu().pin_memory(), ids.cpu().pin_memory(), tw.cpu().pin_memory()
+        in_host, in_dev, (h_dev, ids_dev, tw_dev) = packed_inputs(hidden, ids, tw)
         out_host = torch.empty(shape.M, shape.H, dtype=torch.bfloat16).pin_memory()
-        h_dev, ids_dev, tw_dev = torch.empty_like(hidden), torch.empty_like(ids), torch.empty_like(tw)
 
         def e2e_step():
-            h_dev.copy_(h_host, non_blocking=True)
-            ids_dev.copy_(ids_host, non_blocking=True)
-            tw_dev.copy_(tw_host, non_blocking=True)
+            in_dev.copy_(in_host, non_blocking=True)
             out_host.copy_(model(h_dev, tw_dev, ids_dev), non_blocking=True)
 
         for _ in range(args.warmup):
@@ -362,7 +381,7 @@ def run_ep(args, shape, config):
         clocks.window(t0, clocks.mark())
         ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps)
         e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": (h_host.numel() * 2 + ids_host.numel() * 4 + tw_host.numel() * 4) * ws,
+               "h2d_bytes_per_step": in_host.numel() * ws,
                "d2h_bytes_per_step": out_host.numel() * 2 * ws, "ms_per_step": ms_e2e}
     clk = clocks.stop()
     worst_active = int(max_over_ranks(local_active))
@@ -447,17 +466,11 @@ def run_ours(args, shape, config):
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        h_host = L.hidden.cpu().pin_memory()
-        ids_host = L.topk_ids.cpu().pin_memory()
-        tw_host = L.topk_weights.cpu().pin_memory()
+        in_host, in_dev, (h_dev, ids_dev, tw_dev) = packed_inputs(L.hidden, L.topk_ids, L.topk_weights)
         out_host = torch.empty(shape.M, shape.H, dtype=torch.bfloat16).pin_memory()
-        h_dev, ids_dev, tw_dev = torch.empty_like(L.hidden), torch.empty_like(L.topk_ids), \
-            torch.empty_like(L.topk_weights)
 
         def e2e_step():
-            h_dev.copy_(h_host, non_blocking=True)
-            ids_dev.copy_(ids_host, non_blocking=True)
-            tw_dev.copy_(tw_host, non_blocking=True)
+            in_dev.copy_(in_host, non_blocking=True)
             out = moe.moe_decode_megakernel_full(h_dev, L.w13, L.w13_scale, L.w2, L.w2_scale, tw_dev, ids_dev)
             out_host.copy_(out, non_blocking=True)
 
@@ -473,7 +486,7 @@ def run_ours(args, shape, config):
         barrier()
         clocks.window(t0, clocks.mark())
         ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps)
-        h2d = h_host.numel() * 2 + ids_host.numel() * 4 + tw_host.numel() * 4
+        h2d = in_host.numel()
         e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": out_host.numel() * 2, "ms_per_step": ms_e2e}
 

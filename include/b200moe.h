@@ -238,22 +238,23 @@ B200MOE_API int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int 
                   int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
                   int32_t* err_word, void* stream);
 
-/* Quantise hidden rows into the sorted layout: row p of a_q (ld = H) holds
- * q(hidden[sorted_ids[p] / topk]); scales go to a_sT[g * a_s_ld + p]
- * (transposed). Padding rows and rows p >= num_rows are not written (a padding
- * row only feeds GEMM outputs that are discarded). */
-B200MOE_API int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* sorted_ids,
-                         const int32_t* num_rows, int64_t rows_capacity, uint8_t* a_q, float* a_sT, int64_t a_s_ld,
-                         void* stream);
+/* Quantise hidden rows into the sorted layout: for every flat slot f with
+ * p = slot_pos[f] >= 0 (from b200moe_route), row p of a_q (ld = H) holds
+ * q(hidden[f / topk]) and its scales go to a_sT[g * a_s_ld + p] (transposed).
+ * Padding rows are not written (a padding row only feeds GEMM outputs that are
+ * discarded). a_s_ld >= rows_capacity. */
+B200MOE_API int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* slot_pos,
+                         int64_t rows_capacity, uint8_t* a_q, float* a_sT, int64_t a_s_ld, void* stream);
 
-/* Copy already quantised rows into the sorted layout: row p of a_q (ld = H)
- * = xq[sorted_ids[p] / topk] (row stride ldxq bytes, 16-byte aligned), its
- * scales xs[t * ldxs + g] to a_sT[g * a_s_ld + p]. Padding rows are not
- * written. With b200moe_quant_1x128 first, this is the layer's activation
- * path for large batches (each token quantised once, then copied). */
+/* Copy already quantised rows into the sorted layout: for every flat slot f
+ * with p = slot_pos[f] >= 0, row p of a_q (ld = H) = xq[f / topk] (row stride
+ * ldxq bytes, 16-byte aligned), its scales xs[t * ldxs + g] to
+ * a_sT[g * a_s_ld + p]. Padding rows are not written. With
+ * b200moe_quant_1x128 first, this is the layer's activation path for large
+ * batches (each token quantised once, then copied). */
 B200MOE_API int b200moe_gather_rows(const uint8_t* xq, const float* xs, int64_t ldxq, int64_t ldxs, int64_t M, int64_t H,
-                        int topk, const int32_t* sorted_ids, const int32_t* num_rows, int64_t rows_capacity,
-                        uint8_t* a_q, float* a_sT, int64_t a_s_ld, void* stream);
+                        int topk, const int32_t* slot_pos, int64_t rows_capacity, uint8_t* a_q, float* a_sT,
+                        int64_t a_s_ld, void* stream);
 
 /* Stage 1: inter = silu(gate) * up of (a1 . w13^T), re-quantised 1x128 into
  * a2_q (rows_capacity, I) and a2_sT (I/128, a_s_ld). grid_ctas = 0 picks one

@@ -341,11 +341,10 @@ int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts,
   return cuda_status(launch_align(a, (cudaStream_t)stream), "route");
 }
 
-int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* sorted_ids,
-                         const int32_t* num_rows, int64_t rows_capacity, uint8_t* a_q, float* a_sT, int64_t a_s_ld,
-                         void* stream) {
+int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* slot_pos,
+                         int64_t rows_capacity, uint8_t* a_q, float* a_sT, int64_t a_s_ld, void* stream) {
   if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || rows_capacity < 0 || a_s_ld < rows_capacity ||
-      (rows_capacity > 0 && (!hidden || !sorted_ids || !num_rows || !a_q || !a_sT)))
+      (M > 0 && (!hidden || !slot_pos || !a_q || !a_sT)))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_gather_quant: bad argument%s");
   if (!aligned16(hidden) || (reinterpret_cast<uintptr_t>(a_q) & 7))
     return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_gather_quant: alignment%s");
@@ -353,9 +352,8 @@ int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, con
   a.x = hidden;
   a.ldx = H;
   a.K = H;
-  a.rows = rows_capacity;
-  a.num_rows = num_rows;
-  a.sorted_ids = sorted_ids;
+  a.rows = M * topk;  // one launch row per flat slot
+  a.slot_pos = slot_pos;
   a.topk = topk;
   a.sentinel = (int32_t)(M * topk);
   a.q = a_q;
@@ -367,10 +365,10 @@ int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, con
 }
 
 int b200moe_gather_rows(const uint8_t* xq, const float* xs, int64_t ldxq, int64_t ldxs, int64_t M, int64_t H, int topk,
-                        const int32_t* sorted_ids, const int32_t* num_rows, int64_t rows_capacity, uint8_t* a_q,
-                        float* a_sT, int64_t a_s_ld, void* stream) {
+                        const int32_t* slot_pos, int64_t rows_capacity, uint8_t* a_q, float* a_sT, int64_t a_s_ld,
+                        void* stream) {
   if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || rows_capacity < 0 || a_s_ld < rows_capacity ||
-      ldxq < H || ldxs < H / 128 || (rows_capacity > 0 && (!xq || !xs || !sorted_ids || !num_rows || !a_q || !a_sT)))
+      ldxq < H || ldxs < H / 128 || (M > 0 && (!xq || !xs || !slot_pos || !a_q || !a_sT)))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_gather_rows: bad argument%s");
   if (!aligned16(xq) || ldxq % 16 != 0 || !aligned16(a_q) || H % 16 != 0)
     return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_gather_rows: fp8 rows must be 16-byte aligned%s");
@@ -380,9 +378,8 @@ int b200moe_gather_rows(const uint8_t* xq, const float* xs, int64_t ldxq, int64_
   a.xs = xs;
   a.ldxs = ldxs;
   a.K = H;
-  a.rows = rows_capacity;
-  a.num_rows = num_rows;
-  a.sorted_ids = sorted_ids;
+  a.rows = M * topk;  // one launch row per flat slot
+  a.slot_pos = slot_pos;
   a.topk = topk;
   a.sentinel = (int32_t)(M * topk);
   a.q = a_q;
@@ -573,27 +570,12 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
     src = LayerInput{nullptr, tq, H, ts, H / 128};
   }
   if (src.hidden) {
-    st = b200moe_gather_quant(in.hidden, M, H, topk, sorted, counts + 1, pl.rows_cap, a1, a1s, pl.as_ld, stream);
+    st = b200moe_gather_quant(in.hidden, M, H, topk, pos, pl.rows_cap, a1, a1s, pl.as_ld, stream);
   } else {
     if (!aligned16(src.q) || src.ldq % 16 != 0 || src.ldq < H || src.lds < H / 128 || !src.s)
       return fail(B200MOE_ERR_UNSUPPORTED, "%s: fp8 rows must be 16-byte aligned with scales per row", name);
-    QuantArgs a{};
-    a.xq = src.q;
-    a.ldxq = src.ldq;
-    a.xs = src.s;
-    a.ldxs = src.lds;
-    a.K = H;
-    a.rows = pl.rows_cap;
-    a.num_rows = counts + 1;
-    a.sorted_ids = sorted;
-    a.topk = topk;
-    a.sentinel = (int32_t)(M * topk);
-    a.q = a1;
-    a.ldq = H;
-    a.s = a1s;
-    a.s_row = 1;
-    a.s_grp = pl.as_ld;
-    st = cuda_status(launch_quant_1x128(a, (cudaStream_t)stream), "gather rows");
+    st = b200moe_gather_rows(src.q, src.s, src.ldq, src.lds, M, H, topk, pos, pl.rows_cap, a1, a1s, pl.as_ld,
+                             stream);
   }
   if (st) return st;
   st = b200moe_experts(a1, a1s, pl.as_ld, pl.rows_cap, w13, w13_scale, w2, w2_scale, E, H, I, ce, cr0, crows, counts,

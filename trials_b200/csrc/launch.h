@@ -52,6 +52,10 @@ struct QuantArgs {
   int64_t rows;            // rows (M) or the row capacity in gather mode
   const int32_t* num_rows; // gather mode: device row count
   const int32_t* sorted_ids;
+  // Slot mode (takes precedence over sorted_ids): row r of the launch is the
+  // flat slot r (rows = M*topk); it reads input row r / topk and writes output
+  // row slot_pos[r] (skipped when -1).
+  const int32_t* slot_pos;
   int topk;
   int32_t sentinel;
   uint8_t* q;

@@ -24,22 +24,41 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
   if (row >= n_rows || row >= a.rows) return;
   const int64_t seg0 = (int64_t)blockIdx.y * kQuantSegCols;
   const int64_t seg_end = seg0 + kQuantSegCols < a.K ? seg0 + kQuantSegCols : a.K;
-  int64_t src = row;
-  if (a.sorted_ids) {
+  int64_t src = row, dst = row;
+  int32_t pos = 0;
+  if (a.slot_pos) {
+    src = row / a.topk;
+    pos = __ldg(&a.slot_pos[row]);  // consumed after the row's loads are issued
+  } else if (a.sorted_ids) {
     const int f = __ldg(&a.sorted_ids[row]);
     src = (f >= 0 && f < a.sentinel) ? (int64_t)(f / a.topk) : -1;
     // Padding rows are not written: a padding row only feeds its own MMA
     // column (or row), whose results no epilogue keeps.
     if (src < 0) return;
   }
-  uint8_t* qr = a.q + row * a.ldq;
   if (a.xq != nullptr) {
     // Copy mode: the input is already quantised.
     const uint8_t* sq = a.xq + src * a.ldxq;
-    for (int64_t b = seg0 + lane * 16; b < seg_end; b += 512)
-      *reinterpret_cast<uint4*>(qr + b) = __ldg(reinterpret_cast<const uint4*>(sq + b));
+    uint4 v[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int64_t b = seg0 + lane * 16 + i * 512;
+      if (b < seg_end) v[i] = __ldg(reinterpret_cast<const uint4*>(sq + b));
+    }
     const int64_t g = (seg0 >> 7) + lane;
-    if (lane < kQuantSegCols / 128 && g * 128 < seg_end) a.s[row * a.s_row + g * a.s_grp] = __ldg(&a.xs[src * a.ldxs + g]);
+    const bool gs = lane < kQuantSegCols / 128 && g * 128 < seg_end;
+    const float sv = gs ? __ldg(&a.xs[src * a.ldxs + g]) : 0.f;
+    if (a.slot_pos) {
+      if (pos < 0) return;
+      dst = pos;
+    }
+    uint8_t* qr = a.q + dst * a.ldq;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int64_t b = seg0 + lane * 16 + i * 512;
+      if (b < seg_end) *reinterpret_cast<uint4*>(qr + b) = v[i];
+    }
+    if (gs) a.s[dst * a.s_row + g * a.s_grp] = sv;
     return;
   }
   const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
@@ -61,6 +80,11 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
       for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
     }
   }
+  if (a.slot_pos) {
+    if (pos < 0) return;
+    dst = pos;
+  }
+  uint8_t* qr = a.q + dst * a.ldq;
 #pragma unroll
   for (int i = 0; i < kQuantSegSteps; ++i) {
     if (seg0 + i * 256 >= seg_end) break;  // warp-uniform
@@ -78,7 +102,7 @@ __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const Qua
 #pragma unroll
     for (int j = 0; j < 4; ++j) hi |= (uint32_t)quant_e4m3(v[i][4 + j], scale) << (8 * j);
     *reinterpret_cast<uint2*>(qr + c) = make_uint2(lo, hi);
-    if ((lane & 15) == 0) a.s[row * a.s_row + (c >> 7) * a.s_grp] = scale;
+    if ((lane & 15) == 0) a.s[dst * a.s_row + (c >> 7) * a.s_grp] = scale;
   }
 }
 

@@ -83,8 +83,8 @@ def gather_quant(hidden: torch.Tensor, topk: int, r: Routing):
     ld = r.a_s_ld()
     a_q = torch.empty(r.rows_cap, H, dtype=FP8, device=dev)
     a_sT = torch.empty(H // 128, ld, dtype=torch.float32, device=dev)
-    _lib.check(_lib.lib().b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(r.sorted_ids), _ptr(r.num_rows),
-                                               r.rows_cap, _ptr(a_q), _ptr(a_sT), ld, _stream(dev)), "gather_quant")
+    _lib.check(_lib.lib().b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(r.slot_pos), r.rows_cap, _ptr(a_q),
+                                               _ptr(a_sT), ld, _stream(dev)), "gather_quant")
     return a_q, a_sT
 
 
@@ -97,9 +97,8 @@ def gather_rows(xq: torch.Tensor, xs: torch.Tensor, topk: int, r: Routing):
     ld = r.a_s_ld()
     a_q = torch.empty(r.rows_cap, H, dtype=FP8, device=dev)
     a_sT = torch.empty(H // 128, ld, dtype=torch.float32, device=dev)
-    _lib.check(_lib.lib().b200moe_gather_rows(_ptr(xq), _ptr(xs), H, xs.shape[1], M, H, topk, _ptr(r.sorted_ids),
-                                              _ptr(r.num_rows), r.rows_cap, _ptr(a_q), _ptr(a_sT), ld, _stream(dev)),
-               "gather_rows")
+    _lib.check(_lib.lib().b200moe_gather_rows(_ptr(xq), _ptr(xs), H, xs.shape[1], M, H, topk, _ptr(r.slot_pos),
+                                              r.rows_cap, _ptr(a_q), _ptr(a_sT), ld, _stream(dev)), "gather_rows")
     return a_q, a_sT
 
 
@@ -253,10 +252,10 @@ class LayerPipeline:
             _lib.check(L.b200moe_quant_1x128(_ptr(hidden), M, H, H, _ptr(self.tq), H, _ptr(self.ts), H // 128, 1, st),
                        "quant_1x128")
             _lib.check(L.b200moe_gather_rows(_ptr(self.tq), _ptr(self.ts), H, H // 128, M, H, topk,
-                                             _ptr(self.sorted_ids), rows, self.rows_cap, _ptr(self.a1), _ptr(self.a1s),
+                                             _ptr(self.slot_pos), self.rows_cap, _ptr(self.a1), _ptr(self.a1s),
                                              self.ld, st), "gather_rows")
         else:
-            _lib.check(L.b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(self.sorted_ids), rows, self.rows_cap,
+            _lib.check(L.b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(self.slot_pos), self.rows_cap,
                                               _ptr(self.a1), _ptr(self.a1s), self.ld, st), "gather_quant")
         rec(2)
         if not self.split:
