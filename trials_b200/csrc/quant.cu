@@ -180,6 +180,7 @@ cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K
 // router weight). pos = slot_pos[t*topk+j] (-1: slot dropped); the slot's row
 // of pair is pos (sorted_rows) or t*topk+j. One thread per 8 output columns.
 // ---------------------------------------------------------------------------
+template <int B>
 __global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __restrict__ pair,
                                                              const int32_t* __restrict__ slot_pos, int sorted_rows,
                                                              int64_t M, int topk, int64_t H,
@@ -192,14 +193,30 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __rest
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-  for (int j = 0; j < topk; ++j) {
-    const int pos = __ldg(&slot_pos[t * topk + j]);
-    if (pos < 0) continue;
-    const int64_t row = sorted_rows ? (int64_t)pos : t * topk + j;
-    const float4* src = reinterpret_cast<const float4*>(pair + row * H + c);
-    const float4 a = __ldg(src), b = __ldg(src + 1);
-    acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-    acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+  // Slots in groups of B: all positions, then all row loads of the group are
+  // issued before the sums (in slot order) consume them. B = 8 for small
+  // batches (latency-bound); B = 1 for large ones, where fewer registers per
+  // thread keep more rows in flight.
+  for (int j0 = 0; j0 < topk; j0 += B) {
+    int pos[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j) pos[j] = j0 + j < topk ? __ldg(&slot_pos[t * topk + j0 + j]) : -1;
+    float4 a[B], b[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      if (pos[j] >= 0) {
+        const int64_t row = sorted_rows ? (int64_t)pos[j] : t * topk + j0 + j;
+        const float4* src = reinterpret_cast<const float4*>(pair + row * H + c);
+        a[j] = __ldg(src);
+        b[j] = __ldg(src + 1);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      if (pos[j] < 0) continue;
+      acc[0] += a[j].x; acc[1] += a[j].y; acc[2] += a[j].z; acc[3] += a[j].w;
+      acc[4] += b[j].x; acc[5] += b[j].y; acc[6] += b[j].z; acc[7] += b[j].w;
+    }
   }
   __nv_bfloat162 o[4];
 #pragma unroll
@@ -212,8 +229,12 @@ cudaError_t launch_combine_reduce(const float* pair, const int32_t* slot_pos, in
   const int64_t n = M * (H / 8);
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = (n + 255) / 256;
-  combine_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, M, topk, H,
-                                                              reinterpret_cast<__nv_bfloat16*>(out));
+  if (M * topk <= 1024)
+    combine_reduce_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, M, topk, H,
+                                                                   reinterpret_cast<__nv_bfloat16*>(out));
+  else
+    combine_reduce_kernel<1><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, M, topk, H,
+                                                                   reinterpret_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
 
