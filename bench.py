@@ -56,6 +56,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--split", action="store_true", help="the two GEMM stages as two launches (default: one)")
+    ap.add_argument("--layer-launch", action="store_true",
+                    help="small batches: gather, experts and reduce in one launch (default: three)")
     return ap.parse_args(argv)
 
 
@@ -425,7 +427,7 @@ def run_ours(args, shape, config):
     active = synth.active_experts(L.topk_ids, shape.E)
     pairs = int(((L.topk_ids >= 0) & (L.topk_ids < shape.E)).sum().item())
     pipe = stages.LayerPipeline(shape.M, shape.H, shape.I, shape.E, shape.topk, dev, tile_tokens=args.tile,
-                                split=args.split)
+                                split=args.split, one_launch=args.layer_launch)
     args_run = (L.hidden, L.topk_ids, L.topk_weights, L.w13, L.w13_scale, L.w2, L.w2_scale)
 
     def barrier():
@@ -503,7 +505,13 @@ def run_ours(args, shape, config):
         return 0
     peak, peak_kind = measured_peaks()
     hot = f"_hot{shape.hot_experts}" if shape.hot_experts else ""
-    if "experts" in stage_ms:
+    if "layer" in stage_ms:
+        # Gather + quantise, both GEMM stages and the top-k reduce in one launch.
+        k_name, k_bytes, k_ms = "layer (gather, grouped GEMM stages, top-k reduce; one launch)", \
+            gemm1_bytes(shape, active, pairs) + gemm2_bytes(shape, active, pairs) + shape.M * shape.H * 2 * 2, \
+            stage_ms["layer"]
+        traffic_name = f"layer_glm_decode_m{shape.M}{hot}"
+    elif "experts" in stage_ms:
         # Both GEMM stages in one launch (two launches for token-major tiles).
         k_name, k_bytes, k_ms = "experts (grouped GEMM, both stages)", \
             gemm1_bytes(shape, active, pairs) + gemm2_bytes(shape, active, pairs), stage_ms["experts"]

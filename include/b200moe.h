@@ -228,7 +228,8 @@ B200MOE_API int b200moe_layer_noalloc(const void* hidden, int64_t M, int64_t H, 
  * n_chunks[1] and num_rows[1] (total padded rows) on the device. slot_pos
  * (nullable, M*topk entries) receives the sorted row of every flat slot
  * t*topk+j, or -1 for a dropped slot (for b200moe_combine_reduce). chunk_ready
- * (nullable, chunks_capacity entries) is zeroed for b200moe_experts.
+ * (nullable, chunks_capacity + 2 entries) is zeroed for b200moe_experts and
+ * b200moe_experts_fused.
  * ---------------------------------------------------------------------- */
 B200MOE_API int64_t b200moe_route_capacity_rows(int64_t numel, int num_local_experts);
 B200MOE_API int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_experts, int tile_tokens);
@@ -294,6 +295,26 @@ B200MOE_API int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t
                     int64_t chunks_capacity, int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
                     const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, float* out_pair,
                     int32_t* err_word, int grid_ctas, void* stream);
+
+/* Everything after b200moe_route for small batches (tiles of 16..64 tokens),
+ * in one persistent launch (the single-launch layer the reference deferred,
+ * phase8_findings.md:77-81): phase 0 quantises hidden[f / topk] into
+ * sorted row slot_pos[f] of a1 for every routed slot f (as
+ * b200moe_gather_quant), then both GEMM stages run as in b200moe_experts
+ * (stage-2 rows by slot in out_pair, M*topk rows), then the top-k reduce
+ * writes out (M, H) bf16 (as b200moe_combine_reduce with sorted_rows = 0).
+ * Phases are ordered by device counters after chunk_ready (zeroed by
+ * b200moe_route); results equal the separate stages bit for bit. Measured on
+ * B200: as fast as the three launches at 64 tokens, 24 us slower at 128, so
+ * b200moe_layer keeps the three launches. */
+B200MOE_API int b200moe_experts_fused(const void* hidden, int64_t M, int topk, const int32_t* slot_pos, uint8_t* a1_q,
+                          float* a1_sT, int64_t a_s_ld, int64_t rows_capacity, const uint8_t* w13,
+                          const float* w13_scale, const uint8_t* w2, const float* w2_scale, int num_local_experts,
+                          int64_t H, int64_t I, const int32_t* chunk_expert, const int32_t* chunk_row0,
+                          const int32_t* chunk_rows, const int32_t* n_chunks, int64_t chunks_capacity,
+                          int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
+                          const int32_t* sorted_ids, const float* topk_weights, float* out_pair, void* out,
+                          int32_t* err_word, int grid_ctas, void* stream);
 
 /* out[t, :] = bf16( sum_j row_j ) over the slots j with slot_pos[t*topk + j]
  * >= 0 (from b200moe_route), summed in order j = 0..topk-1; row_j is

@@ -196,6 +196,26 @@ def test_gather_and_gemm_stages(cuda_device, shape, tile):
     assert int(r.err.item()) == 0
 
 
+@pytest.mark.parametrize("shape,tile,grid", [(synth.TINY, 32, 0), (SMALL, 16, 0), (SMALL, 32, 0), (SMALL, 64, 0),
+                                             (SMALL, 32, 5), (SMALL, 64, 37), (SMALL, 32, 148)])
+def test_one_launch_layer_bit_identical(cuda_device, shape, tile, grid):
+    """Gather + quantise, both GEMM stages and the top-k reduce in one launch
+    (phases ordered by device counters) equal the separate stages bit for bit."""
+    L, g = _tiny_layer(cuda_device, shape, seed=4)
+    r = stages.route(g["topk_ids"], shape.E, tile)
+    a1_q, a1_sT = stages.gather_quant(g["hidden"], shape.topk, r)
+    _, _, pair = stages.experts(a1_q, a1_sT, g["w13"], g["w13_scale"], g["w2"], g["w2_scale"], r, g["topk_weights"])
+    ref = stages.combine_reduce(pair, r, shape.M, shape.topk)
+    r2 = stages.route(g["topk_ids"], shape.E, tile)  # fresh counters
+    out = stages.experts_fused(g["hidden"], g["w13"], g["w13_scale"], g["w2"], g["w2_scale"], r2, g["topk_weights"],
+                               grid_ctas=grid)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert int(r2.err.item()) == 0
+    nc = int(r2.counts[0].item())
+    assert (r2.chunk_ready[:nc] == 2 * shape.I // 256).all()
+
+
 @pytest.mark.parametrize("M,tile", [(16, 32), (300, 64), (600, 128)])
 def test_gather_rows_equals_gather_quant(cuda_device, M, tile):
     """Quantise each token once + copy rows (the large-batch path) gives the

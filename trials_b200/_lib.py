@@ -57,6 +57,8 @@ SIGNATURES = {
                                    _P, _P, _I, _P]),
     "b200moe_experts": (_I, [_P, _P, _L, _L, _P, _P, _P, _P, _I, _L, _L, _P, _P, _P, _P, _L, _P, _I, _P, _P, _P, _P,
                              _L, _I, _P, _P, _I, _P]),
+    "b200moe_experts_fused": (_I, [_P, _L, _I, _P, _P, _P, _L, _L, _P, _P, _P, _P, _I, _L, _L, _P, _P, _P, _P, _L,
+                                   _P, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P]),
     "b200moe_combine_reduce": (_I, [_P, _P, _I, _L, _I, _L, _P, _P]),
     "b200moe_read_error": (_I, [_P, _P, _I, _P]),
     "b200moe_selftest_wait_timeout": (_I, [_P, _I, _P]),

@@ -137,7 +137,7 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
   p.off_ce = take(sizeof(int32_t) * p.chunks_cap);
   p.off_cr0 = take(sizeof(int32_t) * p.chunks_cap);
   p.off_crows = take(sizeof(int32_t) * p.chunks_cap);
-  p.off_ready = take(sizeof(int32_t) * p.chunks_cap);
+  p.off_ready = take(sizeof(int32_t) * (p.chunks_cap + 2));
   p.off_counts = take(sizeof(int32_t) * 4);
   p.off_a1 = take((size_t)p.rows_cap * H);
   p.off_a1s = take(sizeof(float) * (size_t)(H / 128) * p.as_ld);
@@ -492,6 +492,73 @@ int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int
   return cuda_status(launch_grouped_gemm_fused(tile_tokens, tw1, ta1, p1, tw2, ta2, p2, (int)grid,
                                                (cudaStream_t)stream),
                      "experts");
+}
+
+int b200moe_experts_fused(const void* hidden, int64_t M, int topk, const int32_t* slot_pos, uint8_t* a1_q,
+                          float* a1_sT, int64_t a_s_ld, int64_t rows_capacity, const uint8_t* w13,
+                          const float* w13_scale, const uint8_t* w2, const float* w2_scale, int num_local_experts,
+                          int64_t H, int64_t I, const int32_t* chunk_expert, const int32_t* chunk_row0,
+                          const int32_t* chunk_rows, const int32_t* n_chunks, int64_t chunks_capacity,
+                          int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
+                          const int32_t* sorted_ids, const float* topk_weights, float* out_pair, void* out,
+                          int32_t* err_word, int grid_ctas, void* stream) {
+  int st = check_gemm_shapes(H, I);
+  if (st) return st;
+  if (tile_tokens > 64)
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_experts_fused: tiles of 16..64 tokens only%s");
+  if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 || M <= 0 || topk <= 0 ||
+      a_s_ld < rows_capacity + (tile_tokens < 32 ? 32 : tile_tokens) || a_s_ld % 4 != 0 || !hidden || !slot_pos ||
+      !a1_q || !a1_sT || !w13 || !w13_scale || !w2 || !w2_scale || !chunk_expert || !chunk_row0 || !chunk_rows ||
+      !n_chunks || !chunk_ready || !a2_q || !a2_sT || !sorted_ids || !topk_weights || !out_pair || !out ||
+      !err_word)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_experts_fused: bad argument%s");
+  if (!aligned16(hidden) || !aligned16(a1_q) || !aligned16(w13) || !aligned16(a1_sT) || !aligned16(a2_q) ||
+      !aligned16(w2) || !aligned16(a2_sT) || !aligned16(out_pair) || !aligned16(out))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_experts_fused: 16-byte alignment required%s");
+  GemmParams p1{}, p2{};
+  CUtensorMap tw1, ta1, tw2, ta2;
+  st = prep_gemm(a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, 2 * I, H, chunk_expert,
+                 chunk_row0, chunk_rows, n_chunks, tile_tokens, p1, tw1, ta1);
+  if (st) return st;
+  st = prep_gemm(a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I, chunk_expert, chunk_row0,
+                 chunk_rows, n_chunks, tile_tokens, p2, tw2, ta2);
+  if (st) return st;
+  p1.out_q = a2_q;
+  p1.out_q_ld = I;
+  p1.out_sT = a2_sT;
+  p1.out_s_ld = a_s_ld;
+  p1.chunk_ready = chunk_ready;
+  p1.phase_count = chunk_ready + chunks_capacity;
+  p1.err = err_word;
+  // phase 0: quantise each routed slot's hidden row into its sorted row
+  p1.q0.x = hidden;
+  p1.q0.ldx = H;
+  p1.q0.K = H;
+  p1.q0.rows = M * topk;
+  p1.q0.slot_pos = slot_pos;
+  p1.q0.topk = topk;
+  p1.q0.sentinel = (int32_t)(M * topk);
+  p1.q0.q = a1_q;
+  p1.q0.ldq = H;
+  p1.q0.s = a1_sT;
+  p1.q0.s_row = 1;
+  p1.q0.s_grp = a_s_ld;
+  // last phase: top-k reduce of the slot rows
+  p1.red_slot_pos = slot_pos;
+  p1.red_out = static_cast<__nv_bfloat16*>(out);
+  p1.red_M = M;
+  p1.red_topk = topk;
+  p2.sorted_ids = sorted_ids;
+  p2.topk_w = topk_weights;
+  p2.sentinel = (int32_t)(M * topk);
+  p2.out_pair = out_pair;
+  p2.err = err_word;
+  const int64_t units_cap = chunks_capacity * ((2 * I) / 256 + H / 256);
+  int64_t grid = grid_ctas > 0 ? grid_ctas : sm_count();
+  if (grid > units_cap) grid = units_cap;
+  return cuda_status(launch_grouped_gemm_fused(tile_tokens, tw1, ta1, p1, tw2, ta2, p2, (int)grid,
+                                               (cudaStream_t)stream),
+                     "experts_fused");
 }
 
 int b200moe_combine_reduce(const float* out_pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,

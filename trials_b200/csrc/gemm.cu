@@ -27,7 +27,7 @@ cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const G
   auto kernel = moe_grouped_gemm_kernel<T, CS, EPI>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (err != cudaSuccess) return err;
-  if (EPI != EPI_FUSED) {
+  if (EPI < EPI_FUSED) {
     kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_a, p, tm_w2, tm_a2, p2);
     return cudaGetLastError();
   }
@@ -133,12 +133,15 @@ cudaError_t launch_grouped_gemm_fused(int tile_tokens, const CUtensorMap& tm_w1,
                                       const GemmParams& p1, const CUtensorMap& tm_w2, const CUtensorMap& tm_a2,
                                       const GemmParams& p2, int grid, cudaStream_t stream) {
   if (grid <= 0) return cudaSuccess;
+  const bool phases = p1.q0.rows > 0;
   switch (tile_tokens) {
     case 16:
     case 32:
-      return launch_cfg<32, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
+      return phases ? launch_cfg<32, 1, EPI_LAYER>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream)
+                    : launch_cfg<32, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
     case 64:
-      return launch_cfg<64, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
+      return phases ? launch_cfg<64, 1, EPI_LAYER>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream)
+                    : launch_cfg<64, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }

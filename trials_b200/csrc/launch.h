@@ -28,7 +28,7 @@ struct AlignArgs {
   int32_t* chunk_rows;
   int64_t chunks_cap;
   int32_t* n_chunks;
-  int32_t* chunk_ready;    // nullable: zeroed over chunks_cap entries
+  int32_t* chunk_ready;    // nullable: zeroed over chunks_cap + 2 entries
   int32_t* slot_pos;       // nullable: sorted position of each flat slot (n entries), -1 if dropped
   int32_t* err;
 };

@@ -36,7 +36,9 @@
 #include <cuda_fp8.h>
 
 #include "common.cuh"
+#include "launch.h"
 #include "ptx.cuh"
+#include "rowops.cuh"
 
 // Weight tiles stream once per launch. An evict_first L2 hint on them measured
 // slower than no hint on a pure TMA read stream (6.9 vs 7.0 TB/s) and no faster
@@ -58,7 +60,9 @@
 
 namespace b200moe {
 
-enum { EPI_SILU = 0, EPI_COMBINE = 1, EPI_FUSED = 2 };
+// EPI_LAYER: EPI_FUSED plus the in-launch phases (gather + quantise first,
+// top-k reduce last) set up in GemmParams.q0 / red_*.
+enum { EPI_SILU = 0, EPI_COMBINE = 1, EPI_FUSED = 2, EPI_LAYER = 3 };
 
 struct GemmParams {
   // routing: chunk list produced by the route kernel (device memory)
@@ -83,8 +87,18 @@ struct GemmParams {
   const float* topk_w;
   int32_t sentinel;   // M * topk
   float* out_pair;    // fp32 rows of Nw: row f = slot (tiles <= 64) or sorted row p (tiles >= 128)
-  // EPI_FUSED: per-chunk count of finished stage-1 units (zeroed by routing)
+  // EPI_FUSED: per-chunk count of finished stage-1 units (zeroed by routing),
+  // followed by two phase counters (CTAs done with phase 0 / with all units)
   int32_t* chunk_ready;
+  int32_t* phase_count;
+  // EPI_FUSED, small batches: activation gather + quantisation as phase 0 of
+  // the launch (q0.rows > 0, slot mode) and the top-k reduce as its last phase
+  // (red_out != nullptr; stage-2 rows by slot, red_slot_pos from routing).
+  QuantArgs q0;
+  const int32_t* red_slot_pos;
+  __nv_bfloat16* red_out;
+  int64_t red_M;
+  int red_topk;
   // unit order: chunks per group (see unit_coords); 1 = chunk-major
   int chunk_group;
   // diagnostics
@@ -207,13 +221,14 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
 // stage-1 unit through an mbarrier, and its GPU-scope fence (which waits for
 // the stores to land) stays off the epilogue's path.
 template <int T, int CS, int EPI>
-__global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 32 : 0), 1)
+__global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 32 : 0), 1)
     moe_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                             const __grid_constant__ GemmParams p, const __grid_constant__ CUtensorMap tm_w2,
                             const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ GemmParams p2) {
   using C = GemmCfg<T, CS>;
   constexpr int EW = C::EW;
-  constexpr bool FUSED = EPI == EPI_FUSED;
+  constexpr bool FUSED = EPI == EPI_FUSED || EPI == EPI_LAYER;
+  constexpr bool PHASES = EPI == EPI_LAYER;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled TMA tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -309,6 +324,27 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
         p0_n = __ldg(&p.chunk_row0[c]);
       };
       if (blockIdx.x < n_units) meta(blockIdx.x);
+      // With phase 0 in the launch (EPI_FUSED, q0.rows > 0) the stage-1
+      // activation rows are written by the epilogue warps of every CTA first:
+      // until all CTAs are done, stage-1 tiles get only their weight half, and
+      // the activation halves and scales of up to NSTAGE stages wait here.
+      bool a_ready = !PHASES;
+      int np = 0;
+      int pst[C::NSTAGE], psl[C::NSTAGE], pkb[C::NSTAGE], pp0[C::NSTAGE];
+      auto flush = [&]() -> bool {
+        const bool got = wait_count_bounded(p.phase_count, (int)gridDim.x, p.timeout_ns, abort_flag);
+        // Issued even after a timeout, so that every barrier they feed completes
+        // (the error word then marks the results).
+        for (int i = 0; i < np; ++i) {
+          tma_load_2d(tiles + pst[i] * C::TILE_BYTES + C::W_BYTES, &tm_a, &full[pst[i]], pkb[i] * 128, pp0[i],
+                      pol_a);
+          mbar_arrive_expect_tx(&sfull[psl[i]], C::S_BYTES);
+          bulk_load(sscale + psl[i] * T, p.a_sT + (int64_t)pkb[i] * p.as_ld + pp0[i], C::S_BYTES, &sfull[psl[i]]);
+        }
+        np = 0;
+        a_ready = true;
+        return got;
+      };
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         bool s2;
         int chunk, nt;
@@ -320,6 +356,10 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
         const CUtensorMap* ta = s2 ? &tm_a2 : &tm_a;
         const int NKB = s2 ? NKB2 : NKB1;
         const int wrow = e * q.Nw + nt * C::UNIT_ROWS;
+        if (FUSED && s2 && !a_ready && !flush()) {
+          ok = false;
+          break;
+        }
         if (FUSED && s2 && !wait_count_bounded(p.chunk_ready + chunk, NT1, p.timeout_ns, abort_flag)) {
           ok = false;
           break;
@@ -337,9 +377,17 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
 #else
           tma_load_2d(tile, tw, &full[stage], kb * 128, wrow);
 #endif
-          tma_load_2d(tile + C::W_BYTES, ta, &full[stage], kb * 128, p0, pol_a);
-          mbar_arrive_expect_tx(&sfull[slot], C::S_BYTES);
-          bulk_load(sscale + slot * T, q.a_sT + (int64_t)kb * q.as_ld + p0, C::S_BYTES, &sfull[slot]);
+          if (a_ready) {
+            tma_load_2d(tile + C::W_BYTES, ta, &full[stage], kb * 128, p0, pol_a);
+            mbar_arrive_expect_tx(&sfull[slot], C::S_BYTES);
+            bulk_load(sscale + slot * T, q.a_sT + (int64_t)kb * q.as_ld + p0, C::S_BYTES, &sfull[slot]);
+          } else {
+            pst[np] = stage;
+            psl[np] = slot;
+            pkb[np] = kb;
+            pp0[np] = p0;
+            ++np;
+          }
           ++issued;
           if (++stage == C::NSTAGE) {
             stage = 0;
@@ -349,8 +397,13 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
             slot = 0;
             sphase ^= 1;
           }
+          if (np == C::NSTAGE && !flush()) {
+            ok = false;
+            break;
+          }
         }
       }
+      if (np > 0 && !flush()) ok = false;
       if (!ok) {
         atomicOr(p.err, ERR_DEV_TIMEOUT);
         *abort_flag = 1;
@@ -455,6 +508,22 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
       wl1 = lane + 32 < nkb ? __ldg(w + lane + 32) : 0.f;
     };
     int n_pub = 0;  // stage-1 units handed to the publisher (EPI_FUSED)
+    const int tid = threadIdx.x - 64;  // 0 .. EW*32-1
+    if (PHASES) {
+      // Phase 0: gather + quantise the routed rows (one warp per routed slot
+      // and 1024-column segment, strided over every epilogue warp of the
+      // grid), then count this CTA done. The producer's first activation loads
+      // wait for every CTA; its weight loads are already in flight.
+      const int nseg = (int)((p.q0.K + kQuantSegCols - 1) / kQuantSegCols);
+      const int64_t ntask = p.q0.rows * nseg;
+      for (int64_t t = (int64_t)blockIdx.x * EW + ew; t < ntask; t += (int64_t)gridDim.x * EW)
+        quant_row_segment(p.q0, t / nseg, (t % nseg) * kQuantSegCols, lane);
+      named_bar_sync(1, EW * 32);
+      if (tid == 0) {
+        __threadfence();
+        atomicAdd(p.phase_count, 1);
+      }
+    }
     if (blockIdx.x < n_units) {
       bool s2;
       int c, nt;
@@ -593,7 +662,6 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
 #pragma unroll
         for (int g = 0; g < NG; ++g)
           if (g < live) red[(hs * 4 + q) * T + col0 + g * 32 + lane] = warp_pair_transpose_max(v + g * 16, lane);
-        const int tid = threadIdx.x - 64;
         if (tid == 0) *stop_sh = *abort_flag;
         named_bar_sync(1, EW * 32);
         // The previous read of stop_sh happened before this unit's second
@@ -659,6 +727,33 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI == EPI_FUSED ? 
             const float w = __shfl_sync(0xffffffffu, wl[j / 32], j % 32);
             if (f < pc.sentinel) dst[(int64_t)f * pc.Nw] = w * acc[j];
           }
+        }
+      }
+    }
+    if (PHASES) {
+      // Last phase: the top-k reduce, once every CTA has stored all its
+      // stage-2 rows (each CTA counts itself after its epilogue warps' last
+      // stores; the fence of that thread orders them all, as in phase 0).
+      named_bar_sync(1, EW * 32);
+      if (tid == 0) {
+        bool go = *abort_flag == 0;
+        __threadfence();
+        atomicAdd(p.phase_count + 1, 1);
+        if (go) go = wait_count_bounded(p.phase_count + 1, (int)gridDim.x, p.timeout_ns, abort_flag);
+        if (!go && *abort_flag == 0) {
+          atomicOr(p.err, ERR_DEV_TIMEOUT);
+          *abort_flag = 1;
+        }
+        *stop_sh = go ? 0 : 1;
+      }
+      named_bar_sync(1, EW * 32);
+      if (*stop_sh == 0) {
+        const int64_t per_row = p2.Nw / 8;
+        const int64_t n = p.red_M * per_row;
+        for (int64_t i = (int64_t)blockIdx.x * (EW * 32) + tid; i < n; i += (int64_t)gridDim.x * (EW * 32)) {
+          const int64_t t = i / per_row;
+          reduce_token_cols<4>(p2.out_pair, p.red_slot_pos, 0, p.red_topk, p2.Nw, t, (i - t * per_row) * 8,
+                               p.red_out);
         }
       }
     }

@@ -2,6 +2,7 @@
 #include "common.cuh"
 #include "launch.h"
 #include "ptx.cuh"
+#include "rowops.cuh"
 
 namespace b200moe {
 
@@ -14,96 +15,13 @@ namespace b200moe {
 // one load round trip rather than K/256 of them.
 // ---------------------------------------------------------------------------
 constexpr int kQuantWarps = 8;
-constexpr int kQuantSegSteps = 4;
-constexpr int kQuantSegCols = 256 * kQuantSegSteps;
 
 __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const QuantArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
   const int64_t n_rows = a.num_rows ? (int64_t)(*a.num_rows) : a.rows;
   if (row >= n_rows || row >= a.rows) return;
-  const int64_t seg0 = (int64_t)blockIdx.y * kQuantSegCols;
-  const int64_t seg_end = seg0 + kQuantSegCols < a.K ? seg0 + kQuantSegCols : a.K;
-  int64_t src = row, dst = row;
-  int32_t pos = 0;
-  if (a.slot_pos) {
-    src = row / a.topk;
-    pos = __ldg(&a.slot_pos[row]);  // consumed after the row's loads are issued
-  } else if (a.sorted_ids) {
-    const int f = __ldg(&a.sorted_ids[row]);
-    src = (f >= 0 && f < a.sentinel) ? (int64_t)(f / a.topk) : -1;
-    // Padding rows are not written: a padding row only feeds its own MMA
-    // column (or row), whose results no epilogue keeps.
-    if (src < 0) return;
-  }
-  if (a.xq != nullptr) {
-    // Copy mode: the input is already quantised.
-    const uint8_t* sq = a.xq + src * a.ldxq;
-    uint4 v[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int64_t b = seg0 + lane * 16 + i * 512;
-      if (b < seg_end) v[i] = __ldg(reinterpret_cast<const uint4*>(sq + b));
-    }
-    const int64_t g = (seg0 >> 7) + lane;
-    const bool gs = lane < kQuantSegCols / 128 && g * 128 < seg_end;
-    const float sv = gs ? __ldg(&a.xs[src * a.ldxs + g]) : 0.f;
-    if (a.slot_pos) {
-      if (pos < 0) return;
-      dst = pos;
-    }
-    uint8_t* qr = a.q + dst * a.ldq;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int64_t b = seg0 + lane * 16 + i * 512;
-      if (b < seg_end) *reinterpret_cast<uint4*>(qr + b) = v[i];
-    }
-    if (gs) a.s[dst * a.s_row + g * a.s_grp] = sv;
-    return;
-  }
-  const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
-  float v[kQuantSegSteps][8];
-#pragma unroll
-  for (int i = 0; i < kQuantSegSteps; ++i) {
-    const int64_t c = seg0 + i * 256 + lane * 8;
-    if (c < seg_end) {
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + c));
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f2 = __bfloat1622float2(h2[j]);
-        v[i][2 * j] = f2.x;
-        v[i][2 * j + 1] = f2.y;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
-    }
-  }
-  if (a.slot_pos) {
-    if (pos < 0) return;
-    dst = pos;
-  }
-  uint8_t* qr = a.q + dst * a.ldq;
-#pragma unroll
-  for (int i = 0; i < kQuantSegSteps; ++i) {
-    if (seg0 + i * 256 >= seg_end) break;  // warp-uniform
-    const int64_t c = seg0 + i * 256 + lane * 8;
-    float m = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
-#pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (c >= seg_end) continue;
-    uint32_t lo = 0, hi = 0;
-    const float scale = group_scale(m);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) lo |= (uint32_t)quant_e4m3(v[i][j], scale) << (8 * j);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) hi |= (uint32_t)quant_e4m3(v[i][4 + j], scale) << (8 * j);
-    *reinterpret_cast<uint2*>(qr + c) = make_uint2(lo, hi);
-    if ((lane & 15) == 0) a.s[dst * a.s_row + (c >> 7) * a.s_grp] = scale;
-  }
+  quant_row_segment(a, row, (int64_t)blockIdx.y * kQuantSegCols, lane);
 }
 
 cudaError_t launch_quant_1x128(const QuantArgs& a, cudaStream_t stream) {
@@ -189,39 +107,7 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __rest
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t t = idx / per_row;
   if (t >= M) return;
-  const int64_t c = (idx - t * per_row) * 8;
-  float acc[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-  // Slots in groups of B: all positions, then all row loads of the group are
-  // issued before the sums (in slot order) consume them. B = 8 for small
-  // batches (latency-bound); B = 1 for large ones, where fewer registers per
-  // thread keep more rows in flight.
-  for (int j0 = 0; j0 < topk; j0 += B) {
-    int pos[B];
-#pragma unroll
-    for (int j = 0; j < B; ++j) pos[j] = j0 + j < topk ? __ldg(&slot_pos[t * topk + j0 + j]) : -1;
-    float4 a[B], b[B];
-#pragma unroll
-    for (int j = 0; j < B; ++j) {
-      if (pos[j] >= 0) {
-        const int64_t row = sorted_rows ? (int64_t)pos[j] : t * topk + j0 + j;
-        const float4* src = reinterpret_cast<const float4*>(pair + row * H + c);
-        a[j] = __ldg(src);
-        b[j] = __ldg(src + 1);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < B; ++j) {
-      if (pos[j] < 0) continue;
-      acc[0] += a[j].x; acc[1] += a[j].y; acc[2] += a[j].z; acc[3] += a[j].w;
-      acc[4] += b[j].x; acc[5] += b[j].y; acc[6] += b[j].z; acc[7] += b[j].w;
-    }
-  }
-  __nv_bfloat162 o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-  *reinterpret_cast<uint4*>(out + t * H + c) = *reinterpret_cast<const uint4*>(o);
+  reduce_token_cols<B>(pair, slot_pos, sorted_rows, topk, H, t, (idx - t * per_row) * 8, out);
 }
 
 cudaError_t launch_combine_reduce(const float* pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,

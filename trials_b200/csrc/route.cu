@@ -78,8 +78,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
   int32_t* padded = base + E + 1;           // [E]
   int32_t* chbase = padded + E;             // [E + 1] chunk offsets
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (a.chunk_ready)
-    for (int64_t i = tid; i < a.chunks_cap; i += kRouteThreads) a.chunk_ready[i] = 0;
+  if (a.chunk_ready)  // per-chunk counters and the two phase counters after them
+    for (int64_t i = tid; i < a.chunks_cap + 2; i += kRouteThreads) a.chunk_ready[i] = 0;
 
   for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) cnt[i] = 0;
   __syncthreads();

@@ -1,0 +1,142 @@
+// Per-row device routines shared by the stand-alone kernels (quant.cu) and
+// the fused experts launch (moe_gemm.cuh): 1x128 quantisation / row copy of
+// one (row, 1024-column segment) by one warp, and the top-k reduce of eight
+// output columns of one token by one thread.
+#pragma once
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace b200moe {
+
+constexpr int kQuantSegSteps = 4;
+constexpr int kQuantSegCols = 256 * kQuantSegSteps;
+
+// One warp: launch row `row` of `a` (see QuantArgs), columns seg0 .. seg0+1023.
+// Each lane converts 8 consecutive bf16 per 16-byte load, a half-warp covers
+// one 128-column group, and the warp issues the loads of its four 256-column
+// steps before it reduces any of them (one load round trip per row).
+__device__ __forceinline__ void quant_row_segment(const QuantArgs& a, int64_t row, int64_t seg0, int lane) {
+  const int64_t seg_end = seg0 + kQuantSegCols < a.K ? seg0 + kQuantSegCols : a.K;
+  int64_t src = row, dst = row;
+  int32_t pos = 0;
+  if (a.slot_pos) {
+    src = row / a.topk;
+    pos = __ldg(&a.slot_pos[row]);  // consumed after the row's loads are issued
+  } else if (a.sorted_ids) {
+    const int f = __ldg(&a.sorted_ids[row]);
+    src = (f >= 0 && f < a.sentinel) ? (int64_t)(f / a.topk) : -1;
+    // Padding rows are not written: a padding row only feeds its own MMA
+    // column (or row), whose results no epilogue keeps.
+    if (src < 0) return;
+  }
+  if (a.xq != nullptr) {
+    // Copy mode: the input is already quantised.
+    const uint8_t* sq = a.xq + src * a.ldxq;
+    uint4 v[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int64_t b = seg0 + lane * 16 + i * 512;
+      if (b < seg_end) v[i] = __ldg(reinterpret_cast<const uint4*>(sq + b));
+    }
+    const int64_t g = (seg0 >> 7) + lane;
+    const bool gs = lane < kQuantSegCols / 128 && g * 128 < seg_end;
+    const float sv = gs ? __ldg(&a.xs[src * a.ldxs + g]) : 0.f;
+    if (a.slot_pos) {
+      if (pos < 0) return;
+      dst = pos;
+    }
+    uint8_t* qr = a.q + dst * a.ldq;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int64_t b = seg0 + lane * 16 + i * 512;
+      if (b < seg_end) *reinterpret_cast<uint4*>(qr + b) = v[i];
+    }
+    if (gs) a.s[dst * a.s_row + g * a.s_grp] = sv;
+    return;
+  }
+  const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
+  float v[kQuantSegSteps][8];
+#pragma unroll
+  for (int i = 0; i < kQuantSegSteps; ++i) {
+    const int64_t c = seg0 + i * 256 + lane * 8;
+    if (c < seg_end) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + c));
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f2 = __bfloat1622float2(h2[j]);
+        v[i][2 * j] = f2.x;
+        v[i][2 * j + 1] = f2.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+    }
+  }
+  if (a.slot_pos) {
+    if (pos < 0) return;
+    dst = pos;
+  }
+  uint8_t* qr = a.q + dst * a.ldq;
+#pragma unroll
+  for (int i = 0; i < kQuantSegSteps; ++i) {
+    if (seg0 + i * 256 >= seg_end) break;  // warp-uniform
+    const int64_t c = seg0 + i * 256 + lane * 8;
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (c >= seg_end) continue;
+    uint32_t lo = 0, hi = 0;
+    const float scale = group_scale(m);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) lo |= (uint32_t)quant_e4m3(v[i][j], scale) << (8 * j);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) hi |= (uint32_t)quant_e4m3(v[i][4 + j], scale) << (8 * j);
+    *reinterpret_cast<uint2*>(qr + c) = make_uint2(lo, hi);
+    if ((lane & 15) == 0) a.s[dst * a.s_row + (c >> 7) * a.s_grp] = scale;
+  }
+}
+
+// One thread: out[t, c .. c+7] = bf16(sum over the routed slots j of the
+// slot's stage-2 row), slots summed in order j. pos = slot_pos[t*topk + j]
+// (-1: dropped); the row is pos (sorted_rows) or t*topk + j. Slots in groups of
+// B: all positions, then all row loads of the group are issued before the
+// sums consume them. Loads go through L2 (the rows may have been written by
+// other CTAs of the same launch).
+template <int B>
+__device__ __forceinline__ void reduce_token_cols(const float* pair, const int32_t* slot_pos, int sorted_rows,
+                                                  int topk, int64_t H, int64_t t, int64_t c, __nv_bfloat16* out) {
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int j0 = 0; j0 < topk; j0 += B) {
+    int pos[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j) pos[j] = j0 + j < topk ? __ldcg(&slot_pos[t * topk + j0 + j]) : -1;
+    float4 x[B], y[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      if (pos[j] >= 0) {
+        const int64_t row = sorted_rows ? (int64_t)pos[j] : t * topk + j0 + j;
+        const float4* src = reinterpret_cast<const float4*>(pair + row * H + c);
+        x[j] = __ldcg(src);
+        y[j] = __ldcg(src + 1);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      if (pos[j] < 0) continue;
+      acc[0] += x[j].x; acc[1] += x[j].y; acc[2] += x[j].z; acc[3] += x[j].w;
+      acc[4] += y[j].x; acc[5] += y[j].y; acc[6] += y[j].z; acc[7] += y[j].w;
+    }
+  }
+  __nv_bfloat162 o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+  *reinterpret_cast<uint4*>(out + t * H + c) = *reinterpret_cast<const uint4*>(o);
+}
+
+}  // namespace b200moe

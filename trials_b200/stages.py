@@ -30,7 +30,7 @@ class Routing:
     chunk_rows: torch.Tensor
     counts: torch.Tensor        # [n_chunks, num_rows] int32
     err: torch.Tensor           # (1,) int32
-    chunk_ready: torch.Tensor   # (chunks_cap,) int32, zeroed by route for experts()
+    chunk_ready: torch.Tensor   # (chunks_cap + 2,) int32, zeroed by route for experts()
     slot_pos: torch.Tensor      # (M*topk,) int32: sorted row of each flat slot, -1 if dropped
 
     @property
@@ -65,7 +65,7 @@ def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map
     z = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=dev)  # noqa: E731
     r = Routing(tile_tokens, rows_cap, chunks_cap, z(rows_cap), z(chunks_cap), z(chunks_cap), z(chunks_cap),
                 torch.zeros(2, dtype=torch.int32, device=dev),
-                err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev), z(chunks_cap), z(M * topk))
+                err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev), z(chunks_cap + 2), z(M * topk))
     if expert_map is not None:
         expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
     _lib.check(L.b200moe_route(_ptr(ids), M, topk, num_experts, _ptr(expert_map), E, tile_tokens,
@@ -158,6 +158,34 @@ def experts(a1_q, a1_sT, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights:
     return a2_q, a2_sT, out_pair
 
 
+def experts_fused(hidden, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights: torch.Tensor,
+                  grid_ctas: int = 0) -> torch.Tensor:
+    """Gather + quantise, both GEMM stages and the top-k reduce in one launch
+    (tiles of 16..64 tokens) -> out (M, H) bf16, the same values as
+    gather_quant, experts and combine_reduce. Needs the counters zeroed by
+    route() for this routing."""
+    dev = _require_cuda(hidden, w13, w2)
+    hidden = hidden.contiguous()
+    E, N2, H = w13.shape
+    I = N2 // 2
+    M, topk = topk_weights.shape
+    ld = r.a_s_ld()
+    a1_q = torch.empty(r.rows_cap, H, dtype=FP8, device=dev)
+    a1_sT = torch.empty(H // 128, ld, dtype=torch.float32, device=dev)
+    a2_q = torch.zeros(r.rows_cap, I, dtype=FP8, device=dev)
+    a2_sT = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
+    out_pair = torch.zeros(M * topk, H, dtype=torch.float32, device=dev)
+    out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    tw = topk_weights.to(torch.float32).contiguous()
+    _lib.check(_lib.lib().b200moe_experts_fused(
+        _ptr(hidden), M, topk, _ptr(r.slot_pos), _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13),
+        _ptr(w13_scale.contiguous()), _ptr(w2), _ptr(w2_scale.contiguous()), E, H, I, _ptr(r.chunk_expert),
+        _ptr(r.chunk_row0), _ptr(r.chunk_rows), _ptr(r.n_chunks), r.chunks_cap, _ptr(r.chunk_ready), r.tile_tokens,
+        _ptr(a2_q), _ptr(a2_sT), _ptr(r.sorted_ids), _ptr(tw), _ptr(out_pair), _ptr(out), _ptr(r.err), grid_ctas,
+        _stream(dev)), "experts_fused")
+    return out
+
+
 def combine_reduce(out_pair: torch.Tensor, r: Routing, M: int, topk: int) -> torch.Tensor:
     """out[t] = bf16(sum over the routed slots j of the slot's stage-2 row)."""
     dev = _require_cuda(out_pair)
@@ -195,12 +223,13 @@ class LayerPipeline:
     gather_quant, experts (both GEMM stages in one launch), combine_reduce;
     with split=True the GEMM stages run as two launches instead."""
 
+    LAYER_STAGES = ("route", "layer")  # small batches: everything after routing in one launch
     FUSED_STAGES = ("route", "gather_quant", "experts", "combine_reduce")
     SPLIT_STAGES = ("route", "gather_quant", "gemm1_silu", "gemm2_combine", "combine_reduce")
 
     def __init__(self, M: int, H: int, I: int, num_experts: int, topk: int, device, tile_tokens: int = 0,
                  expert_map: Optional[torch.Tensor] = None, num_local_experts: Optional[int] = None,
-                 split: bool = False):
+                 split: bool = False, one_launch: Optional[bool] = None):
         self.M, self.H, self.I, self.topk = M, H, I, topk
         self.num_experts = num_experts
         self.E = num_local_experts if expert_map is not None else num_experts
@@ -215,10 +244,14 @@ class LayerPipeline:
         z = lambda n: torch.zeros(max(n, 1), dtype=torch.int32, device=device)  # noqa: E731
         self.sorted_ids, self.ce, self.cr0, self.crows = z(self.rows_cap), z(self.chunks_cap), z(self.chunks_cap), \
             z(self.chunks_cap)
-        self.ready = z(self.chunks_cap)
+        self.ready = z(self.chunks_cap + 2)
         self.slot_pos = z(numel)
         self.split = split
-        self.stages = self.SPLIT_STAGES if split else self.FUSED_STAGES
+        # One launch after routing (b200moe_experts_fused) on request: measured
+        # equal at 64 tokens and 24 us slower at 128 than the three launches.
+        eligible = (not split) and self.tile <= 64 and M * topk < TOKEN_QUANT_MIN_PAIRS
+        self.one_launch = bool(one_launch) and eligible
+        self.stages = self.SPLIT_STAGES if split else (self.LAYER_STAGES if self.one_launch else self.FUSED_STAGES)
         self.counts = z(2)
         self.err = z(1)
         self.a1 = torch.zeros(self.rows_cap, H, dtype=FP8, device=device)
@@ -248,6 +281,16 @@ class LayerPipeline:
                                    _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.slot_pos),
                                    _ptr(self.ready), _ptr(self.err), st), "route")
         rec(1)
+        if self.one_launch:
+            _lib.check(L.b200moe_experts_fused(_ptr(hidden), M, topk, _ptr(self.slot_pos), _ptr(self.a1), _ptr(self.a1s),
+                                               self.ld, self.rows_cap, _ptr(w13), _ptr(w13_scale), _ptr(w2),
+                                               _ptr(w2_scale), E, H, I, _ptr(self.ce), _ptr(self.cr0), _ptr(self.crows),
+                                               cnt, self.chunks_cap, _ptr(self.ready), self.tile, _ptr(self.a2),
+                                               _ptr(self.a2s), _ptr(self.sorted_ids), _ptr(topk_weights),
+                                               _ptr(self.pair), _ptr(self.out), _ptr(self.err), grid_ctas, st),
+                       "experts_fused")
+            rec(2)
+            return self.out
         if self.token_quant:
             _lib.check(L.b200moe_quant_1x128(_ptr(hidden), M, H, H, _ptr(self.tq), H, _ptr(self.ts), H // 128, 1, st),
                        "quant_1x128")
