@@ -55,6 +55,8 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-sample-experts", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: tokens exchanged by the kernels through peer memory, or by NCCL all-to-alls")
     ap.add_argument("--split", action="store_true", help="the two GEMM stages as two launches (default: one)")
     ap.add_argument("--layer-launch", action="store_true",
                     help="small batches: gather, experts and reduce in one launch (default: three)")
@@ -318,7 +320,7 @@ def run_ep(args, shape, config):
     shards = [ep.shard_experts(t, rank, ws) for t in (L.w13, L.w13_scale, L.w2, L.w2_scale)]
     del L
     torch.cuda.empty_cache()
-    model = ep.ExpertParallelMoE(*shards, num_experts=shape.E, rows_per_rank=shape.M)
+    model = ep.ExpertParallelMoE(*shards, num_experts=shape.E, rows_per_rank=shape.M, exchange=args.exchange)
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed + 1000 + rank)
     logits = torch.randn(shape.M, shape.E, generator=g, device=dev)
@@ -402,7 +404,9 @@ def run_ep(args, shape, config):
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": f"{peak_kind} HBM copy bandwidth",
                          "algorithmic_bytes_per_launch": wbytes, "traffic": None},
-            "gpu_launches": 10 * args.steps,
+            # quant, plan, pack, unpack, route, gather, experts, reduce, combine (+ the flag wait of the
+            # peer exchange); the NCCL exchange adds its own all-to-all kernels
+            "gpu_launches": (10 if args.exchange == "peer" else 9) * args.steps,
             "clocks": clk,
         }
         if e2e is not None:
@@ -410,6 +414,7 @@ def run_ep(args, shape, config):
         if errs:
             line["device_errors"] = errs
         print(json.dumps(line), flush=True)
+    model.close()
     dist.destroy_process_group()
     return 0
 
@@ -575,8 +580,9 @@ def main(argv=None):
               "quant": "e4m3 weights with fp32 128x128 block scales, 1x128 activation scales",
               "l2": "no flush: each step streams the active experts' fp8 weights (8.4-9.7 GB) >> 126 MB L2",
               "parallelism": "single GPU" if ws == 1 else
-              f"expert parallel over {ws} GPUs: {shape.E // ws} experts and {shape.M} tokens per GPU, "
-              "NCCL all-to-all dispatch and combine"}
+              f"expert parallel over {ws} GPUs: {shape.E // ws} experts and {shape.M} tokens per GPU, " +
+              ("dispatch and combine stored by the kernels into peer memory over NVLink"
+               if args.exchange == "peer" else "NCCL all-to-all dispatch and combine")}
     if args.impl == "reference":
         return run_reference(args, shape, config)
     if ws > 1:

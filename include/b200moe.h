@@ -192,6 +192,54 @@ B200MOE_API int b200moe_ep_combine(const void* returned_rows, const int32_t* pos
                                    int num_ranks, int64_t rows_per_rank, void* out, void* stream);
 
 /* ------------------------------------------------------------------------
+ * The same expert parallelism with the exchange done by the kernels over
+ * NVLink peer memory instead of two all-to-alls (one process per GPU; the
+ * buffers are shared through CUDA IPC). Same packed rows and results:
+ *   b200moe_ep_dispatch_peer   plan + pack, each destination's rows stored
+ *                              straight into that rank's receive area; the
+ *                              last CTA raises this rank's dispatch flag on
+ *                              every rank;
+ *   b200moe_layer_packed_peer  waits for the G dispatch flags, runs the layer
+ *                              on the received rows; its top-k reduce stores
+ *                              each result row straight into the return area
+ *                              of the rank the token came from, then raises
+ *                              this rank's combine flag on every rank;
+ *   b200moe_ep_combine_peer    waits for the G combine flags and sums the
+ *                              returned rows in rank order (as
+ *                              b200moe_ep_combine).
+ * Set-up: each rank allocates its exchange buffer of b200moe_ep_peer_bytes()
+ * with b200moe_ep_peer_alloc (zeroed flags; B200MOE_IPC_HANDLE_BYTES bytes of
+ * IPC handle out), passes the handle to the other ranks over any host
+ * channel, maps theirs with b200moe_ep_peer_open, and builds a DEVICE array of
+ * G pointers, peer_bases[g] = rank g's buffer as mapped in this process (its
+ * own buffer at g = rank). `epoch` numbers the calls from 1, the same on all
+ * ranks; the areas are double-buffered by its parity, which is safe because a
+ * rank's call e+2 cannot start before every rank has finished reading e.
+ * Flag waits are bounded (B200MOE_DEVERR_TIMEOUT in the error word). At most
+ * 64 ranks. Replaces the DeepEP/Mori dispatch/combine pair the reference
+ * consumes (sglang_integration/aiter.py:554-756).
+ * ---------------------------------------------------------------------- */
+#define B200MOE_IPC_HANDLE_BYTES 64
+B200MOE_API size_t b200moe_ep_peer_bytes(int64_t rows_per_rank, int64_t H, int topk, int num_ranks);
+B200MOE_API int b200moe_ep_peer_alloc(size_t bytes, void** base, void* ipc_handle);
+B200MOE_API int b200moe_ep_peer_open(const void* ipc_handle, void** base);
+B200MOE_API int b200moe_ep_peer_close(void* base);
+B200MOE_API int b200moe_ep_peer_free(void* base);
+B200MOE_API int b200moe_ep_dispatch_peer(const uint8_t* hidden_q, const float* hidden_scale,
+                                         const int32_t* topk_ids, const float* topk_weights, int64_t M, int64_t H,
+                                         int topk, int num_experts, int num_ranks, int rank, int64_t rows_per_rank,
+                                         void* const* peer_bases, void* own_base, int32_t epoch, int32_t* pos,
+                                         int32_t* tok_of, int32_t* counts, int32_t* err_word, void* stream);
+B200MOE_API int b200moe_layer_packed_peer(void* own_base, void* const* peer_bases, int num_ranks, int rank,
+                                          int64_t rows_per_rank, int32_t epoch, int64_t H, int64_t I,
+                                          int num_local_experts, int topk, const uint8_t* w13,
+                                          const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+B200MOE_API int b200moe_ep_combine_peer(void* own_base, const int32_t* pos, int64_t M, int64_t H, int topk,
+                                        int num_ranks, int64_t rows_per_rank, int32_t epoch, void* out,
+                                        int32_t* err_word, void* stream);
+
+/* ------------------------------------------------------------------------
  * b200moe_layer without a workspace argument, for callers that cannot
  * allocate device memory (a fixed memory pool, a host framework that forbids
  * allocation inside an operator). No counterpart in the reference.

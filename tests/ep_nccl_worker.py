@@ -1,8 +1,11 @@
-"""One rank of the NCCL expert-parallel check (launched by torchrun from
+"""One rank of the multi-GPU expert-parallel check (launched by torchrun from
 tests/test_gpu_ep_nccl.py). Every rank builds the same global layer from the
 same seed, keeps its experts, runs its own tokens through ExpertParallelMoE
-and compares with the single-GPU layer over all experts. Rank 0 prints
-EP_NCCL_OK when every rank is within tolerance."""
+with both exchanges (NCCL all-to-alls, and the kernels' own stores into the
+other GPUs' memory) and compares with the single-GPU layer over all experts;
+the two exchanges must agree bit for bit, over several calls (both buffer
+parities of the peer exchange). Rank 0 prints EP_NCCL_OK when every rank
+passes."""
 import os
 import sys
 from datetime import timedelta
@@ -26,24 +29,28 @@ def main():
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     shape = synth.LayerShape(M=48, H=512, I=256, E=16, topk=4, scoring="sigmoid")
     L = synth.make_layer(shape, moe.per_block_quant_fp8, seed=0, device=dev)
-    model = ep.ExpertParallelMoE(ep.shard_experts(L.w13, rank, world), ep.shard_experts(L.w13_scale, rank, world),
-                                 ep.shard_experts(L.w2, rank, world), ep.shard_experts(L.w2_scale, rank, world),
-                                 num_experts=shape.E, rows_per_rank=shape.M)
-    g = torch.Generator().manual_seed(100 + rank)
-    M = shape.M - 5 * rank
-    tw, ids = synth.make_router(torch.randn(M, shape.E, generator=g), shape.topk, shape.scoring)
-    hidden = torch.randn(M, shape.H, generator=g).to(torch.bfloat16).to(dev)
-    tw, ids = tw.to(dev), ids.to(dev)
-    out = model(hidden, tw, ids)
-    out2 = model(hidden, tw, ids)
-    ref = moe.moe_decode_megakernel_full(hidden, L.w13, L.w13_scale, L.w2, L.w2_scale, tw, ids)
-    err = torch.tensor([orc.rel_l2(out, ref), 0.0 if torch.equal(out, out2) else 1.0, float(model.device_errors())],
-                       device=dev, dtype=torch.float64)
+    shards = [ep.shard_experts(w, rank, world) for w in (L.w13, L.w13_scale, L.w2, L.w2_scale)]
+    models = {x: ep.ExpertParallelMoE(*shards, num_experts=shape.E, rows_per_rank=shape.M, exchange=x)
+              for x in ("nccl", "peer")}
+    worst_rel, mismatch, dev_err = 0.0, 0.0, 0
+    for call in range(3):
+        g = torch.Generator().manual_seed(100 + 10 * call + rank)
+        M = shape.M - 5 * rank - call
+        tw, ids = synth.make_router(torch.randn(M, shape.E, generator=g), shape.topk, shape.scoring)
+        hidden = torch.randn(M, shape.H, generator=g).to(torch.bfloat16).to(dev)
+        tw, ids = tw.to(dev), ids.to(dev)
+        out = {x: m(hidden, tw, ids) for x, m in models.items()}
+        ref = moe.moe_decode_megakernel_full(hidden, L.w13, L.w13_scale, L.w2, L.w2_scale, tw, ids)
+        worst_rel = max(worst_rel, orc.rel_l2(out["nccl"], ref), orc.rel_l2(out["peer"], ref))
+        mismatch = max(mismatch, 0.0 if torch.equal(out["nccl"], out["peer"]) else 1.0)
+        dev_err |= models["nccl"].device_errors() | models["peer"].device_errors()
+    err = torch.tensor([worst_rel, mismatch, float(dev_err)], device=dev, dtype=torch.float64)
     dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    models["peer"].close()
     if rank == 0:
         ok = err[0].item() < TOL and err[1].item() == 0 and err[2].item() == 0
         print(("EP_NCCL_OK" if ok else "EP_NCCL_FAIL") + f" world={world} max_rel={err[0].item():.3e} "
-              f"nondeterministic={err[1].item():.0f} device_errors={err[2].item():.0f}", flush=True)
+              f"peer_vs_nccl_mismatch={err[1].item():.0f} device_errors={err[2].item():.0f}", flush=True)
     dist.destroy_process_group()
 
 

@@ -66,6 +66,26 @@ def test_host_side_argument_checks():
     assert b"workspace" in L.b200moe_last_error_message()
 
 
+def test_peer_exchange_host_checks():
+    L = _lib.lib()
+    H, topk, cap, G = 512, 4, 40, 4
+    rb = L.b200moe_ep_row_bytes(H, topk)
+    area_recv = -(-G * cap * rb // 256) * 256
+    area_ret = -(-G * cap * H * 2 // 256) * 256
+    assert L.b200moe_ep_peer_bytes(cap, H, topk, G) == 1024 + 2 * (area_recv + area_ret)
+    assert L.b200moe_ep_peer_bytes(cap, H, topk, 65) == 0     # at most 64 ranks
+    assert L.b200moe_ep_peer_bytes(cap, 100, topk, G) == 0    # H not a multiple of 128
+    # epoch 0, a rank outside the group, an unaligned own buffer: refused before any launch
+    args = [16, 16, 16, 16, 8, H, topk, 16, G]
+    assert L.b200moe_ep_dispatch_peer(*args, 0, cap, 256, 256, 0, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG
+    assert L.b200moe_ep_dispatch_peer(*args, G, cap, 256, 256, 1, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG
+    assert L.b200moe_ep_dispatch_peer(*args, 0, cap, 256, 260, 1, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG
+    assert L.b200moe_layer_packed_peer(256, 256, G, 0, cap, 0, H, 256, 4, topk, 16, 16, 16, 16, 256, 1 << 30,
+                                       None) == _lib.ERR_INVALID_ARG
+    assert L.b200moe_ep_combine_peer(256, 16, 8, H, topk, G, cap, 0, 16, 16, None) == _lib.ERR_INVALID_ARG
+    assert L.b200moe_ep_peer_alloc(16, None, None) == _lib.ERR_INVALID_ARG
+
+
 def test_python_errors_map_to_exceptions():
     with pytest.raises(NotImplementedError):
         _lib.check(_lib.ERR_UNSUPPORTED, "x")

@@ -113,3 +113,132 @@ def test_prequantised_input_is_bit_identical(cuda_device):
     with pytest.raises(NotImplementedError):
         moe.moe_decode_megakernel_full(q, g["w13"], g["w13_scale"], g["w2"], g["w2_scale"], g["topk_weights"],
                                        g["topk_ids"], a1_scale=torch.ones(q.shape[0], device=cuda_device))
+
+
+def _all_to_all_form(G, cap, toks, W, dev):
+    """Outputs of the all-to-all form (dispatch buffers re-sliced in place of
+    the exchange) for G simulated ranks' tokens."""
+    ops = ep.CudaEPOps()
+    H, I, topk, per = SHAPE.H, SHAPE.I, SHAPE.topk, SHAPE.E // G
+    rb = ops.row_bytes(H, topk)
+    sends, poss = [], []
+    for hidden, tw, ids in toks:
+        M = hidden.shape[0]
+        q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
+        s = torch.empty(M, H // 128, dtype=torch.float32, device=dev)
+        ops.quant(hidden, q, s)
+        send = torch.zeros(G * cap * rb, dtype=torch.uint8, device=dev)
+        pos = torch.empty(M * G, dtype=torch.int32, device=dev)
+        ops.dispatch(q, s, ids, tw, SHAPE.E, G, cap, send, pos, torch.empty(G * cap, dtype=torch.int32, device=dev),
+                     torch.empty(G, dtype=torch.int32, device=dev), torch.zeros(1, dtype=torch.int32, device=dev))
+        sends.append(send.view(G, cap * rb))
+        poss.append(pos)
+    local = []
+    for d in range(G):
+        recv = torch.cat([sends[r][d] for r in range(G)]).contiguous()
+        out_d = torch.empty(G * cap, H, dtype=torch.bfloat16, device=dev)
+        ws = torch.zeros(max(ops.workspace_bytes(G * cap, H, I, per, topk), 256), dtype=torch.uint8, device=dev)
+        sl = slice(d * per, (d + 1) * per)
+        ops.layer_packed(recv, G * cap, H, I, per, topk, W["w13"][sl].contiguous(), W["w13_scale"][sl].contiguous(),
+                         W["w2"][sl].contiguous(), W["w2_scale"][sl].contiguous(), out_d, ws)
+        local.append(out_d.view(G, cap, H))
+    outs = []
+    for r, (hidden, _, _) in enumerate(toks):
+        M = hidden.shape[0]
+        out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+        ops.combine(torch.cat([local[d][r] for d in range(G)]).contiguous(), poss[r], M, H, G, cap, out)
+        outs.append(out)
+    return outs
+
+
+@pytest.mark.parametrize("G", [1, 2, 4])
+def test_peer_exchange_simulated_ranks_bit_identical_to_all_to_all(cuda_device, G):
+    """The G ranks' exchange buffers live in one process on one GPU. Every
+    kernel of a call is launched after the kernels whose flags it waits for
+    (all dispatches, then all layers, then all combines), so no wait depends
+    on a later launch. Three calls exercise both buffer parities."""
+    import ctypes
+
+    from trials_b200 import _lib
+
+    dev = cuda_device
+    L = synth.make_layer(SHAPE, orc.per_block_quant_fp8, seed=1)
+    W = {k: getattr(L, k).to(dev) for k in ["w13", "w13_scale", "w2", "w2_scale"]}
+    lib = _lib.lib()
+    H, I, topk, cap, per = SHAPE.H, SHAPE.I, SHAPE.topk, SHAPE.M, SHAPE.E // G
+    nbytes = lib.b200moe_ep_peer_bytes(cap, H, topk, G)
+    bases = []
+    for _ in range(G):
+        b = ctypes.c_void_p()
+        h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+        _lib.check(lib.b200moe_ep_peer_alloc(nbytes, ctypes.byref(b), h), "ep_peer_alloc")
+        bases.append(b.value)
+    table = torch.tensor(bases, dtype=torch.int64, device=dev)
+    ops = ep.CudaEPOps()
+    R = G * cap
+    ws = [torch.zeros(max(ops.workspace_bytes(R, H, I, per, topk), 256), dtype=torch.uint8, device=dev)
+          for _ in range(G)]
+    st = torch.cuda.current_stream(dev).cuda_stream
+    try:
+        for epoch in (1, 2, 3):
+            toks = [_tokens(SHAPE, 100 * epoch + r, cap - 3 * r - epoch, dev) for r in range(G)]
+            state = []
+            for r, (hidden, tw, ids) in enumerate(toks):
+                M = hidden.shape[0]
+                q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
+                s = torch.empty(M, H // 128, dtype=torch.float32, device=dev)
+                ops.quant(hidden, q, s)
+                pos = torch.empty(M * G, dtype=torch.int32, device=dev)
+                tok_of = torch.empty(R, dtype=torch.int32, device=dev)
+                counts = torch.empty(G, dtype=torch.int32, device=dev)
+                err = torch.zeros(1, dtype=torch.int32, device=dev)
+                _lib.check(lib.b200moe_ep_dispatch_peer(
+                    q.data_ptr(), s.data_ptr(), ids.data_ptr(), tw.data_ptr(), M, H, topk, SHAPE.E, G, r, cap,
+                    table.data_ptr(), bases[r], epoch, pos.data_ptr(), tok_of.data_ptr(), counts.data_ptr(),
+                    err.data_ptr(), st), "dispatch_peer")
+                state.append((pos, err))
+            for d in range(G):
+                sl = slice(d * per, (d + 1) * per)
+                _lib.check(lib.b200moe_layer_packed_peer(
+                    bases[d], table.data_ptr(), G, d, cap, epoch, H, I, per, topk,
+                    W["w13"][sl].contiguous().data_ptr(), W["w13_scale"][sl].contiguous().data_ptr(),
+                    W["w2"][sl].contiguous().data_ptr(), W["w2_scale"][sl].contiguous().data_ptr(), ws[d].data_ptr(),
+                    ws[d].numel(), st), "layer_packed_peer")
+            outs = []
+            for r, (hidden, _, _) in enumerate(toks):
+                M = hidden.shape[0]
+                out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+                pos, err = state[r]
+                _lib.check(lib.b200moe_ep_combine_peer(bases[r], pos.data_ptr(), M, H, topk, G, cap, epoch,
+                                                       out.data_ptr(), err.data_ptr(), st), "combine_peer")
+                outs.append(out)
+            ref = _all_to_all_form(G, cap, toks, W, dev)
+            for r in range(G):
+                assert moe.read_device_error(state[r][1]) == 0
+                assert moe.read_device_error(ws[r][:4].view(torch.int32)) == 0
+                assert torch.equal(outs[r], ref[r]), (epoch, r)
+    finally:
+        torch.cuda.synchronize(dev)
+        for b in bases:
+            lib.b200moe_ep_peer_free(b)
+
+
+def test_expert_parallel_module_peer_exchange_one_rank(cuda_device):
+    """ExpertParallelMoE with the peer exchange and no process group (G = 1)
+    equals the single-GPU layer bit for bit on repeated calls."""
+    dev = cuda_device
+    L = synth.make_layer(SHAPE, orc.per_block_quant_fp8, seed=2)
+    W = {k: getattr(L, k).to(dev) for k in ["w13", "w13_scale", "w2", "w2_scale"]}
+    model = ep.ExpertParallelMoE(W["w13"], W["w13_scale"], W["w2"], W["w2_scale"], num_experts=SHAPE.E,
+                                 rows_per_rank=SHAPE.M)
+    assert model.exchange == "peer"
+    try:
+        for call in range(3):
+            hidden, tw, ids = _tokens(SHAPE, 200 + call, SHAPE.M - call, dev)
+            out = model(hidden, tw, ids)
+            single = moe.moe_decode_megakernel_full(hidden, W["w13"], W["w13_scale"], W["w2"], W["w2_scale"], tw,
+                                                    ids)
+            assert orc.rel_l2(out, single) < EP_TOL
+            assert model.device_errors() == 0
+    finally:
+        model.close()

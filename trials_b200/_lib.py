@@ -22,6 +22,8 @@ DEVERR_BAD_EXPERT_ID = 1
 DEVERR_TIMEOUT = 2
 DEVERR_CAPACITY = 4
 
+IPC_HANDLE_BYTES = 64
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _L = ctypes.c_int64
@@ -46,6 +48,16 @@ SIGNATURES = {
     "b200moe_layer_packed_workspace_size": (_S, [_L, _L, _L, _I, _I]),
     "b200moe_layer_packed": (_I, [_P, _L, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _S, _P]),
     "b200moe_ep_combine": (_I, [_P, _P, _L, _L, _I, _L, _P, _P]),
+    "b200moe_ep_peer_bytes": (_S, [_L, _L, _I, _I]),
+    "b200moe_ep_peer_alloc": (_I, [_S, ctypes.POINTER(_P), _P]),
+    "b200moe_ep_peer_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "b200moe_ep_peer_close": (_I, [_P]),
+    "b200moe_ep_peer_free": (_I, [_P]),
+    "b200moe_ep_dispatch_peer": (_I, [_P, _P, _P, _P, _L, _L, _I, _I, _I, _I, _L, _P, _P, ctypes.c_int32, _P, _P, _P,
+                                      _P, _P]),
+    "b200moe_layer_packed_peer": (_I, [_P, _P, _I, _I, _L, ctypes.c_int32, _L, _L, _I, _I, _P, _P, _P, _P, _P, _S,
+                                       _P]),
+    "b200moe_ep_combine_peer": (_I, [_P, _P, _L, _L, _I, _I, _L, ctypes.c_int32, _P, _P, _P]),
     "b200moe_layer_noalloc": (_I, [_P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P]),
     "b200moe_route_capacity_rows": (_L, [_L, _I]),
     "b200moe_route_capacity_chunks": (_L, [_L, _I, _I]),

@@ -18,7 +18,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OBJ = PKG / "_build"
 LIB = PKG / "libb200moe.so"
-SOURCES = ["capi.cu", "route.cu", "router.cu", "quant.cu", "gemm.cu", "ep.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "route.cu", "router.cu", "quant.cu", "gemm.cu", "ep.cu", "ep_peer.cu", "noalloc.cu"]
 HEADERS = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [ROOT / "include" / "b200moe.h"]
 
 

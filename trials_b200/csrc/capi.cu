@@ -1,6 +1,7 @@
 // extern "C" entry points: argument checks, workspace carving, TMA tensor
 // maps and kernel sequencing. No function here allocates device memory or
-// synchronises the stream (except b200moe_read_error, which exists to do so).
+// synchronises the stream, except b200moe_read_error (which exists to do so)
+// and the set-up calls of the peer exchange buffer (b200moe_ep_peer_alloc).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -595,13 +596,14 @@ struct LayerInput {
 int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
                const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
                const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map, int num_local_experts,
-               void* out, void* workspace, size_t workspace_bytes, size_t workspace_offset, void* stream) {
+               void* out, void* workspace, size_t workspace_bytes, size_t workspace_offset, void* stream,
+               const EpPeerArgs* peer_out = nullptr, int32_t* peer_counter = nullptr) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (M < 0 || topk <= 0 || num_experts <= 0) return fail(B200MOE_ERR_INVALID_ARG, "%s: bad argument", name);
   if (M == 0) return B200MOE_OK;
-  if ((!in.hidden && !in.q) || !w13 || !w13_scale || !w2 || !w2_scale || !topk_weights || !topk_ids || !out ||
-      !workspace)
+  if ((!in.hidden && !in.q) || !w13 || !w13_scale || !w2 || !w2_scale || !topk_weights || !topk_ids ||
+      (!out && !peer_out) || !workspace)
     return fail(B200MOE_ERR_INVALID_ARG, "%s: null pointer", name);
   const int E = expert_map ? num_local_experts : num_experts;
   if (E <= 0 || E > 1024) return fail(B200MOE_ERR_UNSUPPORTED, "%s: 1..1024 experts supported", name);
@@ -649,6 +651,10 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
                        pl.chunks_cap, ready, pl.tile_tokens, a2, a2s, sorted, topk_weights, M, topk, pair, err, 0,
                        stream);
   if (st) return st;
+  if (peer_out)  // results straight into the source ranks' return areas
+    return cuda_status(launch_ep_reduce_peer(pair, pos, pair_sorted_rows(pl.tile_tokens), topk, H, *peer_out,
+                                             peer_counter, (cudaStream_t)stream),
+                       "ep_reduce_peer");
   return b200moe_combine_reduce(pair, pos, pair_sorted_rows(pl.tile_tokens), M, topk, H, out, stream);
 }
 
@@ -734,6 +740,137 @@ int b200moe_ep_combine(const void* returned_rows, const int32_t* pos, int64_t M,
     return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_combine: 16-byte alignment required%s");
   return cuda_status(launch_ep_combine(returned_rows, pos, M, H, num_ranks, rows_per_rank, out, (cudaStream_t)stream),
                      "ep_combine");
+}
+
+size_t b200moe_ep_peer_bytes(int64_t rows_per_rank, int64_t H, int topk, int num_ranks) {
+  if (rows_per_rank < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || num_ranks <= 0 ||
+      num_ranks > EpPeerLayout::kMaxRanks)
+    return 0;
+  return (size_t)EpPeerLayout(rows_per_rank, H, b200moe_ep_row_bytes(H, topk), num_ranks).total();
+}
+
+int b200moe_ep_peer_alloc(size_t bytes, void** base, void* ipc_handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == B200MOE_IPC_HANDLE_BYTES, "IPC handle size");
+  if (bytes < (size_t)EpPeerLayout::kHeader || !base || !ipc_handle)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_peer_alloc: bad argument%s");
+  void* p = nullptr;
+  int st = cuda_status(cudaMalloc(&p, bytes), "ep_peer_alloc");
+  if (st) return st;
+  // Flags start at 0 (epochs count from 1); done before the handle leaves.
+  st = cuda_status(cudaMemset(p, 0, EpPeerLayout::kHeader), "ep_peer_alloc memset");
+  if (!st) st = cuda_status(cudaDeviceSynchronize(), "ep_peer_alloc sync");
+  cudaIpcMemHandle_t h;
+  if (!st) st = cuda_status(cudaIpcGetMemHandle(&h, p), "ep_peer_alloc handle");
+  if (st) {
+    cudaFree(p);
+    return st;
+  }
+  memcpy(ipc_handle, &h, sizeof h);
+  *base = p;
+  return B200MOE_OK;
+}
+
+int b200moe_ep_peer_open(const void* ipc_handle, void** base) {
+  if (!ipc_handle || !base) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_peer_open: null pointer%s");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof h);
+  return cuda_status(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess), "ep_peer_open");
+}
+
+int b200moe_ep_peer_close(void* base) {
+  if (!base) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_peer_close: null pointer%s");
+  return cuda_status(cudaIpcCloseMemHandle(base), "ep_peer_close");
+}
+
+int b200moe_ep_peer_free(void* base) {
+  if (!base) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_peer_free: null pointer%s");
+  return cuda_status(cudaFree(base), "ep_peer_free");
+}
+
+namespace {
+constexpr uint64_t kPeerWaitNs = 10ull * 1000 * 1000 * 1000;  // ranks may start a call seconds apart
+
+bool peer_args_ok(int num_ranks, int rank, int64_t rows_per_rank, int32_t epoch, void* const* peer_bases,
+                  const void* own_base) {
+  return num_ranks > 0 && num_ranks <= EpPeerLayout::kMaxRanks && rank >= 0 && rank < num_ranks &&
+         rows_per_rank >= 0 && epoch >= 1 && peer_bases && own_base &&
+         (reinterpret_cast<uintptr_t>(own_base) & 255) == 0;
+}
+}  // namespace
+
+int b200moe_ep_dispatch_peer(const uint8_t* hidden_q, const float* hidden_scale, const int32_t* topk_ids,
+                             const float* topk_weights, int64_t M, int64_t H, int topk, int num_experts,
+                             int num_ranks, int rank, int64_t rows_per_rank, void* const* peer_bases, void* own_base,
+                             int32_t epoch, int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err_word,
+                             void* stream) {
+  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || num_experts % num_ranks != 0 || !err_word || !counts ||
+      !peer_args_ok(num_ranks, rank, rows_per_rank, epoch, peer_bases, own_base) ||
+      (M > 0 && (!hidden_q || !hidden_scale || !topk_ids || !topk_weights || !pos)) ||
+      (rows_per_rank > 0 && !tok_of))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_dispatch_peer: bad argument%s");
+  if (!aligned16(hidden_q)) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_dispatch_peer: 16-byte alignment%s");
+  const int64_t rb = b200moe_ep_row_bytes(H, topk);
+  const EpPeerLayout lay(rows_per_rank, H, rb, num_ranks);
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = cuda_status(launch_ep_plan(topk_ids, M, topk, num_experts, num_ranks, rows_per_rank, pos, tok_of, counts,
+                                      err_word, s),
+                       "ep_plan");
+  if (st) return st;
+  const EpPeerArgs a{reinterpret_cast<uint8_t* const*>(peer_bases), lay.recv_off(epoch), rows_per_rank, num_ranks,
+                     rank, epoch};
+  int32_t* counter = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(own_base) + EpPeerLayout::kCounters);
+  return cuda_status(launch_ep_pack_peer(hidden_q, hidden_scale, topk_ids, topk_weights, H, topk, num_experts, tok_of,
+                                         counts, rb, a, counter, s),
+                     "ep_pack_peer");
+}
+
+int b200moe_layer_packed_peer(void* own_base, void* const* peer_bases, int num_ranks, int rank,
+                              int64_t rows_per_rank, int32_t epoch, int64_t H, int64_t I, int num_local_experts,
+                              int topk, const uint8_t* w13, const float* w13_scale, const uint8_t* w2,
+                              const float* w2_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!peer_args_ok(num_ranks, rank, rows_per_rank, epoch, peer_bases, own_base) || H <= 0 || H % 128 != 0 ||
+      topk <= 0 || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer_packed_peer: bad argument%s");
+  const int64_t R = (int64_t)num_ranks * rows_per_rank;
+  const int64_t rb = b200moe_ep_row_bytes(H, topk);
+  const EpPeerLayout lay(rows_per_rank, H, rb, num_ranks);
+  uint8_t* own = static_cast<uint8_t*>(own_base);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (R > 0 && workspace_bytes < b200moe_layer_packed_workspace_size(R, H, I, num_local_experts, topk))
+    return fail(B200MOE_ERR_WORKSPACE, "b200moe_layer_packed_peer: workspace too small%s");
+  int32_t* err = static_cast<int32_t*>(workspace);
+  int st = cuda_status(launch_ep_wait_flags(reinterpret_cast<const int32_t*>(own + EpPeerLayout::kDispatchFlags),
+                                            num_ranks, epoch, err, kPeerWaitNs, s),
+                       "ep_wait_flags");
+  if (st) return st;
+  const EpPeerArgs a{reinterpret_cast<uint8_t* const*>(peer_bases), lay.ret_off(epoch), rows_per_rank, num_ranks,
+                     rank, epoch};
+  int32_t* counter = reinterpret_cast<int32_t*>(own + EpPeerLayout::kCounters) + 1;
+  if (R == 0) return cuda_status(launch_ep_reduce_peer(nullptr, nullptr, 0, topk, H, a, counter, s), "ep_reduce_peer");
+  const uint8_t* rows = own + lay.recv_off(epoch);
+  const size_t meta = (size_t)round_up(R * topk * 8 + 256, 256);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* ids = reinterpret_cast<int32_t*>(ws + 256);
+  float* w = reinterpret_cast<float*>(ids + R * topk);
+  st = cuda_status(launch_ep_unpack_meta(rows, R, rb, H, topk, ids, w, s), "ep_unpack_meta");
+  if (st) return st;
+  LayerInput in{nullptr, rows, rb, reinterpret_cast<const float*>(rows + H), rb / 4};
+  return layer_core("b200moe_layer_packed_peer", in, R, H, I, num_local_experts, topk, w13, w13_scale, w2, w2_scale, w,
+                    ids, nullptr, num_local_experts, nullptr, workspace, workspace_bytes, meta, stream, &a, counter);
+}
+
+int b200moe_ep_combine_peer(void* own_base, const int32_t* pos, int64_t M, int64_t H, int topk, int num_ranks,
+                            int64_t rows_per_rank, int32_t epoch, void* out, int32_t* err_word, void* stream) {
+  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || !err_word ||
+      num_ranks <= 0 || num_ranks > EpPeerLayout::kMaxRanks || rows_per_rank < 0 || epoch < 1 || !own_base ||
+      (M > 0 && (!pos || !out)))
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_combine_peer: bad argument%s");
+  if (!aligned16(out)) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_combine_peer: 16-byte alignment%s");
+  const EpPeerLayout lay(rows_per_rank, H, b200moe_ep_row_bytes(H, topk), num_ranks);
+  return cuda_status(launch_ep_combine_peer(static_cast<const uint8_t*>(own_base), lay.ret_off(epoch), pos, M, H,
+                                            num_ranks, rows_per_rank, epoch, out, err_word, kPeerWaitNs,
+                                            (cudaStream_t)stream),
+                     "ep_combine_peer");
 }
 
 int b200moe_router_topk(const void* logits, int logits_bf16, int64_t M, int num_experts, int topk, int scoring,

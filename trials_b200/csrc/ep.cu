@@ -164,13 +164,18 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __
 
 }  // namespace
 
+cudaError_t launch_ep_plan(const int32_t* ids, int64_t M, int topk, int num_experts, int G, int64_t rows_per_rank,
+                           int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err, cudaStream_t stream) {
+  ep_plan_kernel<<<G, kPlanThreads, 0, stream>>>(ids, M, topk, num_experts, G, rows_per_rank, pos, tok_of, counts,
+                                                 err);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_ep_dispatch(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t M,
                                int64_t H, int topk, int num_experts, int G, int64_t rows_per_rank, uint8_t* send,
                                int64_t row_bytes, int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err,
                                cudaStream_t stream) {
-  ep_plan_kernel<<<G, kPlanThreads, 0, stream>>>(ids, M, topk, num_experts, G, rows_per_rank, pos, tok_of, counts,
-                                                 err);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_ep_plan(ids, M, topk, num_experts, G, rows_per_rank, pos, tok_of, counts, err, stream);
   if (e != cudaSuccess) return e;
   const int64_t rows = (int64_t)G * rows_per_rank;
   if (rows == 0) return cudaSuccess;

@@ -1,0 +1,225 @@
+// Expert-parallel exchange through NVLink peer memory: the two all-to-alls of
+// the NCCL form (ep.cu) are folded into the kernels on either side of them.
+//
+// Every rank owns one exchange buffer (layout: EpPeerLayout in launch.h) that
+// the other ranks map through CUDA IPC:
+//   - the dispatch pack kernel stores each destination's rows straight into
+//     that rank's receive area (block = source rank) and, when the last of its
+//     CTAs is done, raises flag dflag[src] = epoch in every rank's header;
+//   - on the receiving side a one-CTA kernel waits for the G dispatch flags
+//     before the layer kernels read the rows;
+//   - the layer's top-k reduce stores each result row straight into the
+//     return area of the rank the token came from (block = expert-side rank)
+//     and raises cflag[src] = epoch the same way;
+//   - the combine kernel waits for the G combine flags, then sums.
+// Flags only grow (epoch = call count, from 1), so nothing is reset between
+// calls. Areas are double-buffered by epoch parity. Rank a stores into b's
+// receive area (e & 1) in call e after a's layer of call e-1, which waited for
+// b's dispatch of call e-1, which b issued after its layer of call e-2 had
+// read that area. Likewise b stores into a's return area (e & 1) in call e+2
+// after waiting for a's dispatch of call e+2, which a issued after its combine
+// of call e had read the area. Waits are bounded by %globaltimer and set
+// B200MOE_DEVERR_TIMEOUT on expiry.
+#include "common.cuh"
+#include "launch.h"
+#include "ptx.cuh"
+#include "rowops.cuh"
+
+namespace b200moe {
+
+namespace {
+
+__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Threads 0..G-1 wait until flags[thread] >= epoch, then the whole CTA passes
+// a barrier: everything the G writers stored before raising their flags is
+// visible to the CTA (and to later kernels of the stream) afterwards. Once a
+// wait has expired (timeout bit in err), later waits give up after 1 ms, so a
+// many-CTA launch whose peer is gone ends in about one limit, not one per wave.
+__device__ __forceinline__ void wait_flags(const int32_t* flags, int G, int32_t epoch, int32_t* err,
+                                           uint64_t limit_ns) {
+  if ((int)threadIdx.x < G) {
+    const int32_t* f = flags + threadIdx.x;
+    if (ld_acquire_sys(f) < epoch) {
+      const uint64_t t0 = globaltimer_ns();
+      const uint64_t limit =
+          (*reinterpret_cast<volatile int32_t*>(err) & ERR_DEV_TIMEOUT) ? 1000000ull : limit_ns;
+      while (ld_acquire_sys(f) < epoch) {
+        if (globaltimer_ns() - t0 > limit) {
+          atomicOr(err, ERR_DEV_TIMEOUT);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Called by every thread of every CTA after its stores: the last CTA to finish
+// raises this rank's flag (at byte offset flag_off of each rank's buffer) to
+// epoch on all G ranks and resets the CTA counter for the next launch.
+__device__ __forceinline__ void signal_done(const EpPeerArgs& a, int64_t flag_off, int32_t* counter) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(counter, 1) == (int)(gridDim.x * gridDim.y) - 1) {
+      atomicExch(counter, 0);
+      __threadfence_system();
+      for (int g = 0; g < a.G; ++g)
+        st_release_sys(reinterpret_cast<int32_t*>(a.bases[g] + flag_off) + a.rank, a.epoch);
+    }
+  }
+}
+
+// One warp per destination row, as ep_pack_kernel, with the row stored into
+// the destination's receive area (row rank*rows_per_rank + r).
+__global__ void __launch_bounds__(256) ep_pack_peer_kernel(const uint8_t* __restrict__ q, const float* __restrict__ s,
+                                                           const int32_t* __restrict__ ids,
+                                                           const float* __restrict__ w, int64_t H, int topk,
+                                                           int num_experts, const int32_t* __restrict__ tok_of,
+                                                           const int32_t* __restrict__ counts, int64_t row_bytes,
+                                                           const EpPeerArgs a, int32_t* counter) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row < (int64_t)a.G * a.rows_per_rank) {
+    const int d = (int)(row / a.rows_per_rank);
+    const int64_t r = row - (int64_t)d * a.rows_per_rank;
+    const int per_rank = num_experts / a.G;
+    uint8_t* dst = a.bases[d] + a.area_off + ((int64_t)a.rank * a.rows_per_rank + r) * row_bytes;
+    int32_t* dst_ids = reinterpret_cast<int32_t*>(dst + H + (H / 128) * 4);
+    float* dst_w = reinterpret_cast<float*>(dst_ids + topk);
+    if (r >= __ldg(&counts[d])) {
+      for (int j = lane; j < topk; j += 32) {
+        dst_ids[j] = -1;
+        dst_w[j] = 0.f;
+      }
+    } else {
+      const int64_t t = __ldg(&tok_of[row]);
+      const uint4* src = reinterpret_cast<const uint4*>(q + t * H);
+      uint4* out = reinterpret_cast<uint4*>(dst);
+      for (int64_t i = lane; i < H / 16; i += 32) out[i] = __ldg(&src[i]);
+      float* dst_s = reinterpret_cast<float*>(dst + H);
+      for (int64_t g = lane; g < H / 128; g += 32) dst_s[g] = __ldg(&s[t * (H / 128) + g]);
+      for (int j = lane; j < topk; j += 32) {
+        const int id = __ldg(&ids[t * topk + j]);
+        const bool mine = id >= 0 && id < num_experts && id / per_rank == d;
+        dst_ids[j] = mine ? id - d * per_rank : -1;
+        dst_w[j] = mine ? __ldg(&w[t * topk + j]) : 0.f;
+      }
+    }
+  }
+  signal_done(a, EpPeerLayout::kDispatchFlags, counter);
+}
+
+__global__ void ep_wait_flags_kernel(const int32_t* flags, int G, int32_t epoch, int32_t* err, uint64_t limit_ns) {
+  wait_flags(flags, G, epoch, err, limit_ns);
+}
+
+// Top-k reduce of the received rows (R = G*rows_per_rank, row i = row
+// i % rows_per_rank of source rank i / rows_per_rank), each bf16 result row
+// stored into the source rank's return area at row rank*rows_per_rank + r.
+template <int B>
+__global__ void __launch_bounds__(256) ep_reduce_peer_kernel(const float* __restrict__ pair,
+                                                             const int32_t* __restrict__ slot_pos, int sorted_rows,
+                                                             int topk, int64_t H, const EpPeerArgs a,
+                                                             int32_t* counter) {
+  const int64_t per_row = H / 8;
+  const int64_t R = (int64_t)a.G * a.rows_per_rank;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t t = idx / per_row;
+  if (t < R) {
+    const int src = (int)(t / a.rows_per_rank);
+    const int64_t r = t - (int64_t)src * a.rows_per_rank;
+    __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(a.bases[src] + a.area_off) +
+                         ((int64_t)a.rank * a.rows_per_rank + r) * H;
+    reduce_token_cols<B>(pair, slot_pos, sorted_rows, topk, H, t, (idx - t * per_row) * 8, row);
+  }
+  signal_done(a, EpPeerLayout::kCombineFlags, counter);
+}
+
+// out[t] = bf16(sum over ranks d, ascending, of the return-area row d*rpr + pos[t][d]),
+// after the G combine flags of this epoch are up.
+__global__ void __launch_bounds__(256) ep_combine_peer_kernel(const uint8_t* own, int64_t area_off,
+                                                              const int32_t* __restrict__ pos, int64_t M, int64_t H,
+                                                              int G, int64_t rows_per_rank, int32_t epoch,
+                                                              __nv_bfloat16* __restrict__ out, int32_t* err,
+                                                              uint64_t limit_ns) {
+  wait_flags(reinterpret_cast<const int32_t*>(own + EpPeerLayout::kCombineFlags), G, epoch, err, limit_ns);
+  const __nv_bfloat16* comb = reinterpret_cast<const __nv_bfloat16*>(own + area_off);
+  const int64_t per_row = H / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t t = idx / per_row;
+  if (t >= M) return;
+  const int64_t c = (idx - t * per_row) * 8;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int d = 0; d < G; ++d) {
+    const int r = __ldg(&pos[t * G + d]);
+    if (r < 0) continue;
+    // Written by another GPU in this kernel's lifetime: read through L2.
+    const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(comb + ((int64_t)d * rows_per_rank + r) * H + c));
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h2[i]);
+      acc[2 * i] += f.x;
+      acc[2 * i + 1] += f.y;
+    }
+  }
+  __nv_bfloat162 o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+  *reinterpret_cast<uint4*>(out + t * H + c) = *reinterpret_cast<const uint4*>(o);
+}
+
+}  // namespace
+
+cudaError_t launch_ep_pack_peer(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t H,
+                                int topk, int num_experts, const int32_t* tok_of, const int32_t* counts,
+                                int64_t row_bytes, const EpPeerArgs& a, int32_t* counter, cudaStream_t stream) {
+  const int64_t rows = (int64_t)a.G * a.rows_per_rank;
+  const int64_t blocks = rows > 0 ? (rows + 7) / 8 : 1;  // one CTA at least, to raise the flags
+  ep_pack_peer_kernel<<<(unsigned)blocks, 256, 0, stream>>>(q, s, ids, w, H, topk, num_experts, tok_of, counts,
+                                                             row_bytes, a, counter);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait_flags(const int32_t* flags, int G, int32_t epoch, int32_t* err, uint64_t limit_ns,
+                                 cudaStream_t stream) {
+  ep_wait_flags_kernel<<<1, 64, 0, stream>>>(flags, G, epoch, err, limit_ns);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_reduce_peer(const float* pair, const int32_t* slot_pos, int sorted_rows, int topk, int64_t H,
+                                  const EpPeerArgs& a, int32_t* counter, cudaStream_t stream) {
+  const int64_t R = (int64_t)a.G * a.rows_per_rank;
+  const int64_t n = R * (H / 8);
+  const int64_t blocks = n > 0 ? (n + 255) / 256 : 1;
+  if (R * topk <= 1024)
+    ep_reduce_peer_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, topk, H, a, counter);
+  else
+    ep_reduce_peer_kernel<1><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, topk, H, a, counter);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine_peer(const uint8_t* own, int64_t area_off, const int32_t* pos, int64_t M, int64_t H,
+                                   int G, int64_t rows_per_rank, int32_t epoch, void* out, int32_t* err,
+                                   uint64_t limit_ns, cudaStream_t stream) {
+  const int64_t n = M * (H / 8);
+  if (n <= 0) return cudaSuccess;
+  ep_combine_peer_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      own, area_off, pos, M, H, G, rows_per_rank, epoch, reinterpret_cast<__nv_bfloat16*>(out), err, limit_ns);
+  return cudaGetLastError();
+}
+
+}  // namespace b200moe

@@ -72,6 +72,8 @@ cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K
 cudaError_t launch_combine_reduce(const float* pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
                                   int64_t H, void* out, cudaStream_t stream);
 
+cudaError_t launch_ep_plan(const int32_t* ids, int64_t M, int topk, int num_experts, int G, int64_t rows_per_rank,
+                           int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err, cudaStream_t stream);
 cudaError_t launch_ep_dispatch(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t M,
                                int64_t H, int topk, int num_experts, int G, int64_t rows_per_rank, uint8_t* send,
                                int64_t row_bytes, int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err,
@@ -80,6 +82,45 @@ cudaError_t launch_ep_unpack_meta(const uint8_t* rows, int64_t R, int64_t row_by
                                   int32_t* ids, float* w, cudaStream_t stream);
 cudaError_t launch_ep_combine(const void* comb, const int32_t* pos, int64_t M, int64_t H, int G,
                               int64_t rows_per_rank, void* out, cudaStream_t stream);
+
+// Exchange buffer of one rank for expert parallelism through peer memory:
+// [header | receive area x 2 | return area x 2], areas double-buffered by the
+// parity of the call count. Receive area: G blocks of rows_per_rank packed
+// rows (block = source rank). Return area: G blocks of rows_per_rank bf16 rows
+// of H (block = expert-side rank). Header: the flags the other ranks raise and
+// this rank's CTA counters.
+struct EpPeerLayout {
+  static constexpr int64_t kDispatchFlags = 0;   // int32[kMaxRanks]: source rank -> epoch of its rows
+  static constexpr int64_t kCombineFlags = 256;  // int32[kMaxRanks]: expert-side rank -> epoch of its results
+  static constexpr int64_t kCounters = 512;      // int32[2]: CTAs done (pack, reduce), local
+  static constexpr int64_t kHeader = 1024;
+  static constexpr int kMaxRanks = 64;
+  int64_t recv_bytes, ret_bytes;
+  EpPeerLayout(int64_t rows_per_rank, int64_t H, int64_t row_bytes, int G)
+      : recv_bytes(((int64_t)G * rows_per_rank * row_bytes + 255) / 256 * 256),
+        ret_bytes(((int64_t)G * rows_per_rank * H * 2 + 255) / 256 * 256) {}
+  int64_t recv_off(int32_t epoch) const { return kHeader + (epoch & 1) * recv_bytes; }
+  int64_t ret_off(int32_t epoch) const { return kHeader + 2 * recv_bytes + (epoch & 1) * ret_bytes; }
+  int64_t total() const { return kHeader + 2 * (recv_bytes + ret_bytes); }
+};
+
+struct EpPeerArgs {
+  uint8_t* const* bases;  // device array: the G ranks' exchange buffers as mapped here
+  int64_t area_off;       // the area written on the far side (receive or return, this call's parity)
+  int64_t rows_per_rank;
+  int G, rank;
+  int32_t epoch;
+};
+cudaError_t launch_ep_pack_peer(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t H,
+                                int topk, int num_experts, const int32_t* tok_of, const int32_t* counts,
+                                int64_t row_bytes, const EpPeerArgs& a, int32_t* counter, cudaStream_t stream);
+cudaError_t launch_ep_wait_flags(const int32_t* flags, int G, int32_t epoch, int32_t* err, uint64_t limit_ns,
+                                 cudaStream_t stream);
+cudaError_t launch_ep_reduce_peer(const float* pair, const int32_t* slot_pos, int sorted_rows, int topk, int64_t H,
+                                  const EpPeerArgs& a, int32_t* counter, cudaStream_t stream);
+cudaError_t launch_ep_combine_peer(const uint8_t* own, int64_t area_off, const int32_t* pos, int64_t M, int64_t H,
+                                   int G, int64_t rows_per_rank, int32_t epoch, void* out, int32_t* err,
+                                   uint64_t limit_ns, cudaStream_t stream);
 
 cudaError_t launch_router_topk(const void* logits, int bf16, int64_t M, int E, int topk, int scoring,
                                const float* bias, int renormalize, float scaling, float* out_w, int32_t* out_ids,

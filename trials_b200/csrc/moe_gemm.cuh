@@ -753,7 +753,7 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
         for (int64_t i = (int64_t)blockIdx.x * (EW * 32) + tid; i < n; i += (int64_t)gridDim.x * (EW * 32)) {
           const int64_t t = i / per_row;
           reduce_token_cols<4>(p2.out_pair, p.red_slot_pos, 0, p.red_topk, p2.Nw, t, (i - t * per_row) * 8,
-                               p.red_out);
+                               p.red_out + t * p2.Nw);
         }
       }
     }

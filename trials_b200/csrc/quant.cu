@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __rest
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t t = idx / per_row;
   if (t >= M) return;
-  reduce_token_cols<B>(pair, slot_pos, sorted_rows, topk, H, t, (idx - t * per_row) * 8, out);
+  reduce_token_cols<B>(pair, slot_pos, sorted_rows, topk, H, t, (idx - t * per_row) * 8, out + t * H);
 }
 
 cudaError_t launch_combine_reduce(const float* pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,

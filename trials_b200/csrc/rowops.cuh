@@ -100,15 +100,16 @@ __device__ __forceinline__ void quant_row_segment(const QuantArgs& a, int64_t ro
   }
 }
 
-// One thread: out[t, c .. c+7] = bf16(sum over the routed slots j of the
-// slot's stage-2 row), slots summed in order j. pos = slot_pos[t*topk + j]
+// One thread: out_row[c .. c+7] = bf16(sum over the routed slots j of token t's
+// stage-2 rows), slots summed in order j. pos = slot_pos[t*topk + j]
 // (-1: dropped); the row is pos (sorted_rows) or t*topk + j. Slots in groups of
 // B: all positions, then all row loads of the group are issued before the
 // sums consume them. Loads go through L2 (the rows may have been written by
 // other CTAs of the same launch).
 template <int B>
 __device__ __forceinline__ void reduce_token_cols(const float* pair, const int32_t* slot_pos, int sorted_rows,
-                                                  int topk, int64_t H, int64_t t, int64_t c, __nv_bfloat16* out) {
+                                                  int topk, int64_t H, int64_t t, int64_t c,
+                                                  __nv_bfloat16* out_row) {
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -136,7 +137,7 @@ __device__ __forceinline__ void reduce_token_cols(const float* pair, const int32
   __nv_bfloat162 o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-  *reinterpret_cast<uint4*>(out + t * H + c) = *reinterpret_cast<const uint4*>(o);
+  *reinterpret_cast<uint4*>(out_row + c) = *reinterpret_cast<const uint4*>(o);
 }
 
 }  // namespace b200moe

@@ -1,5 +1,7 @@
 """Expert-parallel MoE layer: one rank per GPU, experts sharded over ranks,
-tokens exchanged with two equal-split all-to-alls (NCCL over NVLink).
+tokens exchanged either by the kernels themselves through NVLink peer memory
+(exchange="peer", the default on GPUs) or with two equal-split all-to-alls
+(exchange="nccl").
 
 Rank r of G owns experts [r*E/G, (r+1)*E/G). Per forward call:
   1. quantise this rank's tokens 1x128 (fp8 + scales);
@@ -15,6 +17,14 @@ Rank r of G owns experts [r*E/G, (r+1)*E/G). Per forward call:
 Blocks have a fixed size so the exchange needs no count all-to-all and no
 host synchronisation; rows_per_rank is the largest token count any rank passes.
 
+With exchange="peer" steps 2-3 are one kernel (the pack stores each block
+straight into the destination's receive area, mapped through CUDA IPC, and
+raises a flag there), the layer waits for the G flags, and steps 4-5 are one
+kernel (the top-k reduce stores each result row straight into the source
+rank's return area and raises a flag); step 6 waits for those flags. No NCCL
+call on the data path (b200moe_ep_dispatch_peer, b200moe_layer_packed_peer,
+b200moe_ep_combine_peer).
+
 This is the dispatch/combine the reference consumes from DeepEP/Mori
 (sglang_integration/aiter.py:554-756), with the reference's conventions:
 per-group fp8 dispatch with fp32 scales (:614-617) and local ids, -1 for
@@ -22,6 +32,7 @@ experts elsewhere (:660-668).
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional
 
 import torch
@@ -62,16 +73,68 @@ class CudaEPOps:
                                                  _stream(out.device)), "ep_combine")
 
 
+class PeerExchange:
+    """This rank's exchange buffer and the device table of all G buffers as
+    mapped in this process (b200moe_ep_peer_*). Collective: every rank of the
+    group constructs it with the same arguments."""
+
+    def __init__(self, rows_per_rank: int, H: int, topk: int, G: int, rank: int, group, device):
+        lib = _lib.lib()
+        nbytes = lib.b200moe_ep_peer_bytes(rows_per_rank, H, topk, G)
+        if nbytes == 0:
+            raise ValueError("unsupported exchange shape")
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+        _lib.check(lib.b200moe_ep_peer_alloc(nbytes, ctypes.byref(base), handle), "ep_peer_alloc")
+        self.own = base.value
+        self.opened = []
+        handles = [bytes(handle)] * G
+        if G > 1:
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs = []
+        for g in range(G):
+            if g == rank:
+                ptrs.append(self.own)
+                continue
+            p = ctypes.c_void_p()
+            h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES).from_buffer_copy(handles[g])
+            _lib.check(lib.b200moe_ep_peer_open(h, ctypes.byref(p)), "ep_peer_open")
+            self.opened.append(p.value)
+            ptrs.append(p.value)
+        self.bases = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.group = group
+        self.G = G
+        if G > 1:
+            dist.barrier(group=group)  # every buffer mapped everywhere before any rank stores
+
+    def close(self):
+        """Collective: unmap the peers' buffers and free this rank's."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        if self.G > 1:
+            dist.barrier(group=self.group)  # no rank still stores into a buffer being freed
+        lib = _lib.lib()
+        for p in self.opened:
+            _lib.check(lib.b200moe_ep_peer_close(p), "ep_peer_close")
+        _lib.check(lib.b200moe_ep_peer_free(self.own), "ep_peer_free")
+        self.own, self.opened = None, []
+
+
 class ExpertParallelMoE:
     """One rank's share of an expert-parallel MoE layer.
 
     w13 (E/G, 2I, H), w2 (E/G, H, I) fp8 with their 128x128 scales are the
     experts this rank owns. forward() takes this rank's tokens with GLOBAL
     top-k ids and returns their (M, H) bf16 outputs. Every rank must call
-    forward() the same number of times (collectives)."""
+    forward() the same number of times (collectives).
+
+    exchange: "peer" (kernels store into the other GPUs' memory; needs the
+    CUDA ops) or "nccl" (all-to-alls; also runs with the oracle ops on gloo);
+    None picks "peer" for the CUDA ops and "nccl" otherwise."""
 
     def __init__(self, w13, w13_scale, w2, w2_scale, num_experts: int, rows_per_rank: int,
-                 group: Optional[dist.ProcessGroup] = None, ops=None, device=None):
+                 group: Optional[dist.ProcessGroup] = None, ops=None, device=None, exchange: Optional[str] = None):
         self.group = group
         self.G = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -86,6 +149,15 @@ class ExpertParallelMoE:
         self.cap = int(rows_per_rank)
         self.ops = ops or CudaEPOps()
         self.device = torch.device(device) if device is not None else w13.device
+        if exchange is None:
+            exchange = "peer" if isinstance(self.ops, CudaEPOps) else "nccl"
+        if exchange not in ("peer", "nccl"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        if exchange == "peer" and not isinstance(self.ops, CudaEPOps):
+            raise ValueError("the peer exchange runs on the CUDA ops only")
+        self.exchange = exchange
+        self.peer = None
+        self.epoch = 0
         self._topk = None
 
     def _buffers(self, topk: int):
@@ -97,14 +169,21 @@ class ExpertParallelMoE:
         self.row_bytes = rb
         self.q = torch.empty(cap, H, dtype=FP8, device=dev)
         self.s = torch.empty(cap, H // 128, dtype=torch.float32, device=dev)
-        self.send = torch.empty(R * rb, dtype=torch.uint8, device=dev)
-        self.recv = torch.empty(R * rb, dtype=torch.uint8, device=dev)
+        if self.exchange == "peer":
+            if self.peer is not None:
+                self.peer.close()
+            self.peer = PeerExchange(cap, H, topk, G, self.rank, self.group, dev)
+            self.epoch = 0
+        else:
+            self.send = torch.empty(R * rb, dtype=torch.uint8, device=dev)
+            self.recv = torch.empty(R * rb, dtype=torch.uint8, device=dev)
         self.pos = torch.empty(cap * G, dtype=torch.int32, device=dev)
         self.tok_of = torch.empty(R, dtype=torch.int32, device=dev)
         self.counts = torch.empty(G, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.local_out = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
-        self.returned = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+        if self.exchange == "nccl":
+            self.local_out = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+            self.returned = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
         self.ws = torch.empty(max(self.ops.workspace_bytes(R, H, self.I, self.E_local, topk), 256),
                               dtype=torch.uint8, device=dev)
         self.ws[:256].zero_()
@@ -132,6 +211,8 @@ class ExpertParallelMoE:
             out = torch.empty(M, H, dtype=torch.bfloat16, device=self.device)
         rec = (lambda i: events[i].record()) if events is not None else (lambda i: None)
         q, s = self.q[:M], self.s[:M]
+        if self.exchange == "peer":
+            return self._forward_peer(hidden, ids, tw, q, s, out, rec)
         rec(0)
         self.ops.quant(hidden.contiguous(), q, s)
         self.ops.dispatch(q, s, ids, tw, self.E, self.G, self.cap, self.send, self.pos[: M * self.G],
@@ -150,6 +231,38 @@ class ExpertParallelMoE:
         return out
 
     __call__ = forward
+
+    def _forward_peer(self, hidden, ids, tw, q, s, out, rec):
+        """forward() with the exchange inside the kernels: the two all-to-all
+        stages record no time of their own."""
+        lib, M, H, G, cap = _lib.lib(), hidden.shape[0], self.H, self.G, self.cap
+        topk = ids.shape[1]
+        self.epoch += 1
+        st = _stream(self.device)
+        bases, own = _ptr(self.peer.bases), self.peer.own
+        rec(0)
+        self.ops.quant(hidden.contiguous(), q, s)
+        _lib.check(lib.b200moe_ep_dispatch_peer(
+            _ptr(q), _ptr(s), _ptr(ids), _ptr(tw), M, H, topk, self.E, G, self.rank, cap, bases, own, self.epoch,
+            _ptr(self.pos[: M * G]), _ptr(self.tok_of), _ptr(self.counts), _ptr(self.err), st), "ep_dispatch_peer")
+        rec(1)
+        rec(2)
+        _lib.check(lib.b200moe_layer_packed_peer(
+            own, bases, G, self.rank, cap, self.epoch, H, self.I, self.E_local, topk, _ptr(self.w13),
+            _ptr(self.w13_scale), _ptr(self.w2), _ptr(self.w2_scale), _ptr(self.ws), self.ws.numel(), st),
+            "layer_packed_peer")
+        rec(3)
+        rec(4)
+        _lib.check(lib.b200moe_ep_combine_peer(own, _ptr(self.pos[: M * G]), M, H, topk, G, cap, self.epoch,
+                                               _ptr(out), _ptr(self.err), st), "ep_combine_peer")
+        rec(5)
+        return out
+
+    def close(self):
+        """Collective with the peer exchange: release the exchange buffers."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def device_errors(self) -> int:
         """OR of the dispatch and layer device error words (synchronises)."""
