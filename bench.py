@@ -362,6 +362,14 @@ def run_ep(args, shape, config):
                                                      for k in range(args.steps)))
                 for i, name in enumerate(ep.ExpertParallelMoE.STAGES)}
     errs = model.device_errors()
+    # Ours per step: plan, pack (quantising on the way with the peer exchange; a
+    # separate quant before it with NCCL), unpack, route, gather, the experts
+    # launch (two for token-major tiles), top-k reduce, combine. The NCCL
+    # exchange adds its own all-to-all kernels, not counted.
+    from trials_b200.stages import pick_tile_tokens
+
+    experts_launches = 2 if pick_tile_tokens(ws * shape.M * shape.topk, per) > 64 else 1
+    ep_launches = 7 + experts_launches + (0 if args.exchange == "peer" else 1)
 
     e2e = None
     if not args.no_e2e:
@@ -404,9 +412,7 @@ def run_ep(args, shape, config):
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": f"{peak_kind} HBM copy bandwidth",
                          "algorithmic_bytes_per_launch": wbytes, "traffic": None},
-            # quant, plan, pack, unpack, route, gather, experts, reduce, combine (+ the flag wait of the
-            # peer exchange); the NCCL exchange adds its own all-to-all kernels
-            "gpu_launches": (10 if args.exchange == "peer" else 9) * args.steps,
+            "gpu_launches": ep_launches * args.steps,
             "clocks": clk,
         }
         if e2e is not None:

@@ -196,7 +196,9 @@ B200MOE_API int b200moe_ep_combine(const void* returned_rows, const int32_t* pos
  * NVLink peer memory instead of two all-to-alls (one process per GPU; the
  * buffers are shared through CUDA IPC). Same packed rows and results:
  *   b200moe_ep_dispatch_peer   plan + pack, each destination's rows stored
- *                              straight into that rank's receive area; the
+ *                              straight into that rank's receive area (bf16
+ *                              `hidden` is quantised 1x128 on the way, or
+ *                              hidden_q/hidden_scale copied; pass one); the
  *                              last CTA raises this rank's dispatch flag on
  *                              every rank;
  *   b200moe_layer_packed_peer  waits for the G dispatch flags, runs the layer
@@ -225,7 +227,7 @@ B200MOE_API int b200moe_ep_peer_alloc(size_t bytes, void** base, void* ipc_handl
 B200MOE_API int b200moe_ep_peer_open(const void* ipc_handle, void** base);
 B200MOE_API int b200moe_ep_peer_close(void* base);
 B200MOE_API int b200moe_ep_peer_free(void* base);
-B200MOE_API int b200moe_ep_dispatch_peer(const uint8_t* hidden_q, const float* hidden_scale,
+B200MOE_API int b200moe_ep_dispatch_peer(const void* hidden, const uint8_t* hidden_q, const float* hidden_scale,
                                          const int32_t* topk_ids, const float* topk_weights, int64_t M, int64_t H,
                                          int topk, int num_experts, int num_ranks, int rank, int64_t rows_per_rank,
                                          void* const* peer_bases, void* own_base, int32_t epoch, int32_t* pos,

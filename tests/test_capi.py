@@ -76,7 +76,7 @@ def test_peer_exchange_host_checks():
     assert L.b200moe_ep_peer_bytes(cap, H, topk, 65) == 0     # at most 64 ranks
     assert L.b200moe_ep_peer_bytes(cap, 100, topk, G) == 0    # H not a multiple of 128
     # epoch 0, a rank outside the group, an unaligned own buffer: refused before any launch
-    args = [16, 16, 16, 16, 8, H, topk, 16, G]
+    args = [None, 16, 16, 16, 16, 8, H, topk, 16, G]
     assert L.b200moe_ep_dispatch_peer(*args, 0, cap, 256, 256, 0, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG
     assert L.b200moe_ep_dispatch_peer(*args, G, cap, 256, 256, 1, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG
     assert L.b200moe_ep_dispatch_peer(*args, 0, cap, 256, 260, 1, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG

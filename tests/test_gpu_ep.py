@@ -156,7 +156,9 @@ def test_peer_exchange_simulated_ranks_bit_identical_to_all_to_all(cuda_device, 
     """The G ranks' exchange buffers live in one process on one GPU. Every
     kernel of a call is launched after the kernels whose flags it waits for
     (all dispatches, then all layers, then all combines), so no wait depends
-    on a later launch. Three calls exercise both buffer parities."""
+    on a later launch. Three calls exercise both buffer parities; the pack
+    quantises the bf16 rows itself in calls 1 and 3 and copies rows quantised
+    beforehand in call 2."""
     import ctypes
 
     from trials_b200 import _lib
@@ -192,8 +194,11 @@ def test_peer_exchange_simulated_ranks_bit_identical_to_all_to_all(cuda_device, 
                 tok_of = torch.empty(R, dtype=torch.int32, device=dev)
                 counts = torch.empty(G, dtype=torch.int32, device=dev)
                 err = torch.zeros(1, dtype=torch.int32, device=dev)
+                quantise_in_pack = epoch != 2
                 _lib.check(lib.b200moe_ep_dispatch_peer(
-                    q.data_ptr(), s.data_ptr(), ids.data_ptr(), tw.data_ptr(), M, H, topk, SHAPE.E, G, r, cap,
+                    hidden.data_ptr() if quantise_in_pack else None, None if quantise_in_pack else q.data_ptr(),
+                    None if quantise_in_pack else s.data_ptr(), ids.data_ptr(), tw.data_ptr(), M, H, topk, SHAPE.E,
+                    G, r, cap,
                     table.data_ptr(), bases[r], epoch, pos.data_ptr(), tok_of.data_ptr(), counts.data_ptr(),
                     err.data_ptr(), st), "dispatch_peer")
                 state.append((pos, err))

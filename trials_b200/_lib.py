@@ -53,8 +53,8 @@ SIGNATURES = {
     "b200moe_ep_peer_open": (_I, [_P, ctypes.POINTER(_P)]),
     "b200moe_ep_peer_close": (_I, [_P]),
     "b200moe_ep_peer_free": (_I, [_P]),
-    "b200moe_ep_dispatch_peer": (_I, [_P, _P, _P, _P, _L, _L, _I, _I, _I, _I, _L, _P, _P, ctypes.c_int32, _P, _P, _P,
-                                      _P, _P]),
+    "b200moe_ep_dispatch_peer": (_I, [_P, _P, _P, _P, _P, _L, _L, _I, _I, _I, _I, _L, _P, _P, ctypes.c_int32, _P, _P,
+                                      _P, _P, _P]),
     "b200moe_layer_packed_peer": (_I, [_P, _P, _I, _I, _L, ctypes.c_int32, _L, _L, _I, _I, _P, _P, _P, _P, _P, _S,
                                        _P]),
     "b200moe_ep_combine_peer": (_I, [_P, _P, _L, _L, _I, _I, _L, ctypes.c_int32, _P, _P, _P]),

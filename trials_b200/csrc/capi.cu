@@ -798,17 +798,19 @@ bool peer_args_ok(int num_ranks, int rank, int64_t rows_per_rank, int32_t epoch,
 }
 }  // namespace
 
-int b200moe_ep_dispatch_peer(const uint8_t* hidden_q, const float* hidden_scale, const int32_t* topk_ids,
-                             const float* topk_weights, int64_t M, int64_t H, int topk, int num_experts,
+int b200moe_ep_dispatch_peer(const void* hidden, const uint8_t* hidden_q, const float* hidden_scale,
+                             const int32_t* topk_ids, const float* topk_weights, int64_t M, int64_t H, int topk,
+                             int num_experts,
                              int num_ranks, int rank, int64_t rows_per_rank, void* const* peer_bases, void* own_base,
                              int32_t epoch, int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err_word,
                              void* stream) {
   if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || num_experts % num_ranks != 0 || !err_word || !counts ||
       !peer_args_ok(num_ranks, rank, rows_per_rank, epoch, peer_bases, own_base) ||
-      (M > 0 && (!hidden_q || !hidden_scale || !topk_ids || !topk_weights || !pos)) ||
+      (M > 0 && (!(hidden || (hidden_q && hidden_scale)) || !topk_ids || !topk_weights || !pos)) ||
       (rows_per_rank > 0 && !tok_of))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_dispatch_peer: bad argument%s");
-  if (!aligned16(hidden_q)) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_dispatch_peer: 16-byte alignment%s");
+  if (!aligned16(hidden) || !aligned16(hidden_q))
+    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_dispatch_peer: 16-byte alignment%s");
   const int64_t rb = b200moe_ep_row_bytes(H, topk);
   const EpPeerLayout lay(rows_per_rank, H, rb, num_ranks);
   cudaStream_t s = (cudaStream_t)stream;
@@ -819,8 +821,8 @@ int b200moe_ep_dispatch_peer(const uint8_t* hidden_q, const float* hidden_scale,
   const EpPeerArgs a{reinterpret_cast<uint8_t* const*>(peer_bases), lay.recv_off(epoch), rows_per_rank, num_ranks,
                      rank, epoch};
   int32_t* counter = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(own_base) + EpPeerLayout::kCounters);
-  return cuda_status(launch_ep_pack_peer(hidden_q, hidden_scale, topk_ids, topk_weights, H, topk, num_experts, tok_of,
-                                         counts, rb, a, counter, s),
+  return cuda_status(launch_ep_pack_peer(hidden, hidden_q, hidden_scale, topk_ids, topk_weights, H, topk,
+                                         num_experts, tok_of, counts, rb, a, counter, s),
                      "ep_pack_peer");
 }
 
@@ -839,10 +841,6 @@ int b200moe_layer_packed_peer(void* own_base, void* const* peer_bases, int num_r
   if (R > 0 && workspace_bytes < b200moe_layer_packed_workspace_size(R, H, I, num_local_experts, topk))
     return fail(B200MOE_ERR_WORKSPACE, "b200moe_layer_packed_peer: workspace too small%s");
   int32_t* err = static_cast<int32_t*>(workspace);
-  int st = cuda_status(launch_ep_wait_flags(reinterpret_cast<const int32_t*>(own + EpPeerLayout::kDispatchFlags),
-                                            num_ranks, epoch, err, kPeerWaitNs, s),
-                       "ep_wait_flags");
-  if (st) return st;
   const EpPeerArgs a{reinterpret_cast<uint8_t* const*>(peer_bases), lay.ret_off(epoch), rows_per_rank, num_ranks,
                      rank, epoch};
   int32_t* counter = reinterpret_cast<int32_t*>(own + EpPeerLayout::kCounters) + 1;
@@ -852,7 +850,10 @@ int b200moe_layer_packed_peer(void* own_base, void* const* peer_bases, int num_r
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* ids = reinterpret_cast<int32_t*>(ws + 256);
   float* w = reinterpret_cast<float*>(ids + R * topk);
-  st = cuda_status(launch_ep_unpack_meta(rows, R, rb, H, topk, ids, w, s), "ep_unpack_meta");
+  // waits for the G dispatch flags, then unpacks the ids and weights
+  int st = cuda_status(launch_ep_unpack_meta_peer(own, rows, R, rb, H, topk, num_ranks, epoch, ids, w, err,
+                                                  kPeerWaitNs, s),
+                       "ep_unpack_meta_peer");
   if (st) return st;
   LayerInput in{nullptr, rows, rb, reinterpret_cast<const float*>(rows + H), rb / 4};
   return layer_core("b200moe_layer_packed_peer", in, R, H, I, num_local_experts, topk, w13, w13_scale, w2, w2_scale, w,

@@ -80,9 +80,14 @@ __device__ __forceinline__ void signal_done(const EpPeerArgs& a, int64_t flag_of
   }
 }
 
-// One warp per destination row, as ep_pack_kernel, with the row stored into
-// the destination's receive area (row rank*rows_per_rank + r).
-__global__ void __launch_bounds__(256) ep_pack_peer_kernel(const uint8_t* __restrict__ q, const float* __restrict__ s,
+// One warp per (destination row, 1024-column segment), the rows as
+// ep_pack_kernel builds them, stored into the destination's receive area (row
+// rank*rows_per_rank + r). With bf16 input the warp quantises its segment 1x128
+// on the way (the arithmetic of b200moe_quant_1x128, once per destination);
+// otherwise it copies the fp8 bytes and scales. Segment 0 writes the ids and
+// weights.
+__global__ void __launch_bounds__(256) ep_pack_peer_kernel(const __nv_bfloat16* __restrict__ hidden,
+                                                           const uint8_t* __restrict__ q, const float* __restrict__ s,
                                                            const int32_t* __restrict__ ids,
                                                            const float* __restrict__ w, int64_t H, int topk,
                                                            int num_experts, const int32_t* __restrict__ tok_of,
@@ -90,6 +95,7 @@ __global__ void __launch_bounds__(256) ep_pack_peer_kernel(const uint8_t* __rest
                                                            const EpPeerArgs a, int32_t* counter) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t seg0 = (int64_t)blockIdx.y * kQuantSegCols;
   if (row < (int64_t)a.G * a.rows_per_rank) {
     const int d = (int)(row / a.rows_per_rank);
     const int64_t r = row - (int64_t)d * a.rows_per_rank;
@@ -97,21 +103,27 @@ __global__ void __launch_bounds__(256) ep_pack_peer_kernel(const uint8_t* __rest
     uint8_t* dst = a.bases[d] + a.area_off + ((int64_t)a.rank * a.rows_per_rank + r) * row_bytes;
     int32_t* dst_ids = reinterpret_cast<int32_t*>(dst + H + (H / 128) * 4);
     float* dst_w = reinterpret_cast<float*>(dst_ids + topk);
-    if (r >= __ldg(&counts[d])) {
-      for (int j = lane; j < topk; j += 32) {
-        dst_ids[j] = -1;
-        dst_w[j] = 0.f;
+    const bool used = r < __ldg(&counts[d]);
+    const int64_t t = used ? __ldg(&tok_of[row]) : 0;
+    if (used) {
+      // a one-row view: input row t, output row 0 of a zero-stride destination
+      QuantArgs qa{};
+      qa.K = H;
+      qa.q = dst;
+      qa.s = reinterpret_cast<float*>(dst + H);
+      qa.s_grp = 1;
+      if (hidden) {
+        qa.x = hidden + t * H;
+      } else {
+        qa.xq = q + t * H;
+        qa.xs = s + t * (H / 128);
       }
-    } else {
-      const int64_t t = __ldg(&tok_of[row]);
-      const uint4* src = reinterpret_cast<const uint4*>(q + t * H);
-      uint4* out = reinterpret_cast<uint4*>(dst);
-      for (int64_t i = lane; i < H / 16; i += 32) out[i] = __ldg(&src[i]);
-      float* dst_s = reinterpret_cast<float*>(dst + H);
-      for (int64_t g = lane; g < H / 128; g += 32) dst_s[g] = __ldg(&s[t * (H / 128) + g]);
+      quant_row_segment(qa, 0, seg0, lane);
+    }
+    if (blockIdx.y == 0) {
       for (int j = lane; j < topk; j += 32) {
-        const int id = __ldg(&ids[t * topk + j]);
-        const bool mine = id >= 0 && id < num_experts && id / per_rank == d;
+        const int id = used ? __ldg(&ids[t * topk + j]) : -1;
+        const bool mine = used && id >= 0 && id < num_experts && id / per_rank == d;
         dst_ids[j] = mine ? id - d * per_rank : -1;
         dst_w[j] = mine ? __ldg(&w[t * topk + j]) : 0.f;
       }
@@ -120,8 +132,19 @@ __global__ void __launch_bounds__(256) ep_pack_peer_kernel(const uint8_t* __rest
   signal_done(a, EpPeerLayout::kDispatchFlags, counter);
 }
 
-__global__ void ep_wait_flags_kernel(const int32_t* flags, int G, int32_t epoch, int32_t* err, uint64_t limit_ns) {
-  wait_flags(flags, G, epoch, err, limit_ns);
+// Packed rows -> contiguous (R, topk) ids and weights (as ep_unpack_meta_kernel),
+// once the G dispatch flags of this epoch are up.
+__global__ void ep_unpack_meta_peer_kernel(const uint8_t* own, const uint8_t* rows, int64_t R, int64_t row_bytes,
+                                           int64_t H, int topk, int G, int32_t epoch, int32_t* __restrict__ ids,
+                                           float* __restrict__ w, int32_t* err, uint64_t limit_ns) {
+  wait_flags(reinterpret_cast<const int32_t*>(own + EpPeerLayout::kDispatchFlags), G, epoch, err, limit_ns);
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= R * topk) return;
+  const int64_t r = i / topk;
+  const int j = (int)(i - r * topk);
+  const int32_t* src = reinterpret_cast<const int32_t*>(rows + r * row_bytes + H + (H / 128) * 4);
+  ids[i] = __ldcg(&src[j]);  // stored by other GPUs during this kernel's wait: read through L2
+  w[i] = __ldcg(reinterpret_cast<const float*>(src + topk) + j);
 }
 
 // Top-k reduce of the received rows (R = G*rows_per_rank, row i = row
@@ -184,19 +207,26 @@ __global__ void __launch_bounds__(256) ep_combine_peer_kernel(const uint8_t* own
 
 }  // namespace
 
-cudaError_t launch_ep_pack_peer(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t H,
-                                int topk, int num_experts, const int32_t* tok_of, const int32_t* counts,
-                                int64_t row_bytes, const EpPeerArgs& a, int32_t* counter, cudaStream_t stream) {
+cudaError_t launch_ep_pack_peer(const void* hidden, const uint8_t* q, const float* s, const int32_t* ids,
+                                const float* w, int64_t H, int topk, int num_experts, const int32_t* tok_of,
+                                const int32_t* counts, int64_t row_bytes, const EpPeerArgs& a, int32_t* counter,
+                                cudaStream_t stream) {
   const int64_t rows = (int64_t)a.G * a.rows_per_rank;
-  const int64_t blocks = rows > 0 ? (rows + 7) / 8 : 1;  // one CTA at least, to raise the flags
-  ep_pack_peer_kernel<<<(unsigned)blocks, 256, 0, stream>>>(q, s, ids, w, H, topk, num_experts, tok_of, counts,
-                                                             row_bytes, a, counter);
+  const dim3 grid((unsigned)(rows > 0 ? (rows + 7) / 8 : 1),  // one CTA at least, to raise the flags
+                  (unsigned)((H + kQuantSegCols - 1) / kQuantSegCols));
+  ep_pack_peer_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(hidden), q, s, ids, w,
+                                                             H, topk, num_experts, tok_of, counts, row_bytes, a,
+                                                             counter);
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_wait_flags(const int32_t* flags, int G, int32_t epoch, int32_t* err, uint64_t limit_ns,
-                                 cudaStream_t stream) {
-  ep_wait_flags_kernel<<<1, 64, 0, stream>>>(flags, G, epoch, err, limit_ns);
+cudaError_t launch_ep_unpack_meta_peer(const uint8_t* own, const uint8_t* rows, int64_t R, int64_t row_bytes,
+                                       int64_t H, int topk, int G, int32_t epoch, int32_t* ids, float* w,
+                                       int32_t* err, uint64_t limit_ns, cudaStream_t stream) {
+  const int64_t n = R * topk;
+  const int64_t blocks = n > 0 ? (n + 255) / 256 : 1;
+  ep_unpack_meta_peer_kernel<<<(unsigned)blocks, 256, 0, stream>>>(own, rows, R, row_bytes, H, topk, G, epoch, ids,
+                                                                    w, err, limit_ns);
   return cudaGetLastError();
 }
 

@@ -111,11 +111,13 @@ struct EpPeerArgs {
   int G, rank;
   int32_t epoch;
 };
-cudaError_t launch_ep_pack_peer(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t H,
-                                int topk, int num_experts, const int32_t* tok_of, const int32_t* counts,
-                                int64_t row_bytes, const EpPeerArgs& a, int32_t* counter, cudaStream_t stream);
-cudaError_t launch_ep_wait_flags(const int32_t* flags, int G, int32_t epoch, int32_t* err, uint64_t limit_ns,
-                                 cudaStream_t stream);
+cudaError_t launch_ep_pack_peer(const void* hidden, const uint8_t* q, const float* s, const int32_t* ids,
+                                const float* w, int64_t H, int topk, int num_experts, const int32_t* tok_of,
+                                const int32_t* counts, int64_t row_bytes, const EpPeerArgs& a, int32_t* counter,
+                                cudaStream_t stream);
+cudaError_t launch_ep_unpack_meta_peer(const uint8_t* own, const uint8_t* rows, int64_t R, int64_t row_bytes,
+                                       int64_t H, int topk, int G, int32_t epoch, int32_t* ids, float* w,
+                                       int32_t* err, uint64_t limit_ns, cudaStream_t stream);
 cudaError_t launch_ep_reduce_peer(const float* pair, const int32_t* slot_pos, int sorted_rows, int topk, int64_t H,
                                   const EpPeerArgs& a, int32_t* counter, cudaStream_t stream);
 cudaError_t launch_ep_combine_peer(const uint8_t* own, int64_t area_off, const int32_t* pos, int64_t M, int64_t H,

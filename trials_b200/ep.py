@@ -241,9 +241,10 @@ class ExpertParallelMoE:
         st = _stream(self.device)
         bases, own = _ptr(self.peer.bases), self.peer.own
         rec(0)
-        self.ops.quant(hidden.contiguous(), q, s)
+        # the pack kernel quantises each token row on its way to the destinations
         _lib.check(lib.b200moe_ep_dispatch_peer(
-            _ptr(q), _ptr(s), _ptr(ids), _ptr(tw), M, H, topk, self.E, G, self.rank, cap, bases, own, self.epoch,
+            _ptr(hidden.contiguous()), None, None, _ptr(ids), _ptr(tw), M, H, topk, self.E, G, self.rank, cap, bases,
+            own, self.epoch,
             _ptr(self.pos[: M * G]), _ptr(self.tok_of), _ptr(self.counts), _ptr(self.err), st), "ep_dispatch_peer")
         rec(1)
         rec(2)
