@@ -279,15 +279,19 @@ B200MOE_API int b200moe_layer_noalloc(const void* hidden, int64_t M, int64_t H, 
  * (nullable, M*topk entries) receives the sorted row of every flat slot
  * t*topk+j, or -1 for a dropped slot (for b200moe_combine_reduce). chunk_ready
  * (nullable, chunks_capacity + 2 entries) is zeroed for b200moe_experts and
- * b200moe_experts_fused.
+ * b200moe_experts_fused. route_scratch (nullable) with route_scratch_ints >=
+ * b200moe_route_scratch_ints(M*topk, E) entries lets large batches (from
+ * 16,384 routed slots) route on several CTAs in two launches (same result);
+ * without it one CTA routes everything.
  * ---------------------------------------------------------------------- */
 B200MOE_API int64_t b200moe_route_capacity_rows(int64_t numel, int num_local_experts);
 B200MOE_API int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_experts, int tile_tokens);
+B200MOE_API int64_t b200moe_route_scratch_ints(int64_t numel, int num_local_experts);
 B200MOE_API int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
                   int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
                   int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
                   int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
-                  int32_t* err_word, void* stream);
+                  int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream);
 
 /* Quantise hidden rows into the sorted layout: for every flat slot f with
  * p = slot_pos[f] >= 0 (from b200moe_route), row p of a_q (ld = H) holds

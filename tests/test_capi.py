@@ -51,7 +51,8 @@ def test_host_side_argument_checks():
     # K not a multiple of 128
     assert L.b200moe_quant_1x128(16, 4, 100, 100, 16, 100, 16, 1, 1, None) == _lib.ERR_INVALID_ARG
     # tile size outside {16, 32, 64, 128}
-    assert L.b200moe_route(16, 4, 2, 8, None, 8, 48, 16, 1000, 16, 16, 16, 1000, 16, 16, None, None, 16, None) == \
+    assert L.b200moe_route(16, 4, 2, 8, None, 8, 48, 16, 1000, 16, 16, 16, 1000, 16, 16, None, None, None, 0, 16,
+                           None) == \
         _lib.ERR_INVALID_ARG
     # too many experts
     assert L.b200moe_align(16, 4, 2, 2000, 128, None, 0, 16, 1 << 20, 16, 1 << 20, 16, 16, None) == \

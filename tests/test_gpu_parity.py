@@ -125,6 +125,51 @@ def test_route_chunks_exact(cuda_device, M, E, topk, tile):
     assert np.array_equal(got, chunks)
 
 
+def _same_routing(a, b):
+    nc = int(a.counts[0].item())
+    for name in ("sorted_ids", "counts", "slot_pos", "err"):
+        assert torch.equal(getattr(a, name), getattr(b, name)), name
+    for name in ("chunk_expert", "chunk_row0", "chunk_rows"):  # defined up to n_chunks
+        assert torch.equal(getattr(a, name)[:nc], getattr(b, name)[:nc]), name
+
+
+@pytest.mark.parametrize("M,E,topk,tile,skew,minus_one", [(4096, 256, 8, 128, 0, 0.0), (8192, 256, 8, 128, 16, 0.0),
+                                                        (3000, 64, 8, 64, 0, 0.2), (2048, 1024, 8, 32, 0, 0.0)])
+def test_route_on_several_ctas_equals_one_cta(cuda_device, M, E, topk, tile, skew, minus_one):
+    """From 16,384 routed slots routing runs on several CTAs; the result is the
+    one-CTA kernel's and the oracle's, slot positions included."""
+    from trials_b200 import _lib
+
+    assert _lib.lib().b200moe_route_scratch_ints(M * topk, E) > 0
+    ids = _ids(M, E, topk, seed=M + 7, skew=skew, minus_one=minus_one)
+    multi = stages.route(ids.to(cuda_device), E, tile)
+    one = stages.route(ids.to(cuda_device), E, tile, multi_cta=False)
+    _same_routing(multi, one)
+    assert int(multi.err.item()) == 0
+    rs, rn, chunks = orc.route_chunks(ids.numpy(), E, tile)
+    assert int(multi.counts[1].item()) == rn
+    assert np.array_equal(multi.sorted_ids.cpu().numpy()[:rn], rs[:rn])
+    pos = multi.slot_pos.cpu().numpy()
+    flat = ids.numpy().reshape(-1)
+    routed = flat >= 0
+    assert (pos[~routed] == -1).all()
+    assert np.array_equal(multi.sorted_ids.cpu().numpy()[pos[routed]], np.nonzero(routed)[0])
+
+
+def test_route_on_several_ctas_expert_map_and_bad_ids(cuda_device):
+    M, E, topk = 4096, 64, 8
+    ids = _ids(M, E, topk, seed=11)
+    ids[5, 1] = 77
+    ids[4000, 0] = -5
+    emap = torch.full((E,), -1, dtype=torch.int32)
+    emap[8:24] = torch.arange(16, dtype=torch.int32)
+    multi = stages.route(ids.to(cuda_device), E, 128, expert_map=emap.to(cuda_device), num_local_experts=16)
+    one = stages.route(ids.to(cuda_device), E, 128, expert_map=emap.to(cuda_device), num_local_experts=16,
+                       multi_cta=False)
+    _same_routing(multi, one)
+    assert int(multi.err.item()) & 1
+
+
 # ----------------------------------------------------------------------------
 # GEMM stages
 # ----------------------------------------------------------------------------

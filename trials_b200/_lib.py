@@ -61,7 +61,8 @@ SIGNATURES = {
     "b200moe_layer_noalloc": (_I, [_P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P]),
     "b200moe_route_capacity_rows": (_L, [_L, _I]),
     "b200moe_route_capacity_chunks": (_L, [_L, _I, _I]),
-    "b200moe_route": (_I, [_P, _L, _I, _I, _P, _I, _I, _P, _L, _P, _P, _P, _L, _P, _P, _P, _P, _P, _P]),
+    "b200moe_route_scratch_ints": (_L, [_L, _I]),
+    "b200moe_route": (_I, [_P, _L, _I, _I, _P, _I, _I, _P, _L, _P, _P, _P, _L, _P, _P, _P, _P, _P, _L, _P, _P]),
     "b200moe_gather_quant": (_I, [_P, _L, _L, _I, _P, _L, _P, _P, _L, _P]),
     "b200moe_gather_rows": (_I, [_P, _P, _L, _L, _L, _L, _I, _P, _L, _P, _P, _L, _P]),
     "b200moe_gemm1_silu": (_I, [_P, _P, _L, _L, _P, _P, _I, _L, _L, _P, _P, _P, _P, _L, _I, _P, _P, _P, _I, _P]),

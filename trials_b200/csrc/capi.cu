@@ -116,7 +116,8 @@ struct LayerPlan {
   int tile_tokens;
   int64_t rows_cap, chunks_cap, as_ld;
   size_t off_sorted, off_pos, off_ce, off_cr0, off_crows, off_ready, off_counts, off_a1, off_a1s, off_a2, off_a2s,
-      off_pair, off_tq, off_ts, total;
+      off_pair, off_tq, off_ts, off_rscratch, total;
+  int64_t rscratch_ints;  // routing on several CTAs (large batches)
   bool token_quant;  // quantise each token once, then copy rows (large batches)
 };
 
@@ -151,6 +152,8 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
     p.off_tq = take((size_t)M * H);
     p.off_ts = take(sizeof(float) * (size_t)M * (H / 128));
   }
+  p.rscratch_ints = route_scratch_ints(numel, E_local);
+  if (p.rscratch_ints > 0) p.off_rscratch = take(sizeof(int32_t) * (size_t)p.rscratch_ints);
   p.total = off;
   return p;
 }
@@ -303,11 +306,16 @@ int64_t b200moe_route_capacity_chunks(int64_t numel, int num_local_experts, int 
   return ceil_div(b200moe_route_capacity_rows(numel, num_local_experts), tile_tokens) + num_local_experts;
 }
 
+int64_t b200moe_route_scratch_ints(int64_t numel, int num_local_experts) {
+  if (numel < 0 || num_local_experts <= 0) return 0;
+  return route_scratch_ints(numel, num_local_experts);
+}
+
 int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
                   int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
                   int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
-                  int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready, int32_t* err_word,
-                  void* stream) {
+                  int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
+                  int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream) {
   if (M < 0 || topk <= 0 || num_experts <= 0 || !valid_tile(tile_tokens) || !sorted_ids || !chunk_expert ||
       !chunk_row0 || !chunk_rows || !n_chunks || !num_rows || !err_word || (M > 0 && !topk_ids))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_route: bad argument%s");
@@ -339,7 +347,7 @@ int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts,
   a.chunk_ready = chunk_ready;
   a.slot_pos = slot_pos;
   a.err = err_word;
-  return cuda_status(launch_align(a, (cudaStream_t)stream), "route");
+  return cuda_status(launch_route(a, route_scratch, route_scratch_ints, (cudaStream_t)stream), "route");
 }
 
 int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* slot_pos,
@@ -627,8 +635,9 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   float* a2s = reinterpret_cast<float*>(wl + pl.off_a2s);
   float* pair = reinterpret_cast<float*>(wl + pl.off_pair);
 
+  int32_t* rscratch = pl.rscratch_ints > 0 ? reinterpret_cast<int32_t*>(wl + pl.off_rscratch) : nullptr;
   st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,
-                     crows, pl.chunks_cap, counts, counts + 1, pos, ready, err, stream);
+                     crows, pl.chunks_cap, counts, counts + 1, pos, ready, rscratch, pl.rscratch_ints, err, stream);
   if (st) return st;
   LayerInput src = in;
   if (in.hidden && pl.token_quant) {

@@ -35,6 +35,11 @@ struct AlignArgs {
 
 size_t align_smem_bytes(int E);
 cudaError_t launch_align(const AlignArgs& a, cudaStream_t stream);
+// Routing of large batches on several CTAs (two launches) when scratch holds
+// route_scratch_ints() entries; otherwise launch_align.
+int route_ctas(int64_t n);
+int64_t route_scratch_ints(int64_t n, int E);
+cudaError_t launch_route(const AlignArgs& a, int32_t* scratch, int64_t scratch_ints, cudaStream_t stream);
 
 // Per-token-group (1 x 128) FP8 quantisation. With sorted_ids != nullptr the
 // output row p takes its input from token sorted_ids[p] / topk (zeros for the

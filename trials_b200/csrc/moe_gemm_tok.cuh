@@ -95,6 +95,10 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
 #ifndef B200MOE_TOK_W_POLICY
 #define B200MOE_TOK_W_POLICY 0
 #endif
+// L2 hint on token-major activation tiles: 1 evict_last, 0 none.
+#ifndef B200MOE_TOK_A_POLICY
+#define B200MOE_TOK_A_POLICY 1
+#endif
 #ifndef B200MOE_TOK_FFMA2
 #define B200MOE_TOK_FFMA2 1
 #endif
@@ -185,7 +189,10 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
           }
           uint8_t* tile = tiles + stage * C::TILE_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::TILE_BYTES);
-          tma_load_2d(tile, &tm_a, &full[stage], kb * 128, p0, pol_a);
+          if (B200MOE_TOK_A_POLICY)
+            tma_load_2d(tile, &tm_a, &full[stage], kb * 128, p0, pol_a);
+          else
+            tma_load_2d(tile, &tm_a, &full[stage], kb * 128, p0);
           if (B200MOE_TOK_W_POLICY == 1 || B200MOE_TOK_W_POLICY == 2)
             tma_load_2d(tile + C::A_BYTES, &tm_w, &full[stage], kb * 128, wrow, pol_w);
           else

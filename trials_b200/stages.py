@@ -54,7 +54,10 @@ class Routing:
 
 
 def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map: Optional[torch.Tensor] = None,
-          num_local_experts: Optional[int] = None, err: Optional[torch.Tensor] = None) -> Routing:
+          num_local_experts: Optional[int] = None, err: Optional[torch.Tensor] = None,
+          multi_cta: bool = True) -> Routing:
+    """Routing into expert-sorted rows and the GEMM work list. multi_cta=False
+    keeps large batches on the one-CTA kernel (the two give the same result)."""
     dev = _require_cuda(topk_ids)
     ids = topk_ids.to(torch.int32).contiguous()
     M, topk = ids.shape
@@ -68,10 +71,12 @@ def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map
                 err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev), z(chunks_cap + 2), z(M * topk))
     if expert_map is not None:
         expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
+    ns = L.b200moe_route_scratch_ints(M * topk, E) if multi_cta else 0
+    scratch = torch.empty(ns, dtype=torch.int32, device=dev) if ns > 0 else None
     _lib.check(L.b200moe_route(_ptr(ids), M, topk, num_experts, _ptr(expert_map), E, tile_tokens,
                                _ptr(r.sorted_ids), rows_cap, _ptr(r.chunk_expert), _ptr(r.chunk_row0),
                                _ptr(r.chunk_rows), chunks_cap, _ptr(r.n_chunks), _ptr(r.num_rows), _ptr(r.slot_pos),
-                               _ptr(r.chunk_ready), _ptr(r.err), _stream(dev)), "route")
+                               _ptr(r.chunk_ready), _ptr(scratch), ns, _ptr(r.err), _stream(dev)), "route")
     return r
 
 
@@ -246,6 +251,8 @@ class LayerPipeline:
             z(self.chunks_cap)
         self.ready = z(self.chunks_cap + 2)
         self.slot_pos = z(numel)
+        self.rscratch_ints = L.b200moe_route_scratch_ints(numel, self.E)
+        self.rscratch = z(self.rscratch_ints)
         self.split = split
         # One launch after routing (b200moe_experts_fused) on request: measured
         # equal at 64 tokens and 24 us slower at 128 than the three launches.
@@ -279,7 +286,8 @@ class LayerPipeline:
         _lib.check(L.b200moe_route(_ptr(topk_ids), M, topk, self.num_experts, _ptr(self.expert_map), E, self.tile,
                                    _ptr(self.sorted_ids), self.rows_cap, _ptr(self.ce), _ptr(self.cr0),
                                    _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.slot_pos),
-                                   _ptr(self.ready), _ptr(self.err), st), "route")
+                                   _ptr(self.ready), _ptr(self.rscratch), self.rscratch_ints, _ptr(self.err), st),
+                   "route")
         rec(1)
         if self.one_launch:
             _lib.check(L.b200moe_experts_fused(_ptr(hidden), M, topk, _ptr(self.slot_pos), _ptr(self.a1), _ptr(self.a1s),
