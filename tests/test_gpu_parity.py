@@ -297,7 +297,7 @@ def test_schedule_invariance_bit_exact(cuda_device, grid, tile):
 
 @pytest.mark.parametrize("shape,tile,grid", [(synth.TINY, 32, 0), (SMALL, 16, 0), (SMALL, 32, 0), (SMALL, 64, 0),
                                              (SMALL, 32, 1), (SMALL, 32, 5), (SMALL, 64, 37), (SMALL, 32, 148),
-                                             (SMALL, 128, 0)])
+                                             (SMALL, 128, 0), (SMALL, 128, 1), (SMALL, 128, 7)])
 def test_fused_experts_bit_identical_to_split(cuda_device, shape, tile, grid):
     """Both GEMM stages in one launch (stage-2 units wait per chunk on the
     stage-1 units) give exactly the two-launch results, for any grid."""

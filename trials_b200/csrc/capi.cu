@@ -399,11 +399,17 @@ int b200moe_gather_rows(const uint8_t* xq, const float* xs, int64_t ldxq, int64_
   return cuda_status(launch_quant_1x128(a, (cudaStream_t)stream), "gather_rows");
 }
 
-int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
-                       const uint8_t* w13, const float* w13_scale, int num_local_experts, int64_t H, int64_t I,
-                       const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
-                       const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens, uint8_t* a2_q,
-                       float* a2_sT, int32_t* err_word, int grid_ctas, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The stage launches behind b200moe_gemm1_silu / b200moe_gemm2_combine;
+// unit_counter (zeroed, or nullptr) gives token-major tiles a dynamic unit queue.
+int gemm1_silu_core(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
+                    const uint8_t* w13, const float* w13_scale, int num_local_experts, int64_t H, int64_t I,
+                    const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
+                    const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens, uint8_t* a2_q,
+                    float* a2_sT, int32_t* err_word, int grid_ctas, void* stream, int32_t* unit_counter) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 ||
@@ -418,17 +424,18 @@ int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, 
   p.out_sT = a2_sT;
   p.out_s_ld = a_s_ld;
   p.err = err_word;
+  p.unit_counter = unit_counter;
   return run_gemm(EPI_SILU, a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, 2 * I, H,
                   chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, p, grid_ctas,
                   (cudaStream_t)stream);
 }
 
-int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, int64_t rows_capacity,
-                          const uint8_t* w2, const float* w2_scale, int num_local_experts, int64_t H, int64_t I,
-                          const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
-                          const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
-                          const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
-                          float* out_pair, int32_t* err_word, int grid_ctas, void* stream) {
+int gemm2_combine_core(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, int64_t rows_capacity,
+                       const uint8_t* w2, const float* w2_scale, int num_local_experts, int64_t H, int64_t I,
+                       const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
+                       const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
+                       const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
+                       float* out_pair, int32_t* err_word, int grid_ctas, void* stream, int32_t* unit_counter) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 || M < 0 || topk <= 0 ||
@@ -444,9 +451,35 @@ int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_l
   p.sentinel = (int32_t)(M * topk);
   p.out_pair = out_pair;
   p.err = err_word;
+  p.unit_counter = unit_counter;
   return run_gemm(EPI_COMBINE, a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I,
                   chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, p, grid_ctas,
                   (cudaStream_t)stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
+                       const uint8_t* w13, const float* w13_scale, int num_local_experts, int64_t H, int64_t I,
+                       const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
+                       const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens, uint8_t* a2_q,
+                       float* a2_sT, int32_t* err_word, int grid_ctas, void* stream) {
+  return gemm1_silu_core(a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, H, I, chunk_expert,
+                         chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, a2_q, a2_sT, err_word,
+                         grid_ctas, stream, nullptr);
+}
+
+int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, int64_t rows_capacity,
+                          const uint8_t* w2, const float* w2_scale, int num_local_experts, int64_t H, int64_t I,
+                          const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
+                          const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
+                          const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
+                          float* out_pair, int32_t* err_word, int grid_ctas, void* stream) {
+  return gemm2_combine_core(a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I, chunk_expert,
+                            chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, sorted_ids,
+                            topk_weights, M, topk, out_pair, err_word, grid_ctas, stream, nullptr);
 }
 
 int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
@@ -457,14 +490,17 @@ int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int
                     const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, float* out_pair,
                     int32_t* err_word, int grid_ctas, void* stream) {
   if (tile_tokens > 64) {
-    // Token-major tiles: the two stages as two launches.
-    int st = b200moe_gemm1_silu(a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, H, I,
-                                chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, a2_q,
-                                a2_sT, err_word, grid_ctas, stream);
+    // Token-major tiles: the two stages as two launches, each taking its units
+    // from a counter after chunk_ready's per-chunk entries (zeroed by routing).
+    int32_t* q1 = chunk_ready ? chunk_ready + chunks_capacity : nullptr;
+    int st = gemm1_silu_core(a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, H, I,
+                             chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, a2_q,
+                             a2_sT, err_word, grid_ctas, stream, q1);
     if (st) return st;
-    return b200moe_gemm2_combine(a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I,
-                                 chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens,
-                                 sorted_ids, topk_weights, M, topk, out_pair, err_word, grid_ctas, stream);
+    return gemm2_combine_core(a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I,
+                              chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens,
+                              sorted_ids, topk_weights, M, topk, out_pair, err_word, grid_ctas, stream,
+                              q1 ? q1 + 1 : nullptr);
   }
   int st = check_gemm_shapes(H, I);
   if (st) return st;

@@ -101,6 +101,9 @@ struct GemmParams {
   int red_topk;
   // unit order: chunks per group (see unit_coords); 1 = chunk-major
   int chunk_group;
+  // token-major kernels: a zeroed counter from which CTAs take their next unit
+  // (dynamic queue); nullptr = static round-robin over the grid
+  int32_t* unit_counter;
   // diagnostics
   int32_t* err;
   uint64_t timeout_ns;

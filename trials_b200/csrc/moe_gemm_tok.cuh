@@ -37,6 +37,7 @@ struct TokCfg {
   static constexpr int SMEM_LIMIT = 232448;
   static constexpr int MAX_STAGE = 6;
   static constexpr int XPOSE = EW * 32 * 20 * 4;  // stage-2 store transpose blocks
+  static constexpr int NU = 4;                    // unit hand-off ring (producer -> MMA, epilogue)
   static constexpr int FIXED = 1024 + RED + (MAX_STAGE + NBUF) * S_BYTES + 1024 + XPOSE;
   static constexpr int NSTAGE_RAW = (SMEM_LIMIT - FIXED) / TILE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > MAX_STAGE ? MAX_STAGE : NSTAGE_RAW;
@@ -120,11 +121,16 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
   uint64_t* tempty = tfull + C::NBUF;
   uint64_t* sfull = tempty + C::NBUF;
   uint64_t* sempty = sfull + C::NSLOT;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + C::NSLOT);
+  uint64_t* ufull = sempty + C::NSLOT;
+  uint64_t* uempty = ufull + C::NU;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(uempty + C::NU);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // The epilogue's stop decision for a unit, written by one thread before the
   // unit's first named barrier so that every epilogue warp reads the same value.
   volatile int* stop_sh = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  // Units in the order the producer takes them (-1 = no more), read by the MMA
+  // thread and every epilogue warp before the slot is reused.
+  volatile int* unit_sh = reinterpret_cast<volatile int*>(tmem_slot + 4);
   float* xpose = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 1024);  // EW x 32 x 20
 
   const int warp = threadIdx.x >> 5;
@@ -144,6 +150,10 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
     for (int s = 0; s < C::NSLOT; ++s) {
       mbar_init(&sfull[s], 1);
       mbar_init(&sempty[s], EW);
+    }
+    for (int s = 0; s < C::NU; ++s) {
+      mbar_init(&ufull[s], 1);
+      mbar_init(&uempty[s], 1 + EW);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -171,11 +181,27 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
       // H/256 units of a chunk: neither may be evicted first.
       const uint64_t pol_w = B200MOE_TOK_W_POLICY == 2 ? policy_evict_last() : policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
-      int stage = 0, slot = 0;
-      uint32_t phase = 0, sphase = 0;
+      int stage = 0, slot = 0, uslot = 0;
+      uint32_t phase = 0, sphase = 0, uphase = 0;
       long issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      // Units come from the shared counter when there is one (a CTA takes the
+      // next unit when it is ready for it, so units that share weight tiles
+      // through L2 keep running at the same time), else round-robin.
+      for (int k = 0; ok; ++k) {
+        int u = p.unit_counter ? atomicAdd(p.unit_counter, 1) : (int)blockIdx.x + k * (int)gridDim.x;
+        if (u >= n_units) u = -1;
+        if (*abort_flag || !mbar_wait_bounded(&uempty[uslot], uphase ^ 1, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        unit_sh[uslot] = u;
+        mbar_arrive(&ufull[uslot]);
+        if (++uslot == C::NU) {
+          uslot = 0;
+          uphase ^= 1;
+        }
+        if (u < 0) break;
         int chunk, nt;
         unit_coords(u, n_chunks, NT, p.chunk_group, chunk, nt);
         const int e = __ldg(&p.chunk_expert[chunk]);
@@ -228,10 +254,21 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
       int stage = 0, buf = 0;
       uint32_t phase = 0, bphase = 0;
       long committed = 0;
-      int last_buf = 0;
-      uint32_t last_bphase = 0;
+      int last_buf = 0, uslot = 0;
+      uint32_t last_bphase = 0, uphase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      while (ok) {
+        if (*abort_flag || !mbar_wait_bounded(&ufull[uslot], uphase, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        const int u = unit_sh[uslot];
+        mbar_arrive(&uempty[uslot]);
+        if (++uslot == C::NU) {
+          uslot = 0;
+          uphase ^= 1;
+        }
+        if (u < 0) break;
         for (int kb = 0; kb < NKB; ++kb) {
           if (*abort_flag || !mbar_wait_bounded(&tempty[buf], bphase ^ 1, p.timeout_ns)) {
             ok = false;
@@ -295,8 +332,23 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
       wl0 = lane < NKB ? __ldg(w + lane) : 0.f;
       wl1 = lane + 32 < NKB ? __ldg(w + lane + 32) : 0.f;
     };
-    if (blockIdx.x < n_units) load_ws(blockIdx.x);
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x, parity ^= 1) {
+    int uslot = 0;
+    uint32_t uphase = 0;
+    // The next unit of the producer's sequence (-1: none left, -2: timed out).
+    auto next_unit = [&]() -> int {
+      if (!mbar_wait_bounded(&ufull[uslot], uphase, p.timeout_ns)) return -2;
+      const int v = unit_sh[uslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&uempty[uslot]);
+      if (++uslot == C::NU) {
+        uslot = 0;
+        uphase ^= 1;
+      }
+      return v;
+    };
+    int u = next_unit();
+    if (u >= 0) load_ws(u);
+    for (int nu = -1; u >= 0; u = nu, parity ^= 1) {
       int chunk, nt;
       unit_coords(u, n_chunks, NT, p.chunk_group, chunk, nt);
       const int e = __ldg(&p.chunk_expert[chunk]);
@@ -370,7 +422,8 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
         atomicOr(p.err, ERR_DEV_TIMEOUT);
         *abort_flag = 1;
       }
-      if (u + (int)gridDim.x < n_units) load_ws(u + gridDim.x);
+      nu = ok ? next_unit() : -1;
+      if (nu >= 0) load_ws(nu);
 
       if constexpr (EPI == EPI_SILU) {
         // inter column i of this half = silu(acc[2i]) * acc[2i+1]; group of 128
@@ -418,6 +471,10 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
                             p.out_pair + (int64_t)p0 * p.Nw + nt * C::UNIT_ROWS + h * 128, p.Nw);
         }
       }
+    }
+    if (u == -2) {  // the producer never handed over the next unit
+      atomicOr(p.err, ERR_DEV_TIMEOUT);
+      *abort_flag = 1;
     }
   }
 
