@@ -532,7 +532,7 @@ def run_ours(args, shape, config):
             stage_ms["gemm1_silu"]
         traffic_name = f"gemm1_silu_glm_decode_m{shape.M}{hot}"
     achieved = k_bytes / (k_ms / 1e3) / 1e9
-    launches = (len(pipe.stages) + (1 if not args.split and pipe.tile > 64 else 0) + (1 if pipe.token_quant else 0) +
+    launches = (len(pipe.stages) + (1 if not args.split and pipe.tile > 64 else 0) +
                 (1 if pipe.rscratch_ints > 0 else 0))  # routing on several CTAs: two launches
     step_bytes = layer_bytes(shape, active, pairs)
     line = {

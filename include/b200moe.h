@@ -297,16 +297,19 @@ B200MOE_API int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int 
  * p = slot_pos[f] >= 0 (from b200moe_route), row p of a_q (ld = H) holds
  * q(hidden[f / topk]) and its scales go to a_sT[g * a_s_ld + p] (transposed).
  * Padding rows are not written (a padding row only feeds GEMM outputs that are
- * discarded). a_s_ld >= rows_capacity. */
+ * discarded). a_s_ld >= rows_capacity. From 2,048 routed slots on (topk <= 32)
+ * each token is quantised once and stored to all its slot rows; below, every
+ * slot row is quantised on its own (same bytes either way). */
 B200MOE_API int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* slot_pos,
                          int64_t rows_capacity, uint8_t* a_q, float* a_sT, int64_t a_s_ld, void* stream);
 
 /* Copy already quantised rows into the sorted layout: for every flat slot f
  * with p = slot_pos[f] >= 0, row p of a_q (ld = H) = xq[f / topk] (row stride
  * ldxq bytes, 16-byte aligned), its scales xs[t * ldxs + g] to
- * a_sT[g * a_s_ld + p]. Padding rows are not written. With
- * b200moe_quant_1x128 first, this is the layer's activation path for large
- * batches (each token quantised once, then copied). */
+ * a_sT[g * a_s_ld + p]. Padding rows are not written. The activation path of
+ * the layer entries that take quantised rows (b200moe_layer_quantized,
+ * b200moe_layer_packed); per token from 2,048 routed slots on, as
+ * b200moe_gather_quant. */
 B200MOE_API int b200moe_gather_rows(const uint8_t* xq, const float* xs, int64_t ldxq, int64_t ldxs, int64_t M, int64_t H,
                         int topk, const int32_t* slot_pos, int64_t rows_capacity, uint8_t* a_q, float* a_sT,
                         int64_t a_s_ld, void* stream);

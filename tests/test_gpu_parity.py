@@ -263,8 +263,9 @@ def test_one_launch_layer_bit_identical(cuda_device, shape, tile, grid):
 
 @pytest.mark.parametrize("M,tile", [(16, 32), (300, 64), (600, 128)])
 def test_gather_rows_equals_gather_quant(cuda_device, M, tile):
-    """Quantise each token once + copy rows (the large-batch path) gives the
-    same routed rows and scales as quantising every routed copy."""
+    """Quantising in the gather and copying rows quantised beforehand give the
+    same routed rows and scales (per-slot warps at M=16 and 300, per-token
+    fan-out at 600)."""
     shape = synth.LayerShape(M=M, H=512, I=256, E=16, topk=4, scoring="sigmoid")
     L, g = _tiny_layer(cuda_device, shape, seed=3)
     r = stages.route(g["topk_ids"], shape.E, tile)
@@ -276,6 +277,30 @@ def test_gather_rows_equals_gather_quant(cuda_device, M, tile):
     valid = torch.as_tensor(r.sorted_ids[:n_rows].cpu().numpy() < M * shape.topk)
     assert torch.equal(_u8(a_q[:n_rows][valid]), _u8(b_q[:n_rows][valid]))
     assert torch.equal(a_sT[:, :n_rows].T.cpu()[valid], b_sT[:, :n_rows].T.cpu()[valid])
+
+
+@pytest.mark.parametrize("M,topk,minus_one", [(16, 4, 0.0), (600, 4, 0.0), (700, 8, 0.2), (300, 8, 0.0)])
+def test_gathered_rows_are_token_quant_at_slot_rows(cuda_device, M, topk, minus_one):
+    """Both gathers (one warp per slot below 2,048 routed pairs, one per token
+    storing to all its slots from there on) put token t's 1x128 quantisation
+    at every routed slot's sorted row."""
+    E = 16
+    ids = _ids(M, E, topk, seed=M + topk, minus_one=minus_one)
+    g = torch.Generator().manual_seed(M)
+    hidden = torch.randn(M, 512, generator=g).to(torch.bfloat16).to(cuda_device)
+    r = stages.route(ids.to(cuda_device), E, 64)
+    a_q, a_sT = stages.gather_quant(hidden, topk, r)
+    tq, ts = moe.per_token_group_quant_fp8(hidden)
+    b_q, b_sT = stages.gather_rows(tq, ts, topk, r)
+    torch.cuda.synchronize()
+    pos = r.slot_pos.cpu().long()
+    routed = pos >= 0
+    assert bool(routed.any())
+    tok = torch.arange(M * topk)[routed] // topk
+    want_q, want_s = _u8(tq)[tok], ts.cpu()[tok]
+    for q, sT in ((a_q, a_sT), (b_q, b_sT)):
+        assert torch.equal(_u8(q)[pos[routed]], want_q)
+        assert torch.equal(sT.cpu().T[pos[routed]], want_s)
 
 
 @pytest.mark.parametrize("grid,tile", [(1, 32), (5, 32), (37, 32), (1, 128), (7, 128), (3, 64), (2, 256),

@@ -101,12 +101,13 @@ constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per pipeline wait
 #define B200MOE_CHUNK_GROUP_SWAP 1
 #endif
 
-// From this many routed (token, slot) pairs on, the layer quantises each token
-// once and copies its fp8 row into the routed positions (two launches),
-// instead of quantising every routed copy (one launch): topk-fold less
-// conversion work, which outweighs the extra launch at prefill sizes.
-constexpr int64_t kTokenQuantMinPairs = 2048;
-bool token_quant_first(int64_t numel) { return numel >= kTokenQuantMinPairs; }
+// From this many routed (token, slot) pairs on, the gather runs one warp per
+// (token, segment) that quantises (or loads) the token's segment once and
+// stores it to each of its slot rows, instead of one warp per (slot, segment):
+// topk-fold fewer loads and conversions, at the cost of fewer, longer warps,
+// which only pays at prefill sizes.
+constexpr int64_t kFanOutMinPairs = 2048;
+bool fan_out_tokens(int64_t numel, int topk) { return numel >= kFanOutMinPairs && topk <= 32; }
 
 // Stage-2 output row layout of a tile size: token-major tiles (128, 256)
 // write rows in sorted order, the swap-AB tiles one row per slot.
@@ -116,9 +117,8 @@ struct LayerPlan {
   int tile_tokens;
   int64_t rows_cap, chunks_cap, as_ld;
   size_t off_sorted, off_pos, off_ce, off_cr0, off_crows, off_ready, off_counts, off_a1, off_a1s, off_a2, off_a2s,
-      off_pair, off_tq, off_ts, off_rscratch, total;
+      off_pair, off_rscratch, total;
   int64_t rscratch_ints;  // routing on several CTAs (large batches)
-  bool token_quant;  // quantise each token once, then copy rows (large batches)
 };
 
 LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
@@ -147,11 +147,6 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
   p.off_a2s = take(sizeof(float) * (size_t)(I / 128) * p.as_ld);
   // Token-major tiles write sorted rows (rows_cap of them), the others slot rows.
   p.off_pair = take(sizeof(float) * (size_t)(pair_sorted_rows(p.tile_tokens) ? p.rows_cap : numel) * H);
-  p.token_quant = token_quant_first(numel);
-  if (p.token_quant) {
-    p.off_tq = take((size_t)M * H);
-    p.off_ts = take(sizeof(float) * (size_t)M * (H / 128));
-  }
   p.rscratch_ints = route_scratch_ints(numel, E_local);
   if (p.rscratch_ints > 0) p.off_rscratch = take(sizeof(int32_t) * (size_t)p.rscratch_ints);
   p.total = off;
@@ -361,7 +356,11 @@ int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, con
   a.x = hidden;
   a.ldx = H;
   a.K = H;
-  a.rows = M * topk;  // one launch row per flat slot
+  // Large batches: one launch row per token, quantised once and stored to each
+  // of its slot rows; small ones: one launch row per flat slot.
+  const bool fan = fan_out_tokens(M * topk, topk);
+  a.rows = fan ? M : M * topk;
+  a.fanout = fan ? 1 : 0;
   a.slot_pos = slot_pos;
   a.topk = topk;
   a.sentinel = (int32_t)(M * topk);
@@ -387,7 +386,9 @@ int b200moe_gather_rows(const uint8_t* xq, const float* xs, int64_t ldxq, int64_
   a.xs = xs;
   a.ldxs = ldxs;
   a.K = H;
-  a.rows = M * topk;  // one launch row per flat slot
+  const bool fan = fan_out_tokens(M * topk, topk);  // as b200moe_gather_quant
+  a.rows = fan ? M : M * topk;
+  a.fanout = fan ? 1 : 0;
   a.slot_pos = slot_pos;
   a.topk = topk;
   a.sentinel = (int32_t)(M * topk);
@@ -675,14 +676,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,
                      crows, pl.chunks_cap, counts, counts + 1, pos, ready, rscratch, pl.rscratch_ints, err, stream);
   if (st) return st;
-  LayerInput src = in;
-  if (in.hidden && pl.token_quant) {
-    uint8_t* tq = wl + pl.off_tq;
-    float* ts = reinterpret_cast<float*>(wl + pl.off_ts);
-    st = b200moe_quant_1x128(in.hidden, M, H, H, tq, H, ts, H / 128, 1, stream);
-    if (st) return st;
-    src = LayerInput{nullptr, tq, H, ts, H / 128};
-  }
+  const LayerInput& src = in;
   if (src.hidden) {
     st = b200moe_gather_quant(in.hidden, M, H, topk, pos, pl.rows_cap, a1, a1s, pl.as_ld, stream);
   } else {

@@ -62,6 +62,9 @@ struct QuantArgs {
   // row slot_pos[r] (skipped when -1).
   const int32_t* slot_pos;
   int topk;
+  // With slot_pos: row r of the launch is token r instead (rows = M), written
+  // to every one of its slots' rows slot_pos[r*topk + j] (topk <= 32).
+  int fanout;
   int32_t sentinel;
   uint8_t* q;
   int64_t ldq;

@@ -15,12 +15,18 @@ constexpr int kQuantSegCols = 256 * kQuantSegSteps;
 // One warp: launch row `row` of `a` (see QuantArgs), columns seg0 .. seg0+1023.
 // Each lane converts 8 consecutive bf16 per 16-byte load, a half-warp covers
 // one 128-column group, and the warp issues the loads of its four 256-column
-// steps before it reduces any of them (one load round trip per row).
+// steps before it reduces any of them (one load round trip per row). In fan-out
+// mode the segment is quantised (or loaded) once and stored to each of the
+// token's slot rows.
 __device__ __forceinline__ void quant_row_segment(const QuantArgs& a, int64_t row, int64_t seg0, int lane) {
   const int64_t seg_end = seg0 + kQuantSegCols < a.K ? seg0 + kQuantSegCols : a.K;
   int64_t src = row, dst = row;
   int32_t pos = 0;
-  if (a.slot_pos) {
+  const bool fan = a.slot_pos && a.fanout;
+  if (fan) {
+    src = row;  // lane j holds the row of slot j; consumed after the loads are issued
+    pos = lane < a.topk ? __ldg(&a.slot_pos[row * a.topk + lane]) : -1;
+  } else if (a.slot_pos) {
     src = row / a.topk;
     pos = __ldg(&a.slot_pos[row]);  // consumed after the row's loads are issued
   } else if (a.sorted_ids) {
@@ -42,17 +48,27 @@ __device__ __forceinline__ void quant_row_segment(const QuantArgs& a, int64_t ro
     const int64_t g = (seg0 >> 7) + lane;
     const bool gs = lane < kQuantSegCols / 128 && g * 128 < seg_end;
     const float sv = gs ? __ldg(&a.xs[src * a.ldxs + g]) : 0.f;
+    auto put = [&](int64_t d) {
+      uint8_t* qr = a.q + d * a.ldq;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int64_t b = seg0 + lane * 16 + i * 512;
+        if (b < seg_end) *reinterpret_cast<uint4*>(qr + b) = v[i];
+      }
+      if (gs) a.s[d * a.s_row + g * a.s_grp] = sv;
+    };
+    if (fan) {
+      for (int j = 0; j < a.topk; ++j) {
+        const int d = __shfl_sync(0xffffffffu, pos, j);
+        if (d >= 0) put(d);
+      }
+      return;
+    }
     if (a.slot_pos) {
       if (pos < 0) return;
       dst = pos;
     }
-    uint8_t* qr = a.q + dst * a.ldq;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int64_t b = seg0 + lane * 16 + i * 512;
-      if (b < seg_end) *reinterpret_cast<uint4*>(qr + b) = v[i];
-    }
-    if (gs) a.s[dst * a.s_row + g * a.s_grp] = sv;
+    put(dst);
     return;
   }
   const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(a.x) + src * a.ldx;
@@ -74,30 +90,49 @@ __device__ __forceinline__ void quant_row_segment(const QuantArgs& a, int64_t ro
       for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
     }
   }
-  if (a.slot_pos) {
-    if (pos < 0) return;
-    dst = pos;
-  }
-  uint8_t* qr = a.q + dst * a.ldq;
+  uint2 packed[kQuantSegSteps];
+  float scl[kQuantSegSteps];
 #pragma unroll
   for (int i = 0; i < kQuantSegSteps; ++i) {
-    if (seg0 + i * 256 >= seg_end) break;  // warp-uniform
-    const int64_t c = seg0 + i * 256 + lane * 8;
+    packed[i] = make_uint2(0, 0);
+    scl[i] = 0.f;
+    if (seg0 + i * 256 >= seg_end) continue;  // warp-uniform
     float m = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[i][j]));
 #pragma unroll
     for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (c >= seg_end) continue;
     uint32_t lo = 0, hi = 0;
     const float scale = group_scale(m);
 #pragma unroll
     for (int j = 0; j < 4; ++j) lo |= (uint32_t)quant_e4m3(v[i][j], scale) << (8 * j);
 #pragma unroll
     for (int j = 0; j < 4; ++j) hi |= (uint32_t)quant_e4m3(v[i][4 + j], scale) << (8 * j);
-    *reinterpret_cast<uint2*>(qr + c) = make_uint2(lo, hi);
-    if ((lane & 15) == 0) a.s[dst * a.s_row + (c >> 7) * a.s_grp] = scale;
+    packed[i] = make_uint2(lo, hi);
+    scl[i] = scale;
   }
+  auto put = [&](int64_t d) {
+    uint8_t* qr = a.q + d * a.ldq;
+#pragma unroll
+    for (int i = 0; i < kQuantSegSteps; ++i) {
+      const int64_t c = seg0 + i * 256 + lane * 8;
+      if (c >= seg_end) continue;
+      *reinterpret_cast<uint2*>(qr + c) = packed[i];
+      if ((lane & 15) == 0) a.s[d * a.s_row + (c >> 7) * a.s_grp] = scl[i];
+    }
+  };
+  if (fan) {
+    for (int j = 0; j < a.topk; ++j) {
+      const int d = __shfl_sync(0xffffffffu, pos, j);
+      if (d >= 0) put(d);
+    }
+    return;
+  }
+  if (a.slot_pos) {
+    if (pos < 0) return;
+    dst = pos;
+  }
+  put(dst);
 }
 
 // One thread: out_row[c .. c+7] = bf16(sum over the routed slots j of token t's

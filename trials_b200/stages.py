@@ -206,9 +206,10 @@ def selftest_wait_timeout(err: torch.Tensor, timeout_us: int = 20000) -> None:
     _lib.check(_lib.lib().b200moe_selftest_wait_timeout(_ptr(err), timeout_us, _stream(dev)), "selftest")
 
 
-# From this many routed pairs on, hidden rows are quantised once per token and
-# then copied into the sorted layout (the same rule as the C layer, capi.cu).
-TOKEN_QUANT_MIN_PAIRS = 2048
+# From this many routed pairs on, the gather quantises each token once and
+# stores it to all its slot rows (the same rule as the C layer, capi.cu); below
+# it the one-launch layer is eligible.
+FAN_OUT_MIN_PAIRS = 2048
 
 
 def pick_tile_tokens(numel: int, num_local_experts: int) -> int:
@@ -256,7 +257,7 @@ class LayerPipeline:
         self.split = split
         # One launch after routing (b200moe_experts_fused) on request: measured
         # equal at 64 tokens and 24 us slower at 128 than the three launches.
-        eligible = (not split) and self.tile <= 64 and M * topk < TOKEN_QUANT_MIN_PAIRS
+        eligible = (not split) and self.tile <= 64 and M * topk < FAN_OUT_MIN_PAIRS
         self.one_launch = bool(one_launch) and eligible
         self.stages = self.SPLIT_STAGES if split else (self.LAYER_STAGES if self.one_launch else self.FUSED_STAGES)
         self.counts = z(2)
@@ -268,10 +269,6 @@ class LayerPipeline:
         self.sorted_rows = 1 if self.tile > 64 else 0
         self.pair = torch.zeros(max(self.rows_cap if self.sorted_rows else numel, 1), H, dtype=torch.float32,
                                 device=device)
-        self.token_quant = numel >= TOKEN_QUANT_MIN_PAIRS
-        if self.token_quant:
-            self.tq = torch.zeros(M, H, dtype=FP8, device=device)
-            self.ts = torch.zeros(M, H // 128, dtype=torch.float32, device=device)
         self.out = torch.zeros(M, H, dtype=torch.bfloat16, device=device)
 
     def run(self, hidden, topk_ids, topk_weights, w13, w13_scale, w2, w2_scale, events=None, grid_ctas: int = 0):
@@ -299,15 +296,8 @@ class LayerPipeline:
                        "experts_fused")
             rec(2)
             return self.out
-        if self.token_quant:
-            _lib.check(L.b200moe_quant_1x128(_ptr(hidden), M, H, H, _ptr(self.tq), H, _ptr(self.ts), H // 128, 1, st),
-                       "quant_1x128")
-            _lib.check(L.b200moe_gather_rows(_ptr(self.tq), _ptr(self.ts), H, H // 128, M, H, topk,
-                                             _ptr(self.slot_pos), self.rows_cap, _ptr(self.a1), _ptr(self.a1s),
-                                             self.ld, st), "gather_rows")
-        else:
-            _lib.check(L.b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(self.slot_pos), self.rows_cap,
-                                              _ptr(self.a1), _ptr(self.a1s), self.ld, st), "gather_quant")
+        _lib.check(L.b200moe_gather_quant(_ptr(hidden), M, H, topk, _ptr(self.slot_pos), self.rows_cap,
+                                          _ptr(self.a1), _ptr(self.a1s), self.ld, st), "gather_quant")
         rec(2)
         if not self.split:
             _lib.check(L.b200moe_experts(_ptr(self.a1), _ptr(self.a1s), self.ld, self.rows_cap, _ptr(w13),
