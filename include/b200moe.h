@@ -325,7 +325,8 @@ B200MOE_API int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int6
                        float* a2_sT, int32_t* err_word, int grid_ctas, void* stream);
 
 /* Stage 2: topk_weights[f] * (a2 . w2^T)[p, :] for every sorted row p with
- * f = sorted_ids[p] < M*topk, as an f32 row of H. Tiles of 16..64 tokens
+ * f = sorted_ids[p] < M*topk, accumulated in fp32 and stored as a bf16 row of H
+ * (the reference rounds this product to bf16 too, aiter.py:164-177). Tiles of 16..64 tokens
  * write it to row f of out_pair (M*topk, H); token-major tiles (128, 256) to
  * row p of out_pair (rows_capacity, H), which keeps a unit's rows together in
  * memory. Padding rows and dropped slots are not written. */
@@ -334,7 +335,7 @@ B200MOE_API int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, i
                           const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
                           const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
                           const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
-                          float* out_pair, int32_t* err_word, int grid_ctas, void* stream);
+                          void* out_pair, int32_t* err_word, int grid_ctas, void* stream);
 
 /* Stage 1 and stage 2 in one persistent launch (the reference's fused
  * stage-1 / stage-2 launcher pair, moe_decode_megakernel_fused.py:125-157,
@@ -350,7 +351,7 @@ B200MOE_API int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t
                     int num_local_experts, int64_t H, int64_t I, const int32_t* chunk_expert,
                     const int32_t* chunk_row0, const int32_t* chunk_rows, const int32_t* n_chunks,
                     int64_t chunks_capacity, int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
-                    const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, float* out_pair,
+                    const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, void* out_pair,
                     int32_t* err_word, int grid_ctas, void* stream);
 
 /* Everything after b200moe_route for small batches (tiles of 16..64 tokens),
@@ -370,15 +371,16 @@ B200MOE_API int b200moe_experts_fused(const void* hidden, int64_t M, int topk, c
                           int64_t H, int64_t I, const int32_t* chunk_expert, const int32_t* chunk_row0,
                           const int32_t* chunk_rows, const int32_t* n_chunks, int64_t chunks_capacity,
                           int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
-                          const int32_t* sorted_ids, const float* topk_weights, float* out_pair, void* out,
+                          const int32_t* sorted_ids, const float* topk_weights, void* out_pair, void* out,
                           int32_t* err_word, int grid_ctas, void* stream);
 
 /* out[t, :] = bf16( sum_j row_j ) over the slots j with slot_pos[t*topk + j]
- * >= 0 (from b200moe_route), summed in order j = 0..topk-1; row_j is
+ * >= 0 (from b200moe_route), the bf16 rows summed in fp32 in order
+ * j = 0..topk-1; row_j is
  * out_pair[slot_pos[t*topk + j]] when sorted_rows is non-zero (token-major
  * tiles), else out_pair[t*topk + j]. Replaces the unpermute of
  * sglang_integration/aiter.py:164-177. */
-B200MOE_API int b200moe_combine_reduce(const float* out_pair, const int32_t* slot_pos, int sorted_rows, int64_t M,
+B200MOE_API int b200moe_combine_reduce(const void* out_pair, const int32_t* slot_pos, int sorted_rows, int64_t M,
                            int topk, int64_t H, void* out, void* stream);
 
 /* ------------------------------------------------------------------------

@@ -225,7 +225,9 @@ def test_gather_and_gemm_stages(cuda_device, shape, tile):
         got_pair = pair.cpu()[:n_rows][torch.as_tensor(valid)]
     else:
         got_pair = pair.cpu()[torch.as_tensor(sorted_ids[valid], dtype=torch.long)]
-    assert orc.rel_l2(got_pair, ref_pair) < 1e-5
+    # fp32 accumulation, then one bf16 rounding of each weighted row
+    assert orc.rel_l2(got_pair, ref_pair) < 4e-3
+    assert orc.rel_l2(got_pair, ref_pair.float().to(torch.bfloat16)) < 1e-3
 
     # slot positions: the inverse of the routed part of sorted_ids
     pos = r.slot_pos.cpu().numpy()
@@ -235,7 +237,7 @@ def test_gather_and_gemm_stages(cuda_device, shape, tile):
     # top-k reduce: slot rows gathered by position, summed in slot order
     out = stages.combine_reduce(pair, r, shape.M, topk)
     by_slot = torch.zeros(shape.M * topk, shape.H, dtype=torch.float32)
-    by_slot[torch.as_tensor(sorted_ids[valid], dtype=torch.long)] = got_pair
+    by_slot[torch.as_tensor(sorted_ids[valid], dtype=torch.long)] = got_pair.float()
     ref_out = by_slot.view(shape.M, topk, shape.H).sum(1).to(torch.bfloat16)
     assert orc.rel_l2(out, ref_out) < 1e-2 ** 2
     assert int(r.err.item()) == 0

@@ -146,7 +146,7 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk) {
   p.off_a2 = take((size_t)p.rows_cap * I);
   p.off_a2s = take(sizeof(float) * (size_t)(I / 128) * p.as_ld);
   // Token-major tiles write sorted rows (rows_cap of them), the others slot rows.
-  p.off_pair = take(sizeof(float) * (size_t)(pair_sorted_rows(p.tile_tokens) ? p.rows_cap : numel) * H);
+  p.off_pair = take(sizeof(__nv_bfloat16) * (size_t)(pair_sorted_rows(p.tile_tokens) ? p.rows_cap : numel) * H);
   p.rscratch_ints = route_scratch_ints(numel, E_local);
   if (p.rscratch_ints > 0) p.off_rscratch = take(sizeof(int32_t) * (size_t)p.rscratch_ints);
   p.total = off;
@@ -436,7 +436,7 @@ int gemm2_combine_core(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, 
                        const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
                        const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
                        const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
-                       float* out_pair, int32_t* err_word, int grid_ctas, void* stream, int32_t* unit_counter) {
+                       void* out_pair, int32_t* err_word, int grid_ctas, void* stream, int32_t* unit_counter) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 || M < 0 || topk <= 0 ||
@@ -450,7 +450,7 @@ int gemm2_combine_core(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, 
   p.sorted_ids = sorted_ids;
   p.topk_w = topk_weights;
   p.sentinel = (int32_t)(M * topk);
-  p.out_pair = out_pair;
+  p.out_pair = static_cast<__nv_bfloat16*>(out_pair);
   p.err = err_word;
   p.unit_counter = unit_counter;
   return run_gemm(EPI_COMBINE, a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I,
@@ -477,7 +477,7 @@ int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_l
                           const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
                           const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
                           const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
-                          float* out_pair, int32_t* err_word, int grid_ctas, void* stream) {
+                          void* out_pair, int32_t* err_word, int grid_ctas, void* stream) {
   return gemm2_combine_core(a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I, chunk_expert,
                             chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, sorted_ids,
                             topk_weights, M, topk, out_pair, err_word, grid_ctas, stream, nullptr);
@@ -488,7 +488,7 @@ int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int
                     int num_local_experts, int64_t H, int64_t I, const int32_t* chunk_expert,
                     const int32_t* chunk_row0, const int32_t* chunk_rows, const int32_t* n_chunks,
                     int64_t chunks_capacity, int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
-                    const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, float* out_pair,
+                    const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, void* out_pair,
                     int32_t* err_word, int grid_ctas, void* stream) {
   if (tile_tokens > 64) {
     // Token-major tiles: the two stages as two launches, each taking its units
@@ -530,7 +530,7 @@ int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int
   p2.sorted_ids = sorted_ids;
   p2.topk_w = topk_weights;
   p2.sentinel = (int32_t)(M * topk);
-  p2.out_pair = out_pair;
+  p2.out_pair = static_cast<__nv_bfloat16*>(out_pair);
   p2.err = err_word;
   const int64_t units_cap = chunks_capacity * ((2 * I) / 256 + H / 256);
   int64_t grid = grid_ctas > 0 ? grid_ctas : sm_count();
@@ -546,7 +546,7 @@ int b200moe_experts_fused(const void* hidden, int64_t M, int topk, const int32_t
                           int64_t H, int64_t I, const int32_t* chunk_expert, const int32_t* chunk_row0,
                           const int32_t* chunk_rows, const int32_t* n_chunks, int64_t chunks_capacity,
                           int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
-                          const int32_t* sorted_ids, const float* topk_weights, float* out_pair, void* out,
+                          const int32_t* sorted_ids, const float* topk_weights, void* out_pair, void* out,
                           int32_t* err_word, int grid_ctas, void* stream) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
@@ -597,7 +597,7 @@ int b200moe_experts_fused(const void* hidden, int64_t M, int topk, const int32_t
   p2.sorted_ids = sorted_ids;
   p2.topk_w = topk_weights;
   p2.sentinel = (int32_t)(M * topk);
-  p2.out_pair = out_pair;
+  p2.out_pair = static_cast<__nv_bfloat16*>(out_pair);
   p2.err = err_word;
   const int64_t units_cap = chunks_capacity * ((2 * I) / 256 + H / 256);
   int64_t grid = grid_ctas > 0 ? grid_ctas : sm_count();
@@ -607,7 +607,7 @@ int b200moe_experts_fused(const void* hidden, int64_t M, int topk, const int32_t
                      "experts_fused");
 }
 
-int b200moe_combine_reduce(const float* out_pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
+int b200moe_combine_reduce(const void* out_pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
                            int64_t H, void* out, void* stream) {
   if (M < 0 || topk <= 0 || H <= 0 || H % 8 != 0 || (M > 0 && (!out_pair || !slot_pos || !out)))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_combine_reduce: bad argument%s");
@@ -670,7 +670,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   float* a1s = reinterpret_cast<float*>(wl + pl.off_a1s);
   uint8_t* a2 = wl + pl.off_a2;
   float* a2s = reinterpret_cast<float*>(wl + pl.off_a2s);
-  float* pair = reinterpret_cast<float*>(wl + pl.off_pair);
+  __nv_bfloat16* pair = reinterpret_cast<__nv_bfloat16*>(wl + pl.off_pair);
 
   int32_t* rscratch = pl.rscratch_ints > 0 ? reinterpret_cast<int32_t*>(wl + pl.off_rscratch) : nullptr;
   st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,

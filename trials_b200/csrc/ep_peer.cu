@@ -151,7 +151,7 @@ __global__ void ep_unpack_meta_peer_kernel(const uint8_t* own, const uint8_t* ro
 // i % rows_per_rank of source rank i / rows_per_rank), each bf16 result row
 // stored into the source rank's return area at row rank*rows_per_rank + r.
 template <int B>
-__global__ void __launch_bounds__(256) ep_reduce_peer_kernel(const float* __restrict__ pair,
+__global__ void __launch_bounds__(256) ep_reduce_peer_kernel(const __nv_bfloat16* __restrict__ pair,
                                                              const int32_t* __restrict__ slot_pos, int sorted_rows,
                                                              int topk, int64_t H, const EpPeerArgs a,
                                                              int32_t* counter) {
@@ -230,7 +230,7 @@ cudaError_t launch_ep_unpack_meta_peer(const uint8_t* own, const uint8_t* rows, 
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_reduce_peer(const float* pair, const int32_t* slot_pos, int sorted_rows, int topk, int64_t H,
+cudaError_t launch_ep_reduce_peer(const __nv_bfloat16* pair, const int32_t* slot_pos, int sorted_rows, int topk, int64_t H,
                                   const EpPeerArgs& a, int32_t* counter, cudaStream_t stream) {
   const int64_t R = (int64_t)a.G * a.rows_per_rank;
   const int64_t n = R * (H / 8);

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -77,7 +78,7 @@ cudaError_t launch_quant_1x128(const QuantArgs& a, cudaStream_t stream);
 cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K, uint8_t* q, float* s,
                                   cudaStream_t stream);
 
-cudaError_t launch_combine_reduce(const float* pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
+cudaError_t launch_combine_reduce(const void* pair_rows, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
                                   int64_t H, void* out, cudaStream_t stream);
 
 cudaError_t launch_ep_plan(const int32_t* ids, int64_t M, int topk, int num_experts, int G, int64_t rows_per_rank,
@@ -126,7 +127,7 @@ cudaError_t launch_ep_pack_peer(const void* hidden, const uint8_t* q, const floa
 cudaError_t launch_ep_unpack_meta_peer(const uint8_t* own, const uint8_t* rows, int64_t R, int64_t row_bytes,
                                        int64_t H, int topk, int G, int32_t epoch, int32_t* ids, float* w,
                                        int32_t* err, uint64_t limit_ns, cudaStream_t stream);
-cudaError_t launch_ep_reduce_peer(const float* pair, const int32_t* slot_pos, int sorted_rows, int topk, int64_t H,
+cudaError_t launch_ep_reduce_peer(const __nv_bfloat16* pair, const int32_t* slot_pos, int sorted_rows, int topk, int64_t H,
                                   const EpPeerArgs& a, int32_t* counter, cudaStream_t stream);
 cudaError_t launch_ep_combine_peer(const uint8_t* own, int64_t area_off, const int32_t* pos, int64_t M, int64_t H,
                                    int G, int64_t rows_per_rank, int32_t epoch, void* out, int32_t* err,

@@ -86,7 +86,9 @@ struct GemmParams {
   const int32_t* sorted_ids;
   const float* topk_w;
   int32_t sentinel;   // M * topk
-  float* out_pair;    // fp32 rows of Nw: row f = slot (tiles <= 64) or sorted row p (tiles >= 128)
+  // bf16 rows of Nw (router weight applied): row f = slot (tiles <= 64) or
+  // sorted row p (tiles >= 128)
+  __nv_bfloat16* out_pair;
   // EPI_FUSED: per-chunk count of finished stage-1 units (zeroed by routing),
   // followed by two phase counters (CTAs done with phase 0 / with all units)
   int32_t* chunk_ready;
@@ -721,14 +723,14 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
           fl[g] = c < rows ? __ldg(&pc.sorted_ids[p0 + c]) : pc.sentinel;
           wl[g] = fl[g] < pc.sentinel ? __ldg(&pc.topk_w[fl[g]]) : 0.f;
         }
-        // Row f (the slot) of out_pair; one 128-byte store per column.
-        float* dst = pc.out_pair + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane;
+        // Row f (the slot) of out_pair; one 64-byte store per column.
+        __nv_bfloat16* dst = pc.out_pair + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane;
 #pragma unroll
         for (int j = 0; j < C::TC; ++j) {
           if (col0 + (j & ~31) < rows) {  // warp-uniform
             const int f = __shfl_sync(0xffffffffu, fl[j / 32], j % 32);
             const float w = __shfl_sync(0xffffffffu, wl[j / 32], j % 32);
-            if (f < pc.sentinel) dst[(int64_t)f * pc.Nw] = w * acc[j];
+            if (f < pc.sentinel) dst[(int64_t)f * pc.Nw] = __float2bfloat16_rn(w * acc[j]);
           }
         }
       }

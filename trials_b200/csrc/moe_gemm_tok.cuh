@@ -57,7 +57,7 @@ struct TokCfg {
 // routed slot) are written; w_l is the lane's router weight.
 template <int NC>
 __device__ __forceinline__ void store_sorted_rows(const float (&acc)[NC], float w_l, unsigned valid, float* tb,
-                                                  int lane, int row0, float* out, int64_t ld) {
+                                                  int lane, int row0, __nv_bfloat16* out, int64_t ld) {
 #pragma unroll
   for (int cb = 0; cb < NC / 16; ++cb) {
 #pragma unroll
@@ -70,8 +70,13 @@ __device__ __forceinline__ void store_sorted_rows(const float (&acc)[NC], float 
     for (int rr = 0; rr < 4; ++rr) {
       const int row = rr * 8 + (lane >> 2);
       const float4 v = *reinterpret_cast<const float4*>(tb + row * 20 + 4 * (lane & 3));
-      if ((valid >> row) & 1u)
-        *reinterpret_cast<float4*>(out + (int64_t)(row0 + row) * ld + cb * 16 + 4 * (lane & 3)) = v;
+      if ((valid >> row) & 1u) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(out + (int64_t)(row0 + row) * ld + cb * 16 + 4 * (lane & 3)) = pk;
+      }
     }
     __syncwarp();
   }

@@ -94,12 +94,12 @@ cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K
 // ---------------------------------------------------------------------------
 // Top-k combine: out[t, n] = bf16(sum_j pair[pos(t, j), n]) over the routed
 // slots, summed in slot order j (the view(M, k, K).sum(1) of
-// sglang_integration/aiter.py:176-177, on fp32 rows that already carry the
+// sglang_integration/aiter.py:176-177, on bf16 rows that already carry the
 // router weight). pos = slot_pos[t*topk+j] (-1: slot dropped); the slot's row
 // of pair is pos (sorted_rows) or t*topk+j. One thread per 8 output columns.
 // ---------------------------------------------------------------------------
 template <int B>
-__global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __restrict__ pair,
+__global__ void __launch_bounds__(256) combine_reduce_kernel(const __nv_bfloat16* __restrict__ pair,
                                                              const int32_t* __restrict__ slot_pos, int sorted_rows,
                                                              int64_t M, int topk, int64_t H,
                                                              __nv_bfloat16* __restrict__ out) {
@@ -110,11 +110,12 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(const float* __rest
   reduce_token_cols<B>(pair, slot_pos, sorted_rows, topk, H, t, (idx - t * per_row) * 8, out + t * H);
 }
 
-cudaError_t launch_combine_reduce(const float* pair, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
+cudaError_t launch_combine_reduce(const void* pair_rows, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
                                   int64_t H, void* out, cudaStream_t stream) {
   const int64_t n = M * (H / 8);
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = (n + 255) / 256;
+  const __nv_bfloat16* pair = static_cast<const __nv_bfloat16*>(pair_rows);
   if (M * topk <= 1024)
     combine_reduce_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, M, topk, H,
                                                                    reinterpret_cast<__nv_bfloat16*>(out));

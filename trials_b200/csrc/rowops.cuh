@@ -142,7 +142,7 @@ __device__ __forceinline__ void quant_row_segment(const QuantArgs& a, int64_t ro
 // sums consume them. Loads go through L2 (the rows may have been written by
 // other CTAs of the same launch).
 template <int B>
-__device__ __forceinline__ void reduce_token_cols(const float* pair, const int32_t* slot_pos, int sorted_rows,
+__device__ __forceinline__ void reduce_token_cols(const __nv_bfloat16* pair, const int32_t* slot_pos, int sorted_rows,
                                                   int topk, int64_t H, int64_t t, int64_t c,
                                                   __nv_bfloat16* out_row) {
   float acc[8];
@@ -152,21 +152,24 @@ __device__ __forceinline__ void reduce_token_cols(const float* pair, const int32
     int pos[B];
 #pragma unroll
     for (int j = 0; j < B; ++j) pos[j] = j0 + j < topk ? __ldcg(&slot_pos[t * topk + j0 + j]) : -1;
-    float4 x[B], y[B];
+    uint4 x[B];
 #pragma unroll
     for (int j = 0; j < B; ++j) {
       if (pos[j] >= 0) {
         const int64_t row = sorted_rows ? (int64_t)pos[j] : t * topk + j0 + j;
-        const float4* src = reinterpret_cast<const float4*>(pair + row * H + c);
-        x[j] = __ldcg(src);
-        y[j] = __ldcg(src + 1);
+        x[j] = __ldcg(reinterpret_cast<const uint4*>(pair + row * H + c));
       }
     }
 #pragma unroll
     for (int j = 0; j < B; ++j) {
       if (pos[j] < 0) continue;
-      acc[0] += x[j].x; acc[1] += x[j].y; acc[2] += x[j].z; acc[3] += x[j].w;
-      acc[4] += y[j].x; acc[5] += y[j].y; acc[6] += y[j].z; acc[7] += y[j].w;
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&x[j]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
     }
   }
   __nv_bfloat162 o[4];

@@ -124,14 +124,14 @@ def gemm1_silu(a1_q, a1_sT, w13, w13_scale, r: Routing, grid_ctas: int = 0):
 
 def gemm2_combine(a2_q, a2_sT, w2, w2_scale, r: Routing, topk_weights: torch.Tensor, grid_ctas: int = 0,
                   out_pair: Optional[torch.Tensor] = None):
-    """-> out_pair f32 rows of H: row p = sorted row p for token-major tiles (rows_cap
+    """-> out_pair bf16 rows of H: row p = sorted row p for token-major tiles (rows_cap
     rows), else row f = slot (M*topk rows). Padding rows / dropped slots untouched."""
     dev = _require_cuda(a2_q, w2)
     E, H, I = w2.shape
     M, topk = topk_weights.shape
     tw = topk_weights.to(torch.float32).contiguous()
     if out_pair is None:
-        out_pair = torch.zeros(r.pair_rows(M, topk), H, dtype=torch.float32, device=dev)
+        out_pair = torch.zeros(r.pair_rows(M, topk), H, dtype=torch.bfloat16, device=dev)
     _lib.check(_lib.lib().b200moe_gemm2_combine(
         _ptr(a2_q), _ptr(a2_sT), r.a_s_ld(), r.rows_cap, _ptr(w2), _ptr(w2_scale.contiguous()), E, H, I,
         _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows), _ptr(r.n_chunks), r.chunks_cap,
@@ -154,7 +154,7 @@ def experts(a1_q, a1_sT, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights:
     a2_sT = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
     tw = topk_weights.to(torch.float32).contiguous()
     if out_pair is None:
-        out_pair = torch.zeros(r.pair_rows(M, topk), H, dtype=torch.float32, device=dev)
+        out_pair = torch.zeros(r.pair_rows(M, topk), H, dtype=torch.bfloat16, device=dev)
     _lib.check(_lib.lib().b200moe_experts(
         _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13), _ptr(w13_scale.contiguous()), _ptr(w2),
         _ptr(w2_scale.contiguous()), E, H, I, _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows),
@@ -179,7 +179,7 @@ def experts_fused(hidden, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights
     a1_sT = torch.empty(H // 128, ld, dtype=torch.float32, device=dev)
     a2_q = torch.zeros(r.rows_cap, I, dtype=FP8, device=dev)
     a2_sT = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
-    out_pair = torch.zeros(M * topk, H, dtype=torch.float32, device=dev)
+    out_pair = torch.zeros(M * topk, H, dtype=torch.bfloat16, device=dev)
     out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
     tw = topk_weights.to(torch.float32).contiguous()
     _lib.check(_lib.lib().b200moe_experts_fused(
@@ -267,7 +267,7 @@ class LayerPipeline:
         self.a2 = torch.zeros(self.rows_cap, I, dtype=FP8, device=device)
         self.a2s = torch.zeros(I // 128, self.ld, dtype=torch.float32, device=device)
         self.sorted_rows = 1 if self.tile > 64 else 0
-        self.pair = torch.zeros(max(self.rows_cap if self.sorted_rows else numel, 1), H, dtype=torch.float32,
+        self.pair = torch.zeros(max(self.rows_cap if self.sorted_rows else numel, 1), H, dtype=torch.bfloat16,
                                 device=device)
         self.out = torch.zeros(M, H, dtype=torch.bfloat16, device=device)
 
