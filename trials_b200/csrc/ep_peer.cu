@@ -238,7 +238,7 @@ cudaError_t launch_ep_reduce_peer(const __nv_bfloat16* pair, const int32_t* slot
   if (R * topk <= 1024)
     ep_reduce_peer_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, topk, H, a, counter);
   else
-    ep_reduce_peer_kernel<1><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, topk, H, a, counter);
+    ep_reduce_peer_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, topk, H, a, counter);
   return cudaGetLastError();
 }
 
