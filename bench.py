@@ -209,10 +209,10 @@ def packed_inputs(*tensors):
 
 def gemm2_bytes(shape, active, pairs):
     """Algorithmic bytes of one GEMM2 launch: w2 + its scales of every active
-    expert, the fp8 inter rows and scales read, the fp32 weighted rows written."""
+    expert, the fp8 inter rows and scales read, the bf16 weighted rows written."""
     H, I = shape.H, shape.I
     w = active * (H * I + 4 * (H // 128) * (I // 128))
-    return w + pairs * (I + 4 * I // 128) + pairs * H * 4
+    return w + pairs * (I + 4 * I // 128) + pairs * H * 2
 
 
 def gemm1_bytes(shape, active, pairs):
