@@ -171,8 +171,9 @@ B200MOE_API int b200moe_layer_quantized(const uint8_t* hidden_q, const float* hi
  * tok_of[d*rows_per_rank + r] = token of that row; counts[d] = rows used.
  * Tokens beyond rows_per_rank for a destination set B200MOE_DEVERR_CAPACITY
  * (rows_per_rank = M never overflows). After an equal-split all-to-all of the
- * G blocks, the receiving rank runs b200moe_layer_packed on all G*rows_per_rank
- * received rows (rows without a local expert give zero rows) and sends the
+ * G blocks, the receiving rank runs b200moe_layer_packed on all R = G*rows_per_rank
+ * received rows (rows without a local expert give zero rows; num_ranks = G sets
+ * the expected count of local slots, R*topk/G, which picks the tile size) and sends the
  * (R, H) bf16 result back with a second equal-split all-to-all;
  * b200moe_ep_combine then sums, for each token, the returned rows of the ranks
  * it was sent to, in rank order. No host synchronisation anywhere.
@@ -184,7 +185,8 @@ B200MOE_API int b200moe_ep_dispatch(const uint8_t* hidden_q, const float* hidden
                                     int32_t* tok_of, int32_t* counts, int32_t* err_word, void* stream);
 B200MOE_API size_t b200moe_layer_packed_workspace_size(int64_t R, int64_t H, int64_t I, int num_local_experts,
                                                        int topk);
-B200MOE_API int b200moe_layer_packed(const uint8_t* rows, int64_t R, int64_t row_bytes, int64_t H, int64_t I,
+B200MOE_API int b200moe_layer_packed(const uint8_t* rows, int64_t R, int num_ranks, int64_t row_bytes, int64_t H,
+                                     int64_t I,
                                      int num_local_experts, int topk, const uint8_t* w13, const float* w13_scale,
                                      const uint8_t* w2, const float* w2_scale, void* out, void* workspace,
                                      size_t workspace_bytes, void* stream);

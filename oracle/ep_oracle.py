@@ -64,7 +64,7 @@ class OracleEPOps:
     def workspace_bytes(self, R, H, I, E_local, topk):
         return 256
 
-    def layer_packed(self, rows, R, H, I, E_local, topk, w13, w13_scale, w2, w2_scale, out, ws):
+    def layer_packed(self, rows, R, H, I, E_local, topk, w13, w13_scale, w2, w2_scale, out, ws, num_ranks=1):
         rb = row_bytes(H, topk)
         buf = rows.view(R, rb)
         q = buf[:, :H].contiguous().view(torch.float8_e4m3fn)

@@ -82,7 +82,7 @@ def test_ep_kernels_simulated_ranks_match_single_gpu_layer(cuda_device, G):
         ws = torch.zeros(max(ops.workspace_bytes(R, H, SHAPE.I, per, topk), 256), dtype=torch.uint8, device=dev)
         sl = slice(d * per, (d + 1) * per)
         ops.layer_packed(recv, R, H, SHAPE.I, per, topk, W["w13"][sl].contiguous(), W["w13_scale"][sl].contiguous(),
-                         W["w2"][sl].contiguous(), W["w2_scale"][sl].contiguous(), out_d, ws)
+                         W["w2"][sl].contiguous(), W["w2_scale"][sl].contiguous(), out_d, ws, num_ranks=G)
         assert moe.read_device_error(ws[:4].view(torch.int32)) == 0
         local_outs.append(out_d.view(G, cap, H))
     for r in range(G):
@@ -140,7 +140,7 @@ def _all_to_all_form(G, cap, toks, W, dev):
         ws = torch.zeros(max(ops.workspace_bytes(G * cap, H, I, per, topk), 256), dtype=torch.uint8, device=dev)
         sl = slice(d * per, (d + 1) * per)
         ops.layer_packed(recv, G * cap, H, I, per, topk, W["w13"][sl].contiguous(), W["w13_scale"][sl].contiguous(),
-                         W["w2"][sl].contiguous(), W["w2_scale"][sl].contiguous(), out_d, ws)
+                         W["w2"][sl].contiguous(), W["w2_scale"][sl].contiguous(), out_d, ws, num_ranks=G)
         local.append(out_d.view(G, cap, H))
     outs = []
     for r, (hidden, _, _) in enumerate(toks):

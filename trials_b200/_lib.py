@@ -46,7 +46,7 @@ SIGNATURES = {
     "b200moe_ep_row_bytes": (_L, [_L, _I]),
     "b200moe_ep_dispatch": (_I, [_P, _P, _P, _P, _L, _L, _I, _I, _I, _L, _P, _P, _P, _P, _P, _P]),
     "b200moe_layer_packed_workspace_size": (_S, [_L, _L, _L, _I, _I]),
-    "b200moe_layer_packed": (_I, [_P, _L, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _S, _P]),
+    "b200moe_layer_packed": (_I, [_P, _L, _I, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _S, _P]),
     "b200moe_ep_combine": (_I, [_P, _P, _L, _L, _I, _L, _P, _P]),
     "b200moe_ep_peer_bytes": (_S, [_L, _L, _I, _I]),
     "b200moe_ep_peer_alloc": (_I, [_S, ctypes.POINTER(_P), _P]),

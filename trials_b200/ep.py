@@ -63,9 +63,10 @@ class CudaEPOps:
     def workspace_bytes(self, R, H, I, E_local, topk) -> int:
         return _lib.lib().b200moe_layer_packed_workspace_size(R, H, I, E_local, topk)
 
-    def layer_packed(self, rows, R, H, I, E_local, topk, w13, w13_scale, w2, w2_scale, out, ws):
+    def layer_packed(self, rows, R, H, I, E_local, topk, w13, w13_scale, w2, w2_scale, out, ws, num_ranks=1):
         _lib.check(_lib.lib().b200moe_layer_packed(
-            _ptr(rows), R, self.row_bytes(H, topk), H, I, E_local, topk, _ptr(w13), _ptr(w13_scale), _ptr(w2),
+            _ptr(rows), R, num_ranks, self.row_bytes(H, topk), H, I, E_local, topk, _ptr(w13), _ptr(w13_scale),
+            _ptr(w2),
             _ptr(w2_scale), _ptr(out), _ptr(ws), ws.numel(), _stream(rows.device)), "layer_packed")
 
     def combine(self, returned, pos, M, H, G, rows_per_rank, out):
@@ -222,7 +223,7 @@ class ExpertParallelMoE:
         rec(2)
         R = self.G * self.cap
         self.ops.layer_packed(self.recv, R, H, self.I, self.E_local, topk, self.w13, self.w13_scale, self.w2,
-                              self.w2_scale, self.local_out, self.ws)
+                              self.w2_scale, self.local_out, self.ws, num_ranks=self.G)
         rec(3)
         self._all_to_all(self.returned.view(-1), self.local_out.view(-1))
         rec(4)

@@ -215,7 +215,7 @@ FAN_OUT_MIN_PAIRS = 2048
 def pick_tile_tokens(numel: int, num_local_experts: int) -> int:
     """Token columns per GEMM unit; the same rule as the C layer (capi.cu)."""
     avg = numel / max(num_local_experts, 1)
-    if avg <= 20.0:
+    if avg <= 26.0:
         return 32
     if avg <= 48.0:
         return 64
