@@ -251,7 +251,8 @@ B200MOE_API int b200moe_ep_combine_peer(void* own_base, const int32_t* pos, int6
  * 64 MiB device array inside the library, held by every GPU that loads it
  * until the process exits. Layers whose b200moe_layer_workspace_size()
  * exceeds 64 MiB are rejected with B200MOE_ERR_WORKSPACE (the GLM-5-like
- * decode batch of 64 tokens needs about 50 MB). The call allocates nothing.
+ * decode batch of 64 tokens needs about 43 MB; that layer fits up to 208
+ * tokens). The call allocates nothing.
  * The first call on each device looks up the array's device address; make it
  * before any stream capture. All calls on a device share the array and it
  * keeps the last call's contents: calls whose GPU work overlaps (for example

@@ -13,7 +13,8 @@
 // code holds it until the process exits. It covers layers whose
 // b200moe_layer_workspace_size() is at most that size, for example the
 // GLM-5-like decode batch of 64 tokens (hidden 6144, intermediate 2048,
-// 256 experts, top-8) at about 50 MB; larger calls are rejected.
+// 256 experts, top-8) at about 43 MB, and that layer up to 208 tokens;
+// larger calls are rejected.
 #include <cuda_runtime.h>
 
 #include <mutex>
