@@ -114,3 +114,16 @@ def test_ops_refuse_cpu_tensors():
     h = torch.zeros(2, 256, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         moe_decode_megakernel_full(h, h, h, h, h, h, h)
+
+
+def test_packed_workspace_covers_every_tile():
+    """The packed layers pick their tile from the slots expected per rank, so
+    their workspace query covers the largest plan over the tile sizes: never
+    less than the plain layer's workspace for the same rows, plus the unpacked
+    ids and weights."""
+    L = _lib.lib()
+    H, I, topk = 6144, 2048, 8
+    for R, E in ((64, 256), (512, 32), (4096, 128), (8192, 256)):
+        packed = L.b200moe_layer_packed_workspace_size(R, H, I, E, topk)
+        plain = L.b200moe_layer_workspace_size(R, H, I, E, E, topk)
+        assert packed >= plain + R * topk * 8, (R, E)
