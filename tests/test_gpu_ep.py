@@ -151,7 +151,7 @@ def _all_to_all_form(G, cap, toks, W, dev):
     return outs
 
 
-@pytest.mark.parametrize("G", [1, 2, 4])
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
 def test_peer_exchange_simulated_ranks_bit_identical_to_all_to_all(cuda_device, G):
     """The G ranks' exchange buffers live in one process on one GPU. Every
     kernel of a call is launched after the kernels whose flags it waits for
