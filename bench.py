@@ -367,12 +367,17 @@ def run_ep(args, shape, config):
     errs = model.device_errors()
     # Ours per step: plan, pack (quantising on the way with the peer exchange; a
     # separate quant before it with NCCL), unpack, route, gather, the experts
-    # launch (two for token-major tiles), top-k reduce, combine. The NCCL
+    # launch (two for token-major tiles), top-k reduce, combine; routing is two
+    # launches from 16,384 slots. The NCCL
     # exchange adds its own all-to-all kernels, not counted.
     from trials_b200.stages import pick_tile_tokens
 
-    experts_launches = 2 if pick_tile_tokens(ws * shape.M * shape.topk, per) > 64 else 1
-    ep_launches = 7 + experts_launches + (0 if args.exchange == "peer" else 1)
+    from trials_b200 import _lib
+
+    # the packed layer picks its tile from the slots expected on the rank
+    experts_launches = 2 if pick_tile_tokens(shape.M * shape.topk, per) > 64 else 1
+    route_launches = 2 if _lib.lib().b200moe_route_scratch_ints(ws * shape.M * shape.topk, per) > 0 else 1
+    ep_launches = 6 + route_launches + experts_launches + (0 if args.exchange == "peer" else 1)
 
     e2e = None
     if not args.no_e2e:
