@@ -368,11 +368,10 @@ def run_ep(args, shape, config):
     # Ours per step: plan, pack (quantising on the way with the peer exchange; a
     # separate quant before it with NCCL), unpack, route, gather, the experts
     # launch (two for token-major tiles), top-k reduce, combine; routing is two
-    # launches from 16,384 slots. The NCCL
-    # exchange adds its own all-to-all kernels, not counted.
-    from trials_b200.stages import pick_tile_tokens
-
+    # launches from 16,384 slots. The NCCL exchange adds its own all-to-all
+    # kernels, not counted.
     from trials_b200 import _lib
+    from trials_b200.stages import pick_tile_tokens
 
     # the packed layer picks its tile from the slots expected on the rank
     experts_launches = 2 if pick_tile_tokens(shape.M * shape.topk, per) > 64 else 1
