@@ -17,12 +17,20 @@ scales, 1x128 activation scales, bf16 in/out).
               the timed region;
   roofline    the dominant kernel (the grouped GEMMs) against measured HBM
               bandwidth;
-  cpu_baseline the fp32 CPU oracle on a bounded sample of experts (rank 0, N=1).
+  cpu_baseline the fp32 CPU oracle on a bounded sample of experts (rank 0, N=1),
+              with the GPU layer run on the same sample as a parity check;
+  sweep       (N=1) the other single-GPU workloads of the benchmark set on the
+              same weights: decode M = 128..1024, M = 1024 with 16 hot experts,
+              prefill M = 2048/4096/8192, each with its roofline fraction.
 --impl reference times that CPU path alone (the reference is a Python/Triton
 package for AMD GPUs; its algorithm is restated by the oracle).
 
 N > 1 (torchrun, one rank per GPU) runs the expert-parallel layer: E/N experts
-and M tokens per GPU, NCCL all-to-all dispatch and combine (weak scaling).
+and M tokens per GPU (weak scaling), exchanged by the kernels through peer
+memory (or NCCL all-to-alls with --exchange nccl). The line carries a parity
+record (every rank's output against the single-GPU layer over all experts, and
+the other exchange form bit for bit) and a config5 record: 8,192 tokens in
+total split over the ranks.
 """
 from __future__ import annotations
 
@@ -63,6 +71,10 @@ def parse_args(argv=None):
     ap.add_argument("--split", action="store_true", help="the two GEMM stages as two launches (default: one)")
     ap.add_argument("--layer-launch", action="store_true",
                     help="small batches: gather, experts and reduce in one launch (default: three)")
+    ap.add_argument("--sweep-steps", type=int, default=10, help="timed steps per sweep / config5 workload")
+    ap.add_argument("--no-sweep", action="store_true", help="N=1: skip the sweep record")
+    ap.add_argument("--no-config5", action="store_true", help="N>1: skip the config5 record")
+    ap.add_argument("--no-parity", action="store_true", help="N>1: skip the parity record")
     return ap.parse_args(argv)
 
 
@@ -137,10 +149,11 @@ class ClockSampler:
     def mark(self):
         return time.monotonic()
 
-    def window(self, t0, t1):
-        self.windows.append((t0, t1))
+    def window(self, t0, t1, group="main"):
+        self.windows.append((t0, t1, group))
 
     def stop(self):
+        """Stops sampling; returns the summary of the "main" windows."""
         if self.proc is None:
             return None
         time.sleep(0.12)
@@ -149,9 +162,13 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        sel = [s for s in self.samples if any(a - 0.06 <= s[0] <= b + 0.06 for a, b in self.windows)]
-        if not sel and self.samples and self.windows:
-            mid = self.windows[0][0]
+        return self.summary("main")
+
+    def summary(self, group):
+        wins = [(a, b) for a, b, g in self.windows if g == group]
+        sel = [s for s in self.samples if any(a - 0.06 <= s[0] <= b + 0.06 for a, b in wins)]
+        if not sel and self.samples and wins:
+            mid = wins[0][0]
             sel = [min(self.samples, key=lambda s: abs(s[0] - mid))]
         if not sel:
             return None
@@ -215,6 +232,45 @@ def gemm2_bytes(shape, active, pairs):
     return w + pairs * (I + 4 * I // 128) + pairs * H * 2
 
 
+def layer_inputs(shape, M, hot, seed, device):
+    """Seeded router (logits N(0,1), +hot_bias on the first `hot` experts, then
+    the shape's scoring, top-k, renormalised) and bf16 hidden rows N(0,1) of M
+    tokens -> (hidden, topk_weights, topk_ids) on `device`."""
+    import torch
+
+    from trials_b200 import synth
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    logits = torch.randn(M, shape.E, generator=g, device=device)
+    if hot:
+        logits[:, :hot] += shape.hot_bias
+    tw, ids = synth.make_router(logits, shape.topk, shape.scoring)
+    hidden = torch.randn(M, shape.H, generator=g, device=device).to(torch.bfloat16)
+    return hidden, tw, ids
+
+
+def rel_l2(a, b) -> float:
+    """||a - b|| / ||b|| in fp32 (on the tensors' device)."""
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def experts_roofline(shape, active, pairs, ms, hbm_peak):
+    """Roofline of the experts launch(es) (both grouped-GEMM stages): HBM side
+    (algorithmic bytes of both stages, against the measured copy peak) and
+    tensor side (2*pairs*3*I*H flops, against the measured FP8 GEMM peak);
+    `attainable` = the slower of the two floors over the measured time."""
+    nbytes = gemm1_bytes(shape, active, pairs) + gemm2_bytes(shape, active, pairs)
+    flops = 2.0 * pairs * 3 * shape.I * shape.H
+    t = ms / 1e3
+    t_hbm, t_tc = nbytes / (hbm_peak * 1e9), flops / (FP8_PEAK_TFLOPS * 1e12)
+    return {"bound": "hbm" if t_hbm >= t_tc else "tensor", "experts_ms": ms,
+            "hbm_gbs": nbytes / t / 1e9, "hbm_frac": nbytes / t / 1e9 / hbm_peak,
+            "tflops": flops / t / 1e12, "tensor_frac": flops / t / 1e12 / FP8_PEAK_TFLOPS,
+            "attainable_frac": max(t_hbm, t_tc) / t, "algorithmic_bytes": nbytes, "algorithmic_flops": flops}
+
+
 def gemm1_bytes(shape, active, pairs):
     """Algorithmic bytes of one GEMM1 launch: w13 + its scales of every active
     expert, the routed fp8 activation rows and scales read, the fp8 inter rows
@@ -257,50 +313,78 @@ def cpu_sample_setup(shape, n_sample, seed):
 
 def cpu_sample_run(s):
     """One timed pass of the fp32 oracle over the sampled experts; returns
-    seconds per expert."""
+    (seconds for the sample, the oracle's output)."""
     import torch
 
     from oracle import moe_oracle as orc
 
     t0 = time.perf_counter()
-    orc.moe_layer(s["hidden"], s["w13_q"], s["w13_s"], s["w2_q"], s["w2_s"], s["tw"], s["ids"],
-                  expert_map=s["emap"].numpy(), num_local=s["n"], dtype=torch.float32)
-    return (time.perf_counter() - t0) / s["n"]
+    out = orc.moe_layer(s["hidden"], s["w13_q"], s["w13_s"], s["w2_q"], s["w2_s"], s["tw"], s["ids"],
+                        expert_map=s["emap"].numpy(), num_local=s["n"], dtype=torch.float32)
+    return time.perf_counter() - t0, out
 
 
-def cpu_baseline(shape, n_sample, seed, reps=1):
+def cpu_baseline(shape, n_sample, seed, reps=1, device=None):
+    """The CPU baseline on a bounded sample; with `device`, the GPU layer runs
+    the same sample (same weights and tokens, the other experts masked off
+    through fused_moe's expert_mask) and its rel-L2 against the oracle's output
+    is reported as the baseline's parity."""
     import torch
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     s = cpu_sample_setup(shape, n_sample, seed)
-    per_expert = min(cpu_sample_run(s) for _ in range(reps))
+    runs = [cpu_sample_run(s) for _ in range(reps)]
+    sec, out_cpu = min(runs, key=lambda r: r[0])
+    per_expert = sec / s["n"]
     tps = shape.M / (per_expert * s["active"])
-    return {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+    line = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"fp32 torch oracle (dequantise + matmul per expert) over {s['n']} of {s['active']} active "
                       f"experts of the M={shape.M} batch; seconds per expert x active experts = layer time"}
+    if device is not None:
+        from trials_b200 import moe
+
+        g = lambda t: t.to(device)  # noqa: E731
+        out_gpu = moe.fused_moe(g(s["hidden"]), g(s["w13_q"]), g(s["w2_q"]), g(s["tw"]), g(s["ids"]),
+                                w1_scale=g(s["w13_s"]), w2_scale=g(s["w2_s"]),
+                                expert_mask=g((s["emap"] >= 0).to(torch.int32)))
+        line["parity"] = {"gpu_layer_vs_oracle_rel_l2": rel_l2(out_gpu.cpu(), out_cpu), "tol": 5e-3,
+                          "what": "the GPU layer on the sampled experts against the oracle's output"}
+    return line
 
 
 def run_reference(args, shape, config):
+    """The reference's torch path (restated by the oracle) on the host cores:
+    each step runs the oracle over a bounded sample of the active experts of
+    the whole job's tokens (all ranks' tokens at N > 1); ms_per_step is that
+    measured time. The layer time is the measured seconds per expert times
+    the active experts, which sets `value`."""
     import torch
+    from dataclasses import replace
 
     rank, _, ws = dist_setup("gloo")
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    s = cpu_sample_setup(shape, args.cpu_sample_experts, args.seed)
+    job = replace(shape, M=shape.M * ws)
+    s = cpu_sample_setup(job, args.cpu_sample_experts, args.seed)
     for _ in range(args.warmup):
         cpu_sample_run(s)
-    times = [cpu_sample_run(s) for _ in range(args.steps)]
-    per_expert = sum(times) / len(times)
+    times = [cpu_sample_run(s)[0] for _ in range(args.steps)]
+    step_s = sum(times) / len(times)
+    per_expert = step_s / s["n"]
     layer_s = per_expert * s["active"]
-    tps = shape.M * ws / layer_s
+    tps = job.M / layer_s
     sample = (f"fp32 torch oracle (restatement of the reference's torch path) over {s['n']} of {s['active']} "
-              f"active experts per step; layer time = seconds per expert x active experts")
+              f"active experts of the job's {job.M} tokens per step; layer time = seconds per expert x active experts")
     line = {"metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": layer_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config, "impl": "reference",
+            "sample_scaling": {"experts_timed_per_step": s["n"], "active_experts": s["active"],
+                               "measured_ms_per_step": step_s * 1e3, "layer_ms_estimated": layer_s * 1e3,
+                               "tokens": job.M,
+                               "note": "value = tokens / (ms_per_step / experts_timed_per_step x active_experts)"},
             "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -310,8 +394,12 @@ def run_reference(args, shape, config):
 # ----------------------------------------------------------------------------
 # GPU arm
 # ----------------------------------------------------------------------------
+CONFIG5_TOKENS = 8192  # expert-parallel configuration: tokens in total, split evenly over the ranks
+
+
 def run_ep(args, shape, config):
-    """N > 1: expert-parallel layer, E/N experts and M tokens per GPU."""
+    """N > 1: expert-parallel layer, E/N experts and M tokens per GPU, plus the
+    parity and config5 records."""
     import torch
     import torch.distributed as dist
 
@@ -319,23 +407,32 @@ def run_ep(args, shape, config):
 
     rank, local, ws = dist_setup("nccl")
     dev = torch.device("cuda", local)
+    check = not args.no_parity
     L = synth.make_layer(shape, moe.per_block_quant_fp8, seed=args.seed, device=dev)  # same weights on every rank
+    hidden, tw, ids = layer_inputs(shape, shape.M, shape.hot_experts, args.seed + 1000 + rank, dev)
+    M5 = CONFIG5_TOKENS // ws
+    run5 = not args.no_config5 and M5 > 0
+    if run5:
+        h5, tw5, ids5 = layer_inputs(shape, M5, shape.hot_experts, args.seed + 2000 + rank, dev)
+    # The single-GPU layer over all experts, on this rank's tokens: the parity reference.
+    full = lambda h, w, i: moe.moe_decode_megakernel_full(h, L.w13, L.w13_scale, L.w2, L.w2_scale, w, i)  # noqa
+    ref = full(hidden, tw, ids) if check else None
+    ref5 = full(h5, tw5, ids5) if (check and run5) else None
     shards = [ep.shard_experts(t, rank, ws) for t in (L.w13, L.w13_scale, L.w2, L.w2_scale)]
-    del L
+    del L, full
     torch.cuda.empty_cache()
     model = ep.ExpertParallelMoE(*shards, num_experts=shape.E, rows_per_rank=shape.M, exchange=args.exchange)
-    g = torch.Generator(device=dev)
-    g.manual_seed(args.seed + 1000 + rank)
-    logits = torch.randn(shape.M, shape.E, generator=g, device=dev)
-    if shape.hot_experts:
-        logits[:, : shape.hot_experts] += shape.hot_bias
-    tw, ids = synth.make_router(logits, shape.topk, shape.scoring)
-    hidden = torch.randn(shape.M, shape.H, generator=g, device=dev).to(torch.bfloat16)
-    all_ids = [torch.empty_like(ids) for _ in range(ws)]
-    dist.all_gather(all_ids, ids)
     per = shape.E // ws
-    glob = torch.cat(all_ids).reshape(-1)
-    local_active = int(torch.unique(glob[(glob >= rank * per) & (glob < (rank + 1) * per)]).numel())
+
+    def local_work(ids_rank):
+        """(active local experts, local slots) of this rank over every rank's ids."""
+        parts = [torch.empty_like(ids_rank) for _ in range(ws)]
+        dist.all_gather(parts, ids_rank)
+        glob = torch.cat(parts).reshape(-1)
+        mine = glob[(glob >= rank * per) & (glob < (rank + 1) * per)]
+        return int(torch.unique(mine).numel()), int(mine.numel())
+
+    local_active, local_pairs = local_work(ids)
 
     def barrier():
         dist.barrier(device_ids=[local])
@@ -346,24 +443,29 @@ def run_ep(args, shape, config):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        model(hidden, tw, ids)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
     clocks.start()
-    barrier()
-    t0 = clocks.mark()
-    start.record()
-    for k in range(args.steps):
-        model(hidden, tw, ids, events=evs[k])
-    end.record()
-    barrier()
-    clocks.window(t0, clocks.mark())
-    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
-    stage_ms = {name: max_over_ranks(statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1])
-                                                     for k in range(args.steps)))
-                for i, name in enumerate(ep.ExpertParallelMoE.STAGES)}
+
+    def timed(m, h, w, i, steps, warmup, group):
+        """Max over ranks of the mean step time, and of each stage's mean time."""
+        for _ in range(warmup):
+            m(h, w, i)
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        t0 = clocks.mark()
+        start.record()
+        for k in range(steps):
+            m(h, w, i, events=evs[k])
+        end.record()
+        barrier()
+        clocks.window(t0, clocks.mark(), group)
+        ms = max_over_ranks(start.elapsed_time(end) / steps)
+        stage_ms = {name: max_over_ranks(statistics.mean(evs[k][j].elapsed_time(evs[k][j + 1]) for k in range(steps)))
+                    for j, name in enumerate(ep.ExpertParallelMoE.STAGES)}
+        return ms, stage_ms
+
+    ms, stage_ms = timed(model, hidden, tw, ids, args.steps, args.warmup, "main")
     errs = model.device_errors()
     # Ours per step: plan, pack (quantising on the way with the peer exchange; a
     # separate quant before it with NCCL), unpack, route, gather, the experts
@@ -373,10 +475,13 @@ def run_ep(args, shape, config):
     from trials_b200 import _lib
     from trials_b200.stages import pick_tile_tokens
 
-    # the packed layer picks its tile from the slots expected on the rank
-    experts_launches = 2 if pick_tile_tokens(shape.M * shape.topk, per) > 64 else 1
-    route_launches = 2 if _lib.lib().b200moe_route_scratch_ints(ws * shape.M * shape.topk, per) > 0 else 1
-    ep_launches = 6 + route_launches + experts_launches + (0 if args.exchange == "peer" else 1)
+    def launches_per_step(M_rank):
+        # the packed layer picks its tile from the slots expected on the rank
+        experts_launches = 2 if pick_tile_tokens(M_rank * shape.topk, per) > 64 else 1
+        route_launches = 2 if _lib.lib().b200moe_route_scratch_ints(ws * M_rank * shape.topk, per) > 0 else 1
+        return 6 + route_launches + experts_launches + (0 if args.exchange == "peer" else 1)
+
+    ep_launches = launches_per_step(shape.M)
 
     e2e = None
     if not args.no_e2e:
@@ -402,13 +507,52 @@ def run_ep(args, shape, config):
         e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": in_host.numel() * ws,
                "d2h_bytes_per_step": out_host.numel() * 2 * ws, "ms_per_step": ms_e2e}
+
+    other_x = "nccl" if args.exchange == "peer" else "peer"
+
+    def parity(m, h, w, i, r):
+        """This rank's output against the single-GPU layer, and against the
+        other exchange form bit for bit; max / OR over ranks."""
+        out = m(h, w, i).clone()
+        other = ep.ExpertParallelMoE(*shards, num_experts=shape.E, rows_per_rank=m.cap, exchange=other_x)
+        out_o = other(h, w, i)
+        e = m.device_errors() | other.device_errors()
+        other.close()
+        rel = max_over_ranks(rel_l2(out, r))
+        unequal = max_over_ranks(0.0 if torch.equal(out, out_o) else 1.0)
+        e = int(max_over_ranks(float(e)))
+        tol = 5e-3
+        return {"reference": "single-GPU layer (moe_decode_megakernel_full) over all experts, same tokens",
+                "rel_l2_max_over_ranks": rel, "tol": tol, f"bit_equal_{args.exchange}_vs_{other_x}": unequal == 0,
+                "device_errors": e, "ok": rel <= tol and unequal == 0 and e == 0}
+
+    par = parity(model, hidden, tw, ids, ref) if check else None
+
+    c5 = None
+    if run5:
+        model5 = ep.ExpertParallelMoE(*shards, num_experts=shape.E, rows_per_rank=M5, exchange=args.exchange)
+        ms5, st5 = timed(model5, h5, tw5, ids5, args.sweep_steps, 3, "config5")
+        act5, pairs5 = local_work(ids5)
+        act5, pairs5 = int(max_over_ranks(act5)), int(max_over_ranks(pairs5))
+        peak, _ = measured_peaks()
+        roof5 = experts_roofline(shape, act5, pairs5, st5["layer_packed"], peak)
+        roof5["kernel"] = "layer_packed (the layer kernels on this rank's experts, incl. the wait for the dispatch)"
+        c5 = {"workload": f"glm_ep_M{CONFIG5_TOKENS}_total", "tokens_total": M5 * ws, "tokens_per_gpu": M5,
+              "value": M5 * ws / (ms5 / 1e3), "unit": "tokens/s", "ms_per_step": ms5, "steps": args.sweep_steps,
+              "warmup": 3, "stage_ms": st5, "local_active_experts_max": act5, "local_pairs_max": pairs5,
+              "roofline": roof5, "gpu_launches": launches_per_step(M5) * args.sweep_steps,
+              "clocks": clocks.summary("config5")}
+        if check:
+            c5["parity"] = parity(model5, h5, tw5, ids5, ref5)
+        errs |= model5.device_errors()
+        model5.close()
+
     clk = clocks.stop()
     worst_active = int(max_over_ranks(local_active))
     if rank == 0:
-        from trials_b200 import synth as _s
-
         peak, peak_kind = measured_peaks()
-        wbytes = worst_active * (_s.weight_bytes_per_expert(shape.H, shape.I) + _s.scale_bytes_per_expert(shape.H, shape.I))
+        wbytes = worst_active * (synth.weight_bytes_per_expert(shape.H, shape.I) +
+                                 synth.scale_bytes_per_expert(shape.H, shape.I))
         achieved = wbytes / (stage_ms["layer_packed"] / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": shape.M * ws / (ms / 1e3), "unit": "tokens/s", "n_gpus": ws,
@@ -424,12 +568,87 @@ def run_ep(args, shape, config):
         }
         if e2e is not None:
             line["e2e"] = e2e
+        if par is not None:
+            line["parity"] = par
+        if c5 is not None:
+            line["config5"] = c5
         if errs:
             line["device_errors"] = errs
         print(json.dumps(line), flush=True)
     model.close()
     dist.destroy_process_group()
     return 0
+
+
+# The other single-GPU workloads of the benchmark set, measured on the same
+# weights after the headline: (kind, tokens, hot experts).
+SWEEP = (("decode", 128, 0), ("decode", 256, 0), ("decode", 512, 0), ("decode", 1024, 0), ("decode", 1024, 16),
+         ("prefill", 2048, 0), ("prefill", 4096, 0), ("prefill", 8192, 0))
+
+
+def ncu_traffic_ratio(name: str):
+    """DRAM bytes over algorithmic bytes of a kernel, from a committed ncu
+    summary of a small case (profiles/<name>.txt, line
+    'dram_over_algorithmic: X'); scales a full-size launch's algorithmic
+    bytes when the full workload is too large to capture."""
+    p = ROOT / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_over_algorithmic:"):
+            try:
+                return float(line.split(":", 1)[1])
+            except ValueError:
+                return None
+    return None
+
+
+def run_sweep(args, shape, L, dev, clocks, peak):
+    """Each SWEEP workload through the layer's launches (LayerPipeline, the
+    kernels and order of b200moe_layer), CUDA events on their stream."""
+    import torch
+
+    from trials_b200 import stages, synth
+
+    recs = []
+    for kind, M, hot in SWEEP:
+        h, tw, ids = layer_inputs(shape, M, hot, args.seed + 3000 + M + hot, dev)
+        pipe = stages.LayerPipeline(M, shape.H, shape.I, shape.E, shape.topk, dev)
+        w = (L.w13, L.w13_scale, L.w2, L.w2_scale)
+        for _ in range(3):
+            pipe.run(h, ids, tw, *w)
+        steps = args.sweep_steps
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(pipe.stages) + 1)] for _ in range(steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0 = clocks.mark()
+        start.record()
+        for k in range(steps):
+            pipe.run(h, ids, tw, *w, events=evs[k])
+        end.record()
+        torch.cuda.synchronize()
+        clocks.window(t0, clocks.mark(), "sweep")
+        ms = start.elapsed_time(end) / steps
+        stage_ms = {n: statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(steps))
+                    for i, n in enumerate(pipe.stages)}
+        err = int(pipe.err.item())
+        active = synth.active_experts(ids, shape.E)
+        pairs = int(((ids >= 0) & (ids < shape.E)).sum().item())
+        roof = experts_roofline(shape, active, pairs, stage_ms["experts"], peak)
+        ratio = ncu_traffic_ratio("experts_tokmajor_small" if pipe.tile > 64 else "experts_swapab_small")
+        roof["traffic"] = None if ratio is None else ratio * roof["algorithmic_bytes"]
+        name = f"glm_{kind}_M{M}" + (f"_hot{hot}" if hot else "")
+        recs.append({"workload": name, "tokens": M, "tile": pipe.tile, "ms_per_step": ms,
+                     "value": M / (ms / 1e3), "unit": "tokens/s", "active_experts": active, "pairs": pairs,
+                     "layer_hbm_gbs": layer_bytes(synth.glm(M), active, pairs) / (ms / 1e3) / 1e9,
+                     "stage_ms": stage_ms, "roofline": roof, "device_error": err,
+                     "gpu_launches": (len(pipe.stages) + (1 if pipe.tile > 64 else 0) +
+                                      (1 if pipe.rscratch_ints > 0 else 0)) * steps})
+        del pipe, h, tw, ids
+        torch.cuda.empty_cache()
+    return {"steps": args.sweep_steps, "warmup": 3, "records": recs, "clocks": clocks.summary("sweep"),
+            "l2": "no flush: every step streams the active experts' weights (>= 8 GB)",
+            "peaks": {"hbm_gbs": peak, "fp8_tflops": FP8_PEAK_TFLOPS}}
 
 
 def run_ours(args, shape, config):
@@ -510,18 +729,21 @@ def run_ours(args, shape, config):
         e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": out_host.numel() * 2, "ms_per_step": ms_e2e}
 
+    peak, peak_kind = measured_peaks()
+    sweep = None
+    if ws == 1 and not args.no_sweep:
+        sweep = run_sweep(args, shape, L, dev, clocks, peak)
     clk = clocks.stop()
 
-    # ---- CPU baseline (rank 0, one GPU only)
+    # ---- CPU baseline (rank 0, one GPU only), with the GPU layer on the same sample
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(shape, args.cpu_sample_experts, args.seed)
+        cpu = cpu_baseline(shape, args.cpu_sample_experts, args.seed, device=dev)
 
     if rank != 0:
         if ws > 1:
             dist.destroy_process_group()
         return 0
-    peak, peak_kind = measured_peaks()
     hot = f"_hot{shape.hot_experts}" if shape.hot_experts else ""
     if "layer" in stage_ms:
         # Gather + quantise, both GEMM stages and the top-k reduce in one launch.
@@ -554,6 +776,9 @@ def run_ours(args, shape, config):
                 "achieved": tf, "peak": FP8_PEAK_TFLOPS, "unit": "TFLOP/s", "frac": tf / FP8_PEAK_TFLOPS,
                 "peak_kind": "measured dense FP8 GEMM (torch._scaled_mm 8192^3 on this pool)",
                 "algorithmic_flops_per_step": flops, "traffic": None}
+        ratio = ncu_traffic_ratio("experts_tokmajor_small")
+        if ratio is not None:  # small-case DRAM bytes over algorithmic bytes, scaled to this launch
+            roof["traffic"] = ratio * (gemm1_bytes(shape, active, pairs) + gemm2_bytes(shape, active, pairs))
     line = {
         "metric": METRIC,
         "value": shape.M * ws / (ms / 1e3),
@@ -580,6 +805,8 @@ def run_ours(args, shape, config):
         line["e2e"] = e2e
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if sweep is not None:
+        line["sweep"] = sweep
     print(json.dumps(line), flush=True)
     if ws > 1:
         dist.destroy_process_group()

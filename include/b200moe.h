@@ -242,6 +242,14 @@ B200MOE_API int b200moe_layer_packed_peer(void* own_base, void* const* peer_base
 B200MOE_API int b200moe_ep_combine_peer(void* own_base, const int32_t* pos, int64_t M, int64_t H, int topk,
                                         int num_ranks, int64_t rows_per_rank, int32_t epoch, void* out,
                                         int32_t* err_word, void* stream);
+/* Limit of the peer flag waits above, in microseconds, for the whole process
+ * (default 10 s: ranks may start a call seconds apart; at most 60 s). Applies
+ * to launches made after the call. limit_us <= 0 only queries. Returns the
+ * previous limit. A wait that runs out sets B200MOE_DEVERR_TIMEOUT in its
+ * error word and the kernel goes on, so a rank whose peer is gone gets an
+ * error instead of a hung stream. No counterpart in the reference (its
+ * DeepEP/Mori exchange is a library call). */
+B200MOE_API int64_t b200moe_ep_peer_wait_limit_us(int64_t limit_us);
 
 /* ------------------------------------------------------------------------
  * b200moe_layer without a workspace argument, for callers that cannot

@@ -17,7 +17,8 @@ The tiny shape needs the orchestrator's BLOCK_N set to 32: the reference's
 N-split grid uses (N/8)//BLOCK_N programs per slice, which is 0 for N=256 at 128
 (aiter_module/moe_decode_megakernel.py:107-110).
 
-Usage:  python tests/golden/make_golden.py [--reference /root/reference]
+Usage:  python tests/golden/make_golden.py --reference <reference checkout>
+        (or TRIALS_REFERENCE=<reference checkout> python tests/golden/make_golden.py)
 """
 from __future__ import annotations
 
@@ -72,8 +73,11 @@ def bf(t):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TRIALS_REFERENCE"),
+                    help="the reference checkout (default: $TRIALS_REFERENCE)")
     args = ap.parse_args(argv)
+    if not args.reference:
+        ap.error("give the reference checkout with --reference or TRIALS_REFERENCE")
     ref = Path(args.reference)
     sys.path.insert(0, str(ref / "aiter_module"))
     import moe_decode_megakernel as mk  # reference Triton kernel

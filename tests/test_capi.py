@@ -127,3 +127,31 @@ def test_packed_workspace_covers_every_tile():
         packed = L.b200moe_layer_packed_workspace_size(R, H, I, E, topk)
         plain = L.b200moe_layer_workspace_size(R, H, I, E, E, topk)
         assert packed >= plain + R * topk * 8, (R, E)
+
+
+def test_noalloc_layer_host_checks():
+    """The no-allocation layer tells an invalid shape apart from a layer too
+    large for its static scratch (both refused before any launch)."""
+    L = _lib.lib()
+    p = 256
+    # H = 0: an invalid shape, not a size limit
+    assert L.b200moe_layer_noalloc(p, 4, 0, 128, 8, 2, p, p, p, p, p, p, None, 8, p, None, None) == \
+        _lib.ERR_INVALID_ARG
+    assert b"bad argument" in L.b200moe_last_error_message()
+    assert L.b200moe_layer_noalloc(p, -1, 256, 128, 8, 2, p, p, p, p, p, p, None, 8, p, None, None) == \
+        _lib.ERR_INVALID_ARG
+    # GLM-5-like layer at 1,024 tokens: far above the 64 MiB scratch
+    assert L.b200moe_layer_noalloc(p, 1024, 6144, 2048, 256, 8, p, p, p, p, p, p, None, 256, p, None, None) == \
+        _lib.ERR_WORKSPACE
+    assert b"64 MiB" in L.b200moe_last_error_message()
+
+
+def test_peer_wait_limit_setting():
+    L = _lib.lib()
+    default = L.b200moe_ep_peer_wait_limit_us(0)  # query only
+    assert default == 10_000_000
+    assert L.b200moe_ep_peer_wait_limit_us(20_000) == default
+    assert L.b200moe_ep_peer_wait_limit_us(-5) == 20_000          # query: unchanged
+    assert L.b200moe_ep_peer_wait_limit_us(10**12) == 20_000      # clamped to 60 s
+    assert L.b200moe_ep_peer_wait_limit_us(default) == 60_000_000
+    assert L.b200moe_ep_peer_wait_limit_us(0) == default

@@ -247,3 +247,58 @@ def test_expert_parallel_module_peer_exchange_one_rank(cuda_device):
             assert model.device_errors() == 0
     finally:
         model.close()
+
+
+def test_peer_waits_end_with_timeout_when_a_rank_never_dispatches(cuda_device):
+    """Two ranks' exchange buffers in one process; rank 1 never runs. Rank 0's
+    layer waits for rank 1's dispatch flag and its combine for rank 1's
+    combine flag: with a 20 ms limit both calls must return, each set
+    B200MOE_DEVERR_TIMEOUT in its error word, the whole sequence must take
+    about two limits (not the 10 s default), and the context must stay usable."""
+    import time
+
+    from trials_b200 import _lib
+
+    dev = cuda_device
+    lib = _lib.lib()
+    G, rank, cap = 2, 0, 8
+    H, I, topk, per = SHAPE.H, SHAPE.I, SHAPE.topk, SHAPE.E // 2
+    L = synth.make_layer(SHAPE, orc.per_block_quant_fp8, seed=3)
+    W = {k: getattr(L, k)[:per].contiguous().to(dev) for k in ["w13", "w13_scale", "w2", "w2_scale"]}
+    nbytes = lib.b200moe_ep_peer_bytes(cap, H, topk, G)
+    bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(G)]  # zeroed receive areas
+    table = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=dev)
+    ws = torch.zeros(max(lib.b200moe_layer_packed_workspace_size(G * cap, H, I, per, topk), 256), dtype=torch.uint8,
+                     device=dev)
+    hidden, tw, ids = _tokens(SHAPE, 7, cap, dev)
+    pos = torch.empty(cap * G, dtype=torch.int32, device=dev)
+    tok_of = torch.empty(G * cap, dtype=torch.int32, device=dev)
+    counts = torch.empty(G, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.empty(cap, H, dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    limit_us = 20_000
+    previous = lib.b200moe_ep_peer_wait_limit_us(limit_us)
+    try:
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        _lib.check(lib.b200moe_ep_dispatch_peer(
+            hidden.data_ptr(), None, None, ids.data_ptr(), tw.data_ptr(), cap, H, topk, SHAPE.E, G, rank, cap,
+            table.data_ptr(), bufs[rank].data_ptr(), 1, pos.data_ptr(), tok_of.data_ptr(), counts.data_ptr(),
+            err.data_ptr(), st), "dispatch_peer")
+        _lib.check(lib.b200moe_layer_packed_peer(
+            bufs[rank].data_ptr(), table.data_ptr(), G, rank, cap, 1, H, I, per, topk, W["w13"].data_ptr(),
+            W["w13_scale"].data_ptr(), W["w2"].data_ptr(), W["w2_scale"].data_ptr(), ws.data_ptr(), ws.numel(), st),
+            "layer_packed_peer")
+        _lib.check(lib.b200moe_ep_combine_peer(bufs[rank].data_ptr(), pos.data_ptr(), cap, H, topk, G, cap, 1,
+                                               out.data_ptr(), err.data_ptr(), st), "combine_peer")
+        torch.cuda.synchronize(dev)
+        wall = time.perf_counter() - t0
+    finally:
+        lib.b200moe_ep_peer_wait_limit_us(previous)
+    assert moe.read_device_error(ws[:4].view(torch.int32)) & _lib.DEVERR_TIMEOUT   # the layer's dispatch wait
+    assert moe.read_device_error(err) & _lib.DEVERR_TIMEOUT                        # the combine's wait
+    assert 2 * limit_us * 1e-6 <= wall < 2.0, wall
+    # the context still runs work
+    x = torch.arange(1024, device=dev, dtype=torch.float32)
+    assert float(x.sum().item()) == 1023 * 1024 / 2

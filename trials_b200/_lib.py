@@ -58,6 +58,7 @@ SIGNATURES = {
     "b200moe_layer_packed_peer": (_I, [_P, _P, _I, _I, _L, ctypes.c_int32, _L, _L, _I, _I, _P, _P, _P, _P, _P, _S,
                                        _P]),
     "b200moe_ep_combine_peer": (_I, [_P, _P, _L, _L, _I, _I, _L, ctypes.c_int32, _P, _P, _P]),
+    "b200moe_ep_peer_wait_limit_us": (_L, [_L]),
     "b200moe_layer_noalloc": (_I, [_P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P]),
     "b200moe_route_capacity_rows": (_L, [_L, _I]),
     "b200moe_route_capacity_chunks": (_L, [_L, _I, _I]),

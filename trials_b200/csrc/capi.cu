@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -841,7 +842,12 @@ int b200moe_ep_peer_free(void* base) {
 }
 
 namespace {
-constexpr uint64_t kPeerWaitNs = 10ull * 1000 * 1000 * 1000;  // ranks may start a call seconds apart
+// Limit of every peer flag wait (dispatch and combine). Ranks may start a
+// call seconds apart, so the default is long; b200moe_ep_peer_wait_limit_us
+// changes it for the whole process (tests use a short one).
+constexpr uint64_t kPeerWaitDefaultNs = 10ull * 1000 * 1000 * 1000;
+constexpr int64_t kPeerWaitMaxUs = 60ll * 1000 * 1000;
+std::atomic<uint64_t> g_peer_wait_ns{kPeerWaitDefaultNs};
 
 bool peer_args_ok(int num_ranks, int rank, int64_t rows_per_rank, int32_t epoch, void* const* peer_bases,
                   const void* own_base) {
@@ -905,7 +911,7 @@ int b200moe_layer_packed_peer(void* own_base, void* const* peer_bases, int num_r
   float* w = reinterpret_cast<float*>(ids + R * topk);
   // waits for the G dispatch flags, then unpacks the ids and weights
   int st = cuda_status(launch_ep_unpack_meta_peer(own, rows, R, rb, H, topk, num_ranks, epoch, ids, w, err,
-                                                  kPeerWaitNs, s),
+                                                  g_peer_wait_ns.load(), s),
                        "ep_unpack_meta_peer");
   if (st) return st;
   LayerInput in{nullptr, rows, rb, reinterpret_cast<const float*>(rows + H), rb / 4};
@@ -925,9 +931,15 @@ int b200moe_ep_combine_peer(void* own_base, const int32_t* pos, int64_t M, int64
   if (!aligned16(out)) return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_combine_peer: 16-byte alignment%s");
   const EpPeerLayout lay(rows_per_rank, H, b200moe_ep_row_bytes(H, topk), num_ranks);
   return cuda_status(launch_ep_combine_peer(static_cast<const uint8_t*>(own_base), lay.ret_off(epoch), pos, M, H,
-                                            num_ranks, rows_per_rank, epoch, out, err_word, kPeerWaitNs,
+                                            num_ranks, rows_per_rank, epoch, out, err_word, g_peer_wait_ns.load(),
                                             (cudaStream_t)stream),
                      "ep_combine_peer");
+}
+
+int64_t b200moe_ep_peer_wait_limit_us(int64_t limit_us) {
+  const int64_t previous = (int64_t)(g_peer_wait_ns.load() / 1000);
+  if (limit_us > 0) g_peer_wait_ns.store((uint64_t)(limit_us < kPeerWaitMaxUs ? limit_us : kPeerWaitMaxUs) * 1000);
+  return previous;
 }
 
 int b200moe_router_topk(const void* logits, int logits_bf16, int64_t M, int num_experts, int topk, int scoring,

@@ -61,8 +61,11 @@ extern "C" int b200moe_layer_noalloc(const void* hidden, int64_t M, int64_t H, i
                                      const int32_t* expert_map, int num_local_experts, void* out,
                                      int32_t* err_out, void* stream) {
   const int E_plan = expert_map ? num_local_experts : num_experts;
+  // A zero size means the shape itself is invalid (M < 0, H, I or topk <= 0).
   const size_t need = b200moe_layer_workspace_size(M, H, I, num_experts, E_plan, topk);
-  if (need == 0 || need > kNoAllocScratchBytes)
+  if (need == 0 || E_plan <= 0)
+    return b200moe::record_error(B200MOE_ERR_INVALID_ARG, "b200moe_layer_noalloc: bad argument (layer shape)");
+  if (need > kNoAllocScratchBytes)
     return b200moe::record_error(B200MOE_ERR_WORKSPACE,
                                  "b200moe_layer_noalloc: layer needs more than the 64 MiB static scratch");
   void* scratch = nullptr;
