@@ -651,6 +651,61 @@ def run_sweep(args, shape, L, dev, clocks, peak):
             "peaks": {"hbm_gbs": peak, "fp8_tflops": FP8_PEAK_TFLOPS}}
 
 
+def run_router_record(args, shape, L, dev, clocks):
+    """The headline batch from router logits (GLM routing: sigmoid + correction
+    bias, top-k, renormalised, x2.5): the router as its own launch in front of
+    the layer (select_experts, then the layer's launches) against the router
+    inside routing's first launch (LayerPipeline.run_from_logits). Both give
+    the same bits; the record has each one's step time and launches."""
+    import torch
+
+    from trials_b200 import moe, stages
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 4000)
+    logits = torch.randn(shape.M, shape.E, generator=g, device=dev)
+    bias = torch.randn(shape.E, generator=g, device=dev) * 0.05
+    router = {"scoring_func": "sigmoid", "correction_bias": bias, "renormalize": True, "routed_scaling_factor": 2.5}
+    w = (L.w13, L.w13_scale, L.w2, L.w2_scale)
+    sep = stages.LayerPipeline(shape.M, shape.H, shape.I, shape.E, shape.topk, dev)
+    fus = stages.LayerPipeline(shape.M, shape.H, shape.I, shape.E, shape.topk, dev, router=router)
+
+    def separate():
+        tw, ids = moe.select_experts(logits, shape.topk, "sigmoid", bias, True, 2.5)
+        return sep.run(L.hidden, ids, tw, *w)
+
+    def fused():
+        return fus.run_from_logits(L.hidden, logits, *w)
+
+    rec = {"workload": f"glm_decode_M{shape.M}_from_router_logits",
+           "router": "sigmoid + correction bias, top-8, renormalised, x2.5",
+           "timing": "the two forms alternate over 3 rounds of sweep_steps steps; best round of each"}
+    forms = (("separate_router", separate, 1), ("fused_router", fused, 0))
+    for _, fn, _ in forms:
+        for _ in range(3):
+            fn()
+    best = {name: float("inf") for name, _, _ in forms}
+    for _ in range(3):
+        for name, fn, _ in forms:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            t0 = clocks.mark()
+            start.record()
+            for _ in range(args.sweep_steps):
+                fn()
+            end.record()
+            torch.cuda.synchronize()
+            clocks.window(t0, clocks.mark(), "sweep")
+            best[name] = min(best[name], start.elapsed_time(end) / args.sweep_steps)
+    for name, _, router_launches in forms:
+        launches = router_launches + len(sep.stages) + (1 if sep.tile > 64 else 0) + (1 if sep.rscratch_ints > 0 else 0)
+        rec[name] = {"ms_per_step": best[name], "gpu_launches_per_step": launches, "steps": args.sweep_steps}
+    rec["bit_equal"] = bool(torch.equal(separate(), fused()) and torch.equal(fus.topk_ids, moe.select_experts(
+        logits, shape.topk, "sigmoid", bias, True, 2.5)[1]))
+    rec["device_error"] = int(sep.err.item()) | int(fus.err.item())
+    return rec
+
+
 def run_ours(args, shape, config):
     import torch
     import torch.distributed as dist
@@ -732,7 +787,9 @@ def run_ours(args, shape, config):
     peak, peak_kind = measured_peaks()
     sweep = None
     if ws == 1 and not args.no_sweep:
+        router_rec = run_router_record(args, shape, L, dev, clocks)  # before the power-capped prefill points
         sweep = run_sweep(args, shape, L, dev, clocks, peak)
+        sweep["router_fused"] = router_rec
     clk = clocks.stop()
 
     # ---- CPU baseline (rank 0, one GPU only), with the GPU layer on the same sample

@@ -143,6 +143,27 @@ B200MOE_API int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t 
                   const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map,
                   int num_local_experts, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same layer starting from the router: router_logits (M, num_experts) f32
+ * (logits_bf16 = 0) or bf16 (1) go through the router of b200moe_router_topk
+ * (scoring, correction_bias, renormalize, scaling as there) inside routing's
+ * first launch, so the router costs no launch of its own (one launch for the
+ * router and routing below 16,384 routed slots, two above, as routing alone).
+ * The selected ids and weights are stored to topk_ids / topk_weights (M, topk)
+ * for the caller; the result equals b200moe_router_topk followed by
+ * b200moe_layer bit for bit. Replaces the router launch in front of the
+ * reference's MoE call (aiter topksoftmax, MBR/micro/glm52_fp8_moe.log; GLM's
+ * sigmoid routing, measure_xcd_imbalance.py:50-55) and the layer
+ * (sglang_integration/aiter.py:74-177). Workspace: b200moe_layer_workspace_size();
+ * its first 256 bytes must be zeroed once by the caller (the error word and
+ * the router's CTA counter, which every call leaves at zero). */
+B200MOE_API int b200moe_layer_logits(const void* hidden, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
+                                     const void* router_logits, int logits_bf16, int scoring,
+                                     const float* correction_bias, int renormalize, float scaling,
+                                     const uint8_t* w13, const float* w13_scale, const uint8_t* w2,
+                                     const float* w2_scale, const int32_t* expert_map, int num_local_experts,
+                                     float* topk_weights, int32_t* topk_ids, void* out, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 /* Same layer with pre-quantised activations: hidden_q (M, H) fp8 e4m3 and
  * hidden_scale (M, H/128) f32 from a 1x128 per-token-group quantisation. This
  * is the reference's fp8-input case (sglang_integration/aiter.py:126-130 with
@@ -160,6 +181,19 @@ B200MOE_API int b200moe_layer_quantized(const uint8_t* hidden_q, const float* hi
  * Replaces the dispatch/combine that the reference consumes from DeepEP/Mori
  * (sglang_integration/aiter.py:554-756: tokens arrive with local expert ids,
  * -1 for experts on other ranks, and leave as per-token partial sums).
+ *
+ * Expert placement (both dispatch forms): replicas == NULL places expert e on
+ * rank e / (E/G) only (slots_per_rank 0 or E/G). Otherwise every rank holds
+ * slots_per_rank physical experts (slot p = rank * slots_per_rank + local
+ * index; slots_per_rank * G >= E) and the device table replicas, E rows of
+ * 1 + max_replicas int32, lists for expert e its n >= 1 replicas:
+ * [n, p_0, .., p_{n-1}, unused]. This is hot-expert replication (EPLB; the
+ * reference's planned "--enable-eplb", moe_placement_glm52_mi355x.md:98-104).
+ * A routed slot (t, j) of expert e goes to e's replica on the sending rank
+ * `rank` if it has one, else to replica (t*topk + j) mod n; the destination
+ * then sees the local index p mod slots_per_rank as the slot's id. Rank r's
+ * weights are the logical experts of its slots, in slot order. An id whose
+ * table row names no valid slot is dropped and sets B200MOE_DEVERR_BAD_EXPERT_ID.
  *
  * Packed row (b200moe_ep_row_bytes(H, topk) bytes, 16-byte multiple):
  *   [ fp8 row: H bytes | 1x128 scales: H/128 f32 | topk local ids: int32, -1 =
@@ -181,7 +215,8 @@ B200MOE_API int b200moe_layer_quantized(const uint8_t* hidden_q, const float* hi
 B200MOE_API int64_t b200moe_ep_row_bytes(int64_t H, int topk);
 B200MOE_API int b200moe_ep_dispatch(const uint8_t* hidden_q, const float* hidden_scale, const int32_t* topk_ids,
                                     const float* topk_weights, int64_t M, int64_t H, int topk, int num_experts,
-                                    int num_ranks, int64_t rows_per_rank, uint8_t* send_rows, int32_t* pos,
+                                    int num_ranks, int rank, const int32_t* replicas, int max_replicas,
+                                    int slots_per_rank, int64_t rows_per_rank, uint8_t* send_rows, int32_t* pos,
                                     int32_t* tok_of, int32_t* counts, int32_t* err_word, void* stream);
 B200MOE_API size_t b200moe_layer_packed_workspace_size(int64_t R, int64_t H, int64_t I, int num_local_experts,
                                                        int topk);
@@ -231,9 +266,11 @@ B200MOE_API int b200moe_ep_peer_close(void* base);
 B200MOE_API int b200moe_ep_peer_free(void* base);
 B200MOE_API int b200moe_ep_dispatch_peer(const void* hidden, const uint8_t* hidden_q, const float* hidden_scale,
                                          const int32_t* topk_ids, const float* topk_weights, int64_t M, int64_t H,
-                                         int topk, int num_experts, int num_ranks, int rank, int64_t rows_per_rank,
-                                         void* const* peer_bases, void* own_base, int32_t epoch, int32_t* pos,
-                                         int32_t* tok_of, int32_t* counts, int32_t* err_word, void* stream);
+                                         int topk, int num_experts, int num_ranks, int rank,
+                                         const int32_t* replicas, int max_replicas, int slots_per_rank,
+                                         int64_t rows_per_rank, void* const* peer_bases, void* own_base,
+                                         int32_t epoch, int32_t* pos, int32_t* tok_of, int32_t* counts,
+                                         int32_t* err_word, void* stream);
 B200MOE_API int b200moe_layer_packed_peer(void* own_base, void* const* peer_bases, int num_ranks, int rank,
                                           int64_t rows_per_rank, int32_t epoch, int64_t H, int64_t I,
                                           int num_local_experts, int topk, const uint8_t* w13,
@@ -303,6 +340,24 @@ B200MOE_API int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int 
                   int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
                   int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
                   int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream);
+
+/* b200moe_route starting from router logits (the router of b200moe_router_topk
+ * fused into routing's first launch; ids and weights stored to topk_ids /
+ * topk_weights, then routed): results equal b200moe_router_topk followed by
+ * b200moe_route bit for bit. route_scratch (required) holds
+ * b200moe_route_logits_scratch_ints(M*topk, E) ints; its first int must be
+ * zero before the first call and every call leaves it zero. Replaces the
+ * reference's router launch (aiter topksoftmax) and moe_align_block_size. */
+B200MOE_API int64_t b200moe_route_logits_scratch_ints(int64_t numel, int num_local_experts);
+B200MOE_API int b200moe_route_logits(const void* logits, int logits_bf16, int64_t M, int num_experts, int topk,
+                                     int scoring, const float* correction_bias, int renormalize, float scaling,
+                                     float* topk_weights, int32_t* topk_ids, const int32_t* expert_map,
+                                     int num_local_experts, int tile_tokens, int32_t* sorted_ids,
+                                     int64_t rows_capacity, int32_t* chunk_expert, int32_t* chunk_row0,
+                                     int32_t* chunk_rows, int64_t chunks_capacity, int32_t* n_chunks,
+                                     int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
+                                     int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word,
+                                     void* stream);
 
 /* Quantise hidden rows into the sorted layout: for every flat slot f with
  * p = slot_pos[f] >= 0 (from b200moe_route), row p of a_q (ld = H) holds

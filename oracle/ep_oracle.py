@@ -13,6 +13,22 @@ import torch
 from . import moe_oracle as orc
 
 
+def target(table, slots: int, num_experts: int, src_rank: int, expert: int, t: int, j: int, topk: int) -> int:
+    """Physical slot of routed slot (t, j) (the dispatch's replica choice,
+    include/b200moe.h): the replica on the sending rank if there is one,
+    else replica (t*topk + j) mod n; table None = expert e in slot e."""
+    if expert < 0 or expert >= num_experts:
+        return -1
+    if table is None:
+        return expert
+    n = int(table[expert][0])
+    reps = [int(p) for p in table[expert][1:1 + n]]
+    for p in reps:
+        if p // slots == src_rank:
+            return p
+    return reps[(t * topk + j) % n]
+
+
 def row_bytes(H: int, topk: int) -> int:
     n = H + (H // 128) * 4 + 8 * topk
     return (n + 15) // 16 * 16
@@ -29,14 +45,19 @@ class OracleEPOps:
         q.copy_(qq)
         s.copy_(ss)
 
-    def dispatch(self, q, s, topk_ids, topk_weights, num_experts, G, rows_per_rank, send, pos, tok_of, counts, err):
+    def dispatch(self, q, s, topk_ids, topk_weights, num_experts, G, rows_per_rank, send, pos, tok_of, counts, err,
+                 rank=0, placement=None):
         M, H = q.shape
         topk = topk_ids.shape[1]
-        per = num_experts // G
+        table, slots = None, num_experts // G
+        if placement is not None:
+            table, slots = placement[0].cpu().numpy(), placement[1].slots
         rb = row_bytes(H, topk)
         buf = send.view(G * rows_per_rank, rb)
         ids = topk_ids.numpy()
-        owner = np.where((ids >= 0) & (ids < num_experts), ids // per, -1)
+        phys = np.array([[target(table, slots, num_experts, rank, int(ids[t, j]), t, j, topk) for j in range(topk)]
+                         for t in range(M)], dtype=np.int64).reshape(M, topk)
+        owner = np.where(phys >= 0, phys // slots, -1)
         pos_np = np.full((M, G), -1, dtype=np.int32)
         for d in range(G):
             need = np.nonzero((owner == d).any(axis=1))[0]
@@ -55,7 +76,7 @@ class OracleEPOps:
                 row[:H] = q[t].view(torch.uint8)
                 row[H:H + (H // 128) * 4] = s[t].contiguous().view(torch.uint8)
                 mine = owner[t] == d
-                local = np.where(mine, ids[t] - d * per, -1).astype(np.int32)
+                local = np.where(mine, phys[t] - d * slots, -1).astype(np.int32)
                 wts = np.where(mine, topk_weights[t].numpy(), 0.0).astype(np.float32)
                 meta[:topk] = torch.from_numpy(local)
                 meta[topk:2 * topk] = torch.from_numpy(wts).view(torch.int32)

@@ -78,9 +78,21 @@ def test_peer_exchange_host_checks():
     assert L.b200moe_ep_peer_bytes(cap, 100, topk, G) == 0    # H not a multiple of 128
     # epoch 0, a rank outside the group, an unaligned own buffer: refused before any launch
     args = [None, 16, 16, 16, 16, 8, H, topk, 16, G]
-    assert L.b200moe_ep_dispatch_peer(*args, 0, cap, 256, 256, 0, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG
-    assert L.b200moe_ep_dispatch_peer(*args, G, cap, 256, 256, 1, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG
-    assert L.b200moe_ep_dispatch_peer(*args, 0, cap, 256, 260, 1, 16, 16, 16, 16, None) == _lib.ERR_INVALID_ARG
+    ident = [None, 0, 0]
+    assert L.b200moe_ep_dispatch_peer(*args, 0, *ident, cap, 256, 256, 0, 16, 16, 16, 16, None) == \
+        _lib.ERR_INVALID_ARG
+    assert L.b200moe_ep_dispatch_peer(*args, G, *ident, cap, 256, 256, 1, 16, 16, 16, 16, None) == \
+        _lib.ERR_INVALID_ARG
+    assert L.b200moe_ep_dispatch_peer(*args, 0, *ident, cap, 256, 260, 1, 16, 16, 16, 16, None) == \
+        _lib.ERR_INVALID_ARG
+    # replica tables: slots * G must cover the experts, 1 <= max_replicas <= G
+    assert L.b200moe_ep_dispatch_peer(*args, 0, 16, 2, 3, cap, 256, 256, 1, 16, 16, 16, 16, None) == \
+        _lib.ERR_INVALID_ARG
+    assert L.b200moe_ep_dispatch_peer(*args, 0, 16, G + 1, 8, cap, 256, 256, 1, 16, 16, 16, 16, None) == \
+        _lib.ERR_INVALID_ARG
+    # without a table the experts must split evenly over the ranks
+    assert L.b200moe_ep_dispatch(16, 16, 16, 16, 8, H, topk, 18, G, 0, None, 0, 0, cap, 16, 16, 16, 16, 16, None) \
+        == _lib.ERR_INVALID_ARG
     assert L.b200moe_layer_packed_peer(256, 256, G, 0, cap, 0, H, 256, 4, topk, 16, 16, 16, 16, 256, 1 << 30,
                                        None) == _lib.ERR_INVALID_ARG
     assert L.b200moe_ep_combine_peer(256, 16, 8, H, topk, G, cap, 0, 16, 16, None) == _lib.ERR_INVALID_ARG

@@ -37,7 +37,7 @@ def _tokens(shape, rank, M):
     return hidden, tw, ids
 
 
-def _worker(rank, world, port, results, fail_rank):
+def _worker(rank, world, port, results, fail_rank, eplb=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.set_num_threads(1)
@@ -49,12 +49,19 @@ def _worker(rank, world, port, results, fail_rank):
     try:
         shape = synth.LayerShape(**SHAPE_KW)
         L = synth.make_layer(shape, orc.per_block_quant_fp8, seed=0)
-        model = ep.ExpertParallelMoE(ep.shard_experts(L.w13, rank, world), ep.shard_experts(L.w13_scale, rank, world),
-                                     ep.shard_experts(L.w2, rank, world), ep.shard_experts(L.w2_scale, rank, world),
-                                     num_experts=shape.E, rows_per_rank=shape.M, ops=ep_oracle.OracleEPOps(),
-                                     device="cpu")
         M = shape.M - 7 * rank  # ranks bring different token counts
         hidden, tw, ids = _tokens(shape, rank, M)
+        if eplb:
+            # every rank derives the same placement from the load of all ranks' tokens
+            load = sum(torch.bincount(_tokens(shape, r, shape.M - 7 * r)[2].reshape(-1), minlength=shape.E)
+                       for r in range(world))
+            pl = ep.eplb_placement(load.numpy(), world, shape.E // world + 1)
+            w = [ep.place_experts(t, pl, rank) for t in (L.w13, L.w13_scale, L.w2, L.w2_scale)]
+        else:
+            pl = None
+            w = [ep.shard_experts(t, rank, world) for t in (L.w13, L.w13_scale, L.w2, L.w2_scale)]
+        model = ep.ExpertParallelMoE(*w, num_experts=shape.E, rows_per_rank=shape.M, ops=ep_oracle.OracleEPOps(),
+                                     device="cpu", placement=pl)
         if rank == fail_rank:
             raise RuntimeError("injected failure before the exchange")
         out = model(hidden, tw, ids)
@@ -70,11 +77,11 @@ def _worker(rank, world, port, results, fail_rank):
             pass
 
 
-def _run(world, fail_rank=-1, timeout=120):
+def _run(world, fail_rank=-1, timeout=120, eplb=False):
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, results, fail_rank)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, results, fail_rank, eplb)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -88,9 +95,12 @@ def _run(world, fail_rank=-1, timeout=120):
     return out
 
 
+@pytest.mark.parametrize("eplb", [False, True], ids=["split", "replicated"])
 @pytest.mark.parametrize("world", [2, 4])
-def test_expert_parallel_matches_single_process_layer(world):
-    res = _run(world)
+def test_expert_parallel_matches_single_process_layer(world, eplb):
+    """eplb=True: hot experts replicated (one spare slot per rank) by
+    eplb_placement; the result is the same layer."""
+    res = _run(world, eplb=eplb)
     for rank in range(world):
         status, err, same = res[rank]
         assert status == "ok", res[rank]

@@ -198,7 +198,7 @@ def test_peer_exchange_simulated_ranks_bit_identical_to_all_to_all(cuda_device, 
                 _lib.check(lib.b200moe_ep_dispatch_peer(
                     hidden.data_ptr() if quantise_in_pack else None, None if quantise_in_pack else q.data_ptr(),
                     None if quantise_in_pack else s.data_ptr(), ids.data_ptr(), tw.data_ptr(), M, H, topk, SHAPE.E,
-                    G, r, cap,
+                    G, r, None, 0, 0, cap,
                     table.data_ptr(), bases[r], epoch, pos.data_ptr(), tok_of.data_ptr(), counts.data_ptr(),
                     err.data_ptr(), st), "dispatch_peer")
                 state.append((pos, err))
@@ -283,8 +283,8 @@ def test_peer_waits_end_with_timeout_when_a_rank_never_dispatches(cuda_device):
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
         _lib.check(lib.b200moe_ep_dispatch_peer(
-            hidden.data_ptr(), None, None, ids.data_ptr(), tw.data_ptr(), cap, H, topk, SHAPE.E, G, rank, cap,
-            table.data_ptr(), bufs[rank].data_ptr(), 1, pos.data_ptr(), tok_of.data_ptr(), counts.data_ptr(),
+            hidden.data_ptr(), None, None, ids.data_ptr(), tw.data_ptr(), cap, H, topk, SHAPE.E, G, rank, None, 0, 0,
+            cap, table.data_ptr(), bufs[rank].data_ptr(), 1, pos.data_ptr(), tok_of.data_ptr(), counts.data_ptr(),
             err.data_ptr(), st), "dispatch_peer")
         _lib.check(lib.b200moe_layer_packed_peer(
             bufs[rank].data_ptr(), table.data_ptr(), G, rank, cap, 1, H, I, per, topk, W["w13"].data_ptr(),

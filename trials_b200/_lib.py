@@ -42,9 +42,11 @@ SIGNATURES = {
     "b200moe_quant_block128": (_I, [_P, _L, _L, _L, _P, _P, _P]),
     "b200moe_layer_workspace_size": (_S, [_L, _L, _L, _I, _I, _I]),
     "b200moe_layer": (_I, [_P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _S, _P]),
+    "b200moe_layer_logits": (_I, [_P, _L, _L, _L, _I, _I, _P, _I, _I, _P, _I, ctypes.c_float, _P, _P, _P, _P, _P, _I,
+                                  _P, _P, _P, _P, _S, _P]),
     "b200moe_layer_quantized": (_I, [_P, _P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _S, _P]),
     "b200moe_ep_row_bytes": (_L, [_L, _I]),
-    "b200moe_ep_dispatch": (_I, [_P, _P, _P, _P, _L, _L, _I, _I, _I, _L, _P, _P, _P, _P, _P, _P]),
+    "b200moe_ep_dispatch": (_I, [_P, _P, _P, _P, _L, _L, _I, _I, _I, _I, _P, _I, _I, _L, _P, _P, _P, _P, _P, _P]),
     "b200moe_layer_packed_workspace_size": (_S, [_L, _L, _L, _I, _I]),
     "b200moe_layer_packed": (_I, [_P, _L, _I, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _S, _P]),
     "b200moe_ep_combine": (_I, [_P, _P, _L, _L, _I, _L, _P, _P]),
@@ -53,8 +55,8 @@ SIGNATURES = {
     "b200moe_ep_peer_open": (_I, [_P, ctypes.POINTER(_P)]),
     "b200moe_ep_peer_close": (_I, [_P]),
     "b200moe_ep_peer_free": (_I, [_P]),
-    "b200moe_ep_dispatch_peer": (_I, [_P, _P, _P, _P, _P, _L, _L, _I, _I, _I, _I, _L, _P, _P, ctypes.c_int32, _P, _P,
-                                      _P, _P, _P]),
+    "b200moe_ep_dispatch_peer": (_I, [_P, _P, _P, _P, _P, _L, _L, _I, _I, _I, _I, _P, _I, _I, _L, _P, _P,
+                                      ctypes.c_int32, _P, _P, _P, _P, _P]),
     "b200moe_layer_packed_peer": (_I, [_P, _P, _I, _I, _L, ctypes.c_int32, _L, _L, _I, _I, _P, _P, _P, _P, _P, _S,
                                        _P]),
     "b200moe_ep_combine_peer": (_I, [_P, _P, _L, _L, _I, _I, _L, ctypes.c_int32, _P, _P, _P]),
@@ -64,6 +66,9 @@ SIGNATURES = {
     "b200moe_route_capacity_chunks": (_L, [_L, _I, _I]),
     "b200moe_route_scratch_ints": (_L, [_L, _I]),
     "b200moe_route": (_I, [_P, _L, _I, _I, _P, _I, _I, _P, _L, _P, _P, _P, _L, _P, _P, _P, _P, _P, _L, _P, _P]),
+    "b200moe_route_logits_scratch_ints": (_L, [_L, _I]),
+    "b200moe_route_logits": (_I, [_P, _I, _L, _I, _I, _I, _P, _I, ctypes.c_float, _P, _P, _P, _I, _I, _P, _L, _P, _P,
+                                  _P, _L, _P, _P, _P, _P, _P, _L, _P, _P]),
     "b200moe_gather_quant": (_I, [_P, _L, _L, _I, _P, _L, _P, _P, _L, _P]),
     "b200moe_gather_rows": (_I, [_P, _P, _L, _L, _L, _L, _I, _P, _L, _P, _P, _L, _P]),
     "b200moe_gemm1_silu": (_I, [_P, _P, _L, _L, _P, _P, _I, _L, _L, _P, _P, _P, _P, _L, _I, _P, _P, _P, _I, _P]),

@@ -13,6 +13,7 @@
 #include "../../include/b200moe.h"
 #include "launch.h"
 #include "moe_gemm.cuh"
+#include "router.cuh"
 
 using namespace b200moe;
 
@@ -207,6 +208,21 @@ namespace b200moe {
 int record_error(int status, const char* message) { return fail(status, "%s", message); }
 }  // namespace b200moe
 
+namespace {
+
+// Host checks of the router arguments (b200moe_router_topk and routing from logits).
+int check_router(const char* name, const void* logits, int64_t M, int num_experts, int topk, int scoring,
+                 const float* correction_bias, const float* topk_weights, const int32_t* topk_ids) {
+  if (M < 0 || num_experts <= 0 || topk <= 0 || topk > num_experts || (scoring != 0 && scoring != 1) ||
+      (M > 0 && (!logits || !topk_weights || !topk_ids)) || (correction_bias && scoring != 1))
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: bad router argument", name);
+  if (num_experts > 1024 || topk > kRouterMaxTopk)
+    return fail(B200MOE_ERR_UNSUPPORTED, "%s: at most 1024 experts and top-16", name);
+  return B200MOE_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int b200moe_version(void) { return 100; }
@@ -310,11 +326,18 @@ int64_t b200moe_route_scratch_ints(int64_t numel, int num_local_experts) {
   return route_scratch_ints(numel, num_local_experts);
 }
 
-int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
-                  int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
-                  int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
-                  int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
-                  int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// b200moe_route, and b200moe_route_logits when `router` is set (topk_ids then
+// names the router's id output, which routing reads after the router stored it).
+int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
+               int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
+               int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
+               int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
+               int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream,
+               const RouterArgs* router, int32_t* router_counter) {
   if (M < 0 || topk <= 0 || num_experts <= 0 || !valid_tile(tile_tokens) || !sorted_ids || !chunk_expert ||
       !chunk_row0 || !chunk_rows || !n_chunks || !num_rows || !err_word || (M > 0 && !topk_ids))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_route: bad argument%s");
@@ -346,7 +369,53 @@ int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts,
   a.chunk_ready = chunk_ready;
   a.slot_pos = slot_pos;
   a.err = err_word;
+  if (router) {
+    // The CTA counter: router_counter, or the first ints of route_scratch.
+    int32_t* counts = router_counter ? route_scratch : route_scratch + kRouteLogitsCounterInts;
+    const int64_t counts_ints = router_counter ? route_scratch_ints : route_scratch_ints - kRouteLogitsCounterInts;
+    int32_t* counter = router_counter ? router_counter : route_scratch;
+    const int64_t need = b200moe::route_scratch_ints(numel, E);
+    if (!counter || counts_ints < need || (need > 0 && !counts))
+      return fail(B200MOE_ERR_WORKSPACE, "b200moe_route_logits: route_scratch too small%s");
+    return cuda_status(launch_route_logits(a, *router, M, counter, counts, (cudaStream_t)stream), "route_logits");
+  }
   return cuda_status(launch_route(a, route_scratch, route_scratch_ints, (cudaStream_t)stream), "route");
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
+                  int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
+                  int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
+                  int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
+                  int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream) {
+  return route_impl(topk_ids, M, topk, num_experts, expert_map, num_local_experts, tile_tokens, sorted_ids,
+                    rows_capacity, chunk_expert, chunk_row0, chunk_rows, chunks_capacity, n_chunks, num_rows,
+                    slot_pos, chunk_ready, route_scratch, route_scratch_ints, err_word, stream, nullptr, nullptr);
+}
+
+int64_t b200moe_route_logits_scratch_ints(int64_t numel, int num_local_experts) {
+  if (numel < 0 || num_local_experts <= 0) return 0;
+  return route_logits_scratch_ints(numel, num_local_experts);
+}
+
+int b200moe_route_logits(const void* logits, int logits_bf16, int64_t M, int num_experts, int topk, int scoring,
+                         const float* correction_bias, int renormalize, float scaling, float* topk_weights,
+                         int32_t* topk_ids, const int32_t* expert_map, int num_local_experts, int tile_tokens,
+                         int32_t* sorted_ids, int64_t rows_capacity, int32_t* chunk_expert, int32_t* chunk_row0,
+                         int32_t* chunk_rows, int64_t chunks_capacity, int32_t* n_chunks, int32_t* num_rows,
+                         int32_t* slot_pos, int32_t* chunk_ready, int32_t* route_scratch,
+                         int64_t route_scratch_ints, int32_t* err_word, void* stream) {
+  int st = check_router("b200moe_route_logits", logits, M, num_experts, topk, scoring, correction_bias, topk_weights,
+                        topk_ids);
+  if (st) return st;
+  const RouterArgs r{logits, logits_bf16 ? 1 : 0, num_experts, topk, scoring, renormalize ? 1 : 0,
+                     correction_bias, scaling, topk_weights, topk_ids};
+  return route_impl(topk_ids, M, topk, num_experts, expert_map, num_local_experts, tile_tokens, sorted_ids,
+                    rows_capacity, chunk_expert, chunk_row0, chunk_rows, chunks_capacity, n_chunks, num_rows,
+                    slot_pos, chunk_ready, route_scratch, route_scratch_ints, err_word, stream, &r, nullptr);
 }
 
 int b200moe_gather_quant(const void* hidden, int64_t M, int64_t H, int topk, const int32_t* slot_pos,
@@ -646,7 +715,8 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
                const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
                const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map, int num_local_experts,
                void* out, void* workspace, size_t workspace_bytes, size_t workspace_offset, void* stream,
-               const EpPeerArgs* peer_out = nullptr, int32_t* peer_counter = nullptr, int64_t tile_numel = -1) {
+               const EpPeerArgs* peer_out = nullptr, int32_t* peer_counter = nullptr, int64_t tile_numel = -1,
+               const RouterArgs* router = nullptr) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (M < 0 || topk <= 0 || num_experts <= 0) return fail(B200MOE_ERR_INVALID_ARG, "%s: bad argument", name);
@@ -679,8 +749,11 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   __nv_bfloat16* pair = reinterpret_cast<__nv_bfloat16*>(wl + pl.off_pair);
 
   int32_t* rscratch = pl.rscratch_ints > 0 ? reinterpret_cast<int32_t*>(wl + pl.off_rscratch) : nullptr;
-  st = b200moe_route(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0,
-                     crows, pl.chunks_cap, counts, counts + 1, pos, ready, rscratch, pl.rscratch_ints, err, stream);
+  // Routing from router logits: the router's CTA counter is int 1 of the
+  // workspace header (zeroed with the error word; every call leaves it zero).
+  st = route_impl(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0, crows,
+                  pl.chunks_cap, counts, counts + 1, pos, ready, rscratch, pl.rscratch_ints, err, stream, router,
+                  router ? err + 1 : nullptr);
   if (st) return st;
   const LayerInput& src = in;
   if (src.hidden) {
@@ -730,21 +803,71 @@ int b200moe_layer_quantized(const uint8_t* hidden_q, const float* hidden_scale, 
                     stream);
 }
 
+int b200moe_layer_logits(const void* hidden, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
+                         const void* router_logits, int logits_bf16, int scoring, const float* correction_bias,
+                         int renormalize, float scaling, const uint8_t* w13, const float* w13_scale,
+                         const uint8_t* w2, const float* w2_scale, const int32_t* expert_map, int num_local_experts,
+                         float* topk_weights, int32_t* topk_ids, void* out, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (!hidden && M > 0) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_layer_logits: null hidden%s");
+  int st = check_router("b200moe_layer_logits", router_logits, M, num_experts, topk, scoring, correction_bias,
+                        topk_weights, topk_ids);
+  if (st) return st;
+  const RouterArgs r{router_logits, logits_bf16 ? 1 : 0, num_experts, topk, scoring, renormalize ? 1 : 0,
+                     correction_bias, scaling, topk_weights, topk_ids};
+  LayerInput in{hidden, nullptr, 0, nullptr, 0};
+  return layer_core("b200moe_layer_logits", in, M, H, I, num_experts, topk, w13, w13_scale, w2, w2_scale,
+                    topk_weights, topk_ids, expert_map, num_local_experts, out, workspace, workspace_bytes, 0, stream,
+                    nullptr, nullptr, -1, &r);
+}
+
 int64_t b200moe_ep_row_bytes(int64_t H, int topk) { return round_up(H + (H / 128) * 4 + 8 * (int64_t)topk, 16); }
+
+}  // extern "C"
+
+namespace {
+
+// The expert placement of a dispatch: identity (replicas == nullptr: E/G
+// experts per rank, slots_per_rank 0 or E/G) or a replica table.
+int make_place(const char* name, int num_experts, int num_ranks, int rank, const int32_t* replicas,
+               int max_replicas, int slots_per_rank, EpPlace& pl) {
+  if (num_experts <= 0 || num_ranks <= 0 || num_ranks > EpPeerLayout::kMaxRanks || rank < 0 || rank >= num_ranks)
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: bad expert or rank count", name);
+  if (!replicas) {
+    if (num_experts % num_ranks != 0 || (slots_per_rank != 0 && slots_per_rank != num_experts / num_ranks))
+      return fail(B200MOE_ERR_INVALID_ARG, "%s: without a replica table num_experts must split evenly", name);
+    pl = EpPlace{nullptr, 0, num_experts / num_ranks, num_experts, rank, num_ranks};
+    return B200MOE_OK;
+  }
+  if (max_replicas < 1 || max_replicas > num_ranks || slots_per_rank < 1 ||
+      (int64_t)slots_per_rank * num_ranks < num_experts || slots_per_rank > 1024)
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: bad replica table shape", name);
+  pl = EpPlace{replicas, max_replicas, slots_per_rank, num_experts, rank, num_ranks};
+  return B200MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
 
 int b200moe_ep_dispatch(const uint8_t* hidden_q, const float* hidden_scale, const int32_t* topk_ids,
                         const float* topk_weights, int64_t M, int64_t H, int topk, int num_experts, int num_ranks,
+                        int rank, const int32_t* replicas, int max_replicas, int slots_per_rank,
                         int64_t rows_per_rank, uint8_t* send_rows, int32_t* pos, int32_t* tok_of, int32_t* counts,
                         int32_t* err_word, void* stream) {
-  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || num_ranks <= 0 || num_experts % num_ranks != 0 ||
-      rows_per_rank < 0 || !err_word || !counts || (M > 0 && (!hidden_q || !hidden_scale || !topk_ids ||
-      !topk_weights || !pos)) || (rows_per_rank > 0 && (!send_rows || !tok_of)))
+  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || rows_per_rank < 0 || !err_word || !counts ||
+      (M > 0 && (!hidden_q || !hidden_scale || !topk_ids || !topk_weights || !pos)) ||
+      (rows_per_rank > 0 && (!send_rows || !tok_of)))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_dispatch: bad argument%s");
+  EpPlace pl;
+  int st = make_place("b200moe_ep_dispatch", num_experts, num_ranks, rank, replicas, max_replicas, slots_per_rank,
+                      pl);
+  if (st) return st;
   if (!aligned16(hidden_q) || !aligned16(send_rows))
     return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_dispatch: 16-byte alignment required%s");
-  return cuda_status(launch_ep_dispatch(hidden_q, hidden_scale, topk_ids, topk_weights, M, H, topk, num_experts,
-                                        num_ranks, rows_per_rank, send_rows, b200moe_ep_row_bytes(H, topk), pos,
-                                        tok_of, counts, err_word, (cudaStream_t)stream),
+  return cuda_status(launch_ep_dispatch(hidden_q, hidden_scale, topk_ids, topk_weights, M, H, topk, pl,
+                                        rows_per_rank, send_rows, b200moe_ep_row_bytes(H, topk), pos, tok_of, counts,
+                                        err_word, (cudaStream_t)stream),
                      "ep_dispatch");
 }
 
@@ -859,29 +982,32 @@ bool peer_args_ok(int num_ranks, int rank, int64_t rows_per_rank, int32_t epoch,
 
 int b200moe_ep_dispatch_peer(const void* hidden, const uint8_t* hidden_q, const float* hidden_scale,
                              const int32_t* topk_ids, const float* topk_weights, int64_t M, int64_t H, int topk,
-                             int num_experts,
-                             int num_ranks, int rank, int64_t rows_per_rank, void* const* peer_bases, void* own_base,
+                             int num_experts, int num_ranks, int rank, const int32_t* replicas, int max_replicas,
+                             int slots_per_rank, int64_t rows_per_rank, void* const* peer_bases, void* own_base,
                              int32_t epoch, int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err_word,
                              void* stream) {
-  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || num_experts % num_ranks != 0 || !err_word || !counts ||
+  if (M < 0 || H <= 0 || H % 128 != 0 || topk <= 0 || !err_word || !counts ||
       !peer_args_ok(num_ranks, rank, rows_per_rank, epoch, peer_bases, own_base) ||
       (M > 0 && (!(hidden || (hidden_q && hidden_scale)) || !topk_ids || !topk_weights || !pos)) ||
       (rows_per_rank > 0 && !tok_of))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_ep_dispatch_peer: bad argument%s");
+  EpPlace pl;
+  int st0 = make_place("b200moe_ep_dispatch_peer", num_experts, num_ranks, rank, replicas, max_replicas,
+                       slots_per_rank, pl);
+  if (st0) return st0;
   if (!aligned16(hidden) || !aligned16(hidden_q))
     return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_ep_dispatch_peer: 16-byte alignment%s");
   const int64_t rb = b200moe_ep_row_bytes(H, topk);
   const EpPeerLayout lay(rows_per_rank, H, rb, num_ranks);
   cudaStream_t s = (cudaStream_t)stream;
-  int st = cuda_status(launch_ep_plan(topk_ids, M, topk, num_experts, num_ranks, rows_per_rank, pos, tok_of, counts,
-                                      err_word, s),
+  int st = cuda_status(launch_ep_plan(topk_ids, M, topk, pl, rows_per_rank, pos, tok_of, counts, err_word, s),
                        "ep_plan");
   if (st) return st;
   const EpPeerArgs a{reinterpret_cast<uint8_t* const*>(peer_bases), lay.recv_off(epoch), rows_per_rank, num_ranks,
                      rank, epoch};
   int32_t* counter = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(own_base) + EpPeerLayout::kCounters);
-  return cuda_status(launch_ep_pack_peer(hidden, hidden_q, hidden_scale, topk_ids, topk_weights, H, topk,
-                                         num_experts, tok_of, counts, rb, a, counter, s),
+  return cuda_status(launch_ep_pack_peer(hidden, hidden_q, hidden_scale, topk_ids, topk_weights, H, topk, pl, tok_of,
+                                         counts, rb, a, counter, s),
                      "ep_pack_peer");
 }
 
@@ -945,11 +1071,9 @@ int64_t b200moe_ep_peer_wait_limit_us(int64_t limit_us) {
 int b200moe_router_topk(const void* logits, int logits_bf16, int64_t M, int num_experts, int topk, int scoring,
                         const float* correction_bias, int renormalize, float scaling, float* topk_weights,
                         int32_t* topk_ids, void* stream) {
-  if (M < 0 || num_experts <= 0 || topk <= 0 || topk > num_experts || (scoring != 0 && scoring != 1) ||
-      (M > 0 && (!logits || !topk_weights || !topk_ids)) || (correction_bias && scoring != 1))
-    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_router_topk: bad argument%s");
-  if (num_experts > 1024 || topk > 16)
-    return fail(B200MOE_ERR_UNSUPPORTED, "b200moe_router_topk: at most 1024 experts and top-16%s");
+  int st = check_router("b200moe_router_topk", logits, M, num_experts, topk, scoring, correction_bias, topk_weights,
+                        topk_ids);
+  if (st) return st;
   return cuda_status(launch_router_topk(logits, logits_bf16, M, num_experts, topk, scoring, correction_bias,
                                         renormalize, scaling, topk_weights, topk_ids, (cudaStream_t)stream),
                      "router_topk");

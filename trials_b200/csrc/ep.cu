@@ -1,8 +1,10 @@
 // Expert-parallel dispatch and combine kernels.
 //
-// Rank r of G owns experts [r*E/G, (r+1)*E/G). A token is sent once to every
-// rank that owns at least one of its top-k experts, as one fixed-size packed
-// row (layout in include/b200moe.h, b200moe_ep_row_bytes):
+// Rank r of G owns experts [r*E/G, (r+1)*E/G), or, with a replica table
+// (EpPlace, EPLB), the physical expert slots [r*S, (r+1)*S) that the table
+// gives replicas of the logical experts. A token is sent once to every
+// rank that holds the chosen replica of at least one of its top-k experts, as
+// one fixed-size packed row (layout in include/b200moe.h, b200moe_ep_row_bytes):
 //   [ fp8 row (H B) | 1x128 scales (H/128 f32) | k local ids (int32, -1 = not
 //     on that rank) | k router weights (f32) ]
 // Rows for destination d occupy block d of the send buffer, rows_per_rank rows
@@ -12,6 +14,7 @@
 // returns one bf16 row per received row (its experts' weighted sum); the
 // source adds the rows from each rank in rank order.
 #include "common.cuh"
+#include "ep_place.cuh"
 #include "launch.h"
 
 namespace b200moe {
@@ -20,20 +23,17 @@ namespace {
 
 constexpr int kPlanThreads = 1024;
 
-__device__ __forceinline__ int owner_of(int id, int num_experts, int per_rank) {
-  return (id >= 0 && id < num_experts) ? id / per_rank : -1;
-}
-
-// One CTA per destination rank: stable positions of the tokens it needs.
+// One CTA per destination rank: stable positions of the tokens it needs (the
+// tokens with at least one routed slot whose replica, ep_target, is on it).
 __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int32_t* __restrict__ ids, int64_t M, int topk,
-                                                                int num_experts, int G, int64_t rows_per_rank,
+                                                                const EpPlace pl, int64_t rows_per_rank,
                                                                 int32_t* __restrict__ pos,
                                                                 int32_t* __restrict__ tok_of,
                                                                 int32_t* __restrict__ counts, int32_t* err) {
   __shared__ int warp_tot[32];
   __shared__ int base_s;
   const int d = blockIdx.x;
-  const int per_rank = num_experts / G;
+  const int G = pl.G, num_experts = pl.num_experts;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) base_s = 0;
   __syncthreads();
@@ -43,8 +43,11 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int32_t* __
     if (t < M) {
       for (int j = 0; j < topk; ++j) {
         const int id = __ldg(&ids[t * topk + j]);
-        if (owner_of(id, num_experts, per_rank) == d) need = 1;
-        if (d == 0 && id != -1 && (id < 0 || id >= num_experts)) atomicOr(err, ERR_DEV_BAD_EXPERT);
+        const int p = ep_target(pl, id, t, j, topk);
+        if (p >= 0 && p / pl.slots == d) need = 1;
+        // ids outside the expert range (other than -1), or a replica table that
+        // names no physical slot for a valid id, are dropped and reported
+        if (d == 0 && id != -1 && p < 0) atomicOr(err, ERR_DEV_BAD_EXPERT);
       }
     }
     int x = need;
@@ -85,16 +88,15 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int32_t* __
 // its local ids and weights; rows past the count get ids -1.
 __global__ void __launch_bounds__(256) ep_pack_kernel(const uint8_t* __restrict__ q, const float* __restrict__ s,
                                                       const int32_t* __restrict__ ids, const float* __restrict__ w,
-                                                      int64_t H, int topk, int num_experts, int G,
+                                                      int64_t H, int topk, const EpPlace pl,
                                                       int64_t rows_per_rank, const int32_t* __restrict__ tok_of,
                                                       const int32_t* __restrict__ counts, uint8_t* __restrict__ send,
                                                       int64_t row_bytes) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= (int64_t)G * rows_per_rank) return;
+  if (row >= (int64_t)pl.G * rows_per_rank) return;
   const int d = (int)(row / rows_per_rank);
   const int64_t r = row - (int64_t)d * rows_per_rank;
-  const int per_rank = num_experts / G;
   uint8_t* dst = send + row * row_bytes;
   int32_t* dst_ids = reinterpret_cast<int32_t*>(dst + H + (H / 128) * 4);
   float* dst_w = reinterpret_cast<float*>(dst_ids + topk);
@@ -112,9 +114,9 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint8_t* __restrict_
   float* dst_s = reinterpret_cast<float*>(dst + H);
   for (int64_t g = lane; g < H / 128; g += 32) dst_s[g] = __ldg(&s[t * (H / 128) + g]);
   for (int j = lane; j < topk; j += 32) {
-    const int id = __ldg(&ids[t * topk + j]);
-    const bool mine = owner_of(id, num_experts, per_rank) == d;
-    dst_ids[j] = mine ? id - d * per_rank : -1;
+    const int p = ep_target(pl, __ldg(&ids[t * topk + j]), t, j, topk);
+    const bool mine = p >= 0 && p / pl.slots == d;
+    dst_ids[j] = mine ? p - d * pl.slots : -1;
     dst_w[j] = mine ? __ldg(&w[t * topk + j]) : 0.f;
   }
 }
@@ -164,23 +166,22 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __
 
 }  // namespace
 
-cudaError_t launch_ep_plan(const int32_t* ids, int64_t M, int topk, int num_experts, int G, int64_t rows_per_rank,
+cudaError_t launch_ep_plan(const int32_t* ids, int64_t M, int topk, const EpPlace& pl, int64_t rows_per_rank,
                            int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err, cudaStream_t stream) {
-  ep_plan_kernel<<<G, kPlanThreads, 0, stream>>>(ids, M, topk, num_experts, G, rows_per_rank, pos, tok_of, counts,
-                                                 err);
+  ep_plan_kernel<<<pl.G, kPlanThreads, 0, stream>>>(ids, M, topk, pl, rows_per_rank, pos, tok_of, counts, err);
   return cudaGetLastError();
 }
 
 cudaError_t launch_ep_dispatch(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t M,
-                               int64_t H, int topk, int num_experts, int G, int64_t rows_per_rank, uint8_t* send,
+                               int64_t H, int topk, const EpPlace& pl, int64_t rows_per_rank, uint8_t* send,
                                int64_t row_bytes, int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err,
                                cudaStream_t stream) {
-  cudaError_t e = launch_ep_plan(ids, M, topk, num_experts, G, rows_per_rank, pos, tok_of, counts, err, stream);
+  cudaError_t e = launch_ep_plan(ids, M, topk, pl, rows_per_rank, pos, tok_of, counts, err, stream);
   if (e != cudaSuccess) return e;
-  const int64_t rows = (int64_t)G * rows_per_rank;
+  const int64_t rows = (int64_t)pl.G * rows_per_rank;
   if (rows == 0) return cudaSuccess;
-  ep_pack_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(q, s, ids, w, H, topk, num_experts, G,
-                                                                  rows_per_rank, tok_of, counts, send, row_bytes);
+  ep_pack_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(q, s, ids, w, H, topk, pl, rows_per_rank, tok_of,
+                                                                  counts, send, row_bytes);
   return cudaGetLastError();
 }
 

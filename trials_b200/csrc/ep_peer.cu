@@ -21,6 +21,7 @@
 // of call e had read the area. Waits are bounded by %globaltimer and set
 // B200MOE_DEVERR_TIMEOUT on expiry.
 #include "common.cuh"
+#include "ep_place.cuh"
 #include "launch.h"
 #include "ptx.cuh"
 #include "rowops.cuh"
@@ -90,7 +91,7 @@ __global__ void __launch_bounds__(256) ep_pack_peer_kernel(const __nv_bfloat16* 
                                                            const uint8_t* __restrict__ q, const float* __restrict__ s,
                                                            const int32_t* __restrict__ ids,
                                                            const float* __restrict__ w, int64_t H, int topk,
-                                                           int num_experts, const int32_t* __restrict__ tok_of,
+                                                           const EpPlace pl, const int32_t* __restrict__ tok_of,
                                                            const int32_t* __restrict__ counts, int64_t row_bytes,
                                                            const EpPeerArgs a, int32_t* counter) {
   const int lane = threadIdx.x & 31;
@@ -99,7 +100,6 @@ __global__ void __launch_bounds__(256) ep_pack_peer_kernel(const __nv_bfloat16* 
   if (row < (int64_t)a.G * a.rows_per_rank) {
     const int d = (int)(row / a.rows_per_rank);
     const int64_t r = row - (int64_t)d * a.rows_per_rank;
-    const int per_rank = num_experts / a.G;
     uint8_t* dst = a.bases[d] + a.area_off + ((int64_t)a.rank * a.rows_per_rank + r) * row_bytes;
     int32_t* dst_ids = reinterpret_cast<int32_t*>(dst + H + (H / 128) * 4);
     float* dst_w = reinterpret_cast<float*>(dst_ids + topk);
@@ -122,9 +122,9 @@ __global__ void __launch_bounds__(256) ep_pack_peer_kernel(const __nv_bfloat16* 
     }
     if (blockIdx.y == 0) {
       for (int j = lane; j < topk; j += 32) {
-        const int id = used ? __ldg(&ids[t * topk + j]) : -1;
-        const bool mine = used && id >= 0 && id < num_experts && id / per_rank == d;
-        dst_ids[j] = mine ? id - d * per_rank : -1;
+        const int p = used ? ep_target(pl, __ldg(&ids[t * topk + j]), t, j, topk) : -1;
+        const bool mine = p >= 0 && p / pl.slots == d;
+        dst_ids[j] = mine ? p - d * pl.slots : -1;
         dst_w[j] = mine ? __ldg(&w[t * topk + j]) : 0.f;
       }
     }
@@ -208,15 +208,14 @@ __global__ void __launch_bounds__(256) ep_combine_peer_kernel(const uint8_t* own
 }  // namespace
 
 cudaError_t launch_ep_pack_peer(const void* hidden, const uint8_t* q, const float* s, const int32_t* ids,
-                                const float* w, int64_t H, int topk, int num_experts, const int32_t* tok_of,
+                                const float* w, int64_t H, int topk, const EpPlace& pl, const int32_t* tok_of,
                                 const int32_t* counts, int64_t row_bytes, const EpPeerArgs& a, int32_t* counter,
                                 cudaStream_t stream) {
   const int64_t rows = (int64_t)a.G * a.rows_per_rank;
   const dim3 grid((unsigned)(rows > 0 ? (rows + 7) / 8 : 1),  // one CTA at least, to raise the flags
                   (unsigned)((H + kQuantSegCols - 1) / kQuantSegCols));
-  ep_pack_peer_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(hidden), q, s, ids, w,
-                                                             H, topk, num_experts, tok_of, counts, row_bytes, a,
-                                                             counter);
+  ep_pack_peer_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(hidden), q, s, ids, w, H, topk, pl,
+                                                tok_of, counts, row_bytes, a, counter);
   return cudaGetLastError();
 }
 

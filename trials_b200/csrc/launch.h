@@ -32,6 +32,7 @@ struct AlignArgs {
   int32_t* chunk_ready;    // nullable: zeroed over chunks_cap + 2 entries
   int32_t* slot_pos;       // nullable: sorted position of each flat slot (n entries), -1 if dropped
   int32_t* err;
+  int seg_align;           // multi-CTA segments: multiple of this many ids (0/1 = any)
 };
 
 size_t align_smem_bytes(int E);
@@ -41,6 +42,16 @@ cudaError_t launch_align(const AlignArgs& a, cudaStream_t stream);
 int route_ctas(int64_t n);
 int64_t route_scratch_ints(int64_t n, int E);
 cudaError_t launch_route(const AlignArgs& a, int32_t* scratch, int64_t scratch_ints, cudaStream_t stream);
+// Routing from router logits: the router (router.cuh) runs in routing's first
+// launch and stores topk ids and weights to r.out_ids / r.out_w, which routing
+// then uses as a.topk_ids. scratch: kRouteLogitsCounterInts ints (a CTA
+// counter that must be zero before the first call; every call leaves it zero)
+// followed by the route_scratch_ints(n, E) counts of the multi-CTA form.
+struct RouterArgs;
+constexpr int kRouteLogitsCounterInts = 4;
+int64_t route_logits_scratch_ints(int64_t n, int E);
+cudaError_t launch_route_logits(const AlignArgs& a, const RouterArgs& r, int64_t M, int32_t* counter,
+                                int32_t* counts, cudaStream_t stream);
 
 // Per-token-group (1 x 128) FP8 quantisation. With sorted_ids != nullptr the
 // output row p takes its input from token sorted_ids[p] / topk (zeros for the
@@ -81,10 +92,24 @@ cudaError_t launch_quant_block128(const void* w, int64_t E, int64_t N, int64_t K
 cudaError_t launch_combine_reduce(const void* pair_rows, const int32_t* slot_pos, int sorted_rows, int64_t M, int topk,
                                   int64_t H, void* out, cudaStream_t stream);
 
-cudaError_t launch_ep_plan(const int32_t* ids, int64_t M, int topk, int num_experts, int G, int64_t rows_per_rank,
+// Where each expert's weights live for expert parallelism: physical expert
+// slots p = rank * slots + local index. rep == nullptr: expert e only in slot
+// e (slots = num_experts / G, rank r holds [r*slots, (r+1)*slots)). Otherwise
+// rep[e * (1 + max_rep)] = n replicas of e, followed by their n slots; a
+// routed slot (t, j) of expert e goes to the replica on src_rank if there is
+// one, else to replica (t * topk + j) mod n (ep_place.cuh).
+struct EpPlace {
+  const int32_t* rep;
+  int max_rep;
+  int slots;
+  int num_experts;
+  int src_rank;
+  int G;
+};
+cudaError_t launch_ep_plan(const int32_t* ids, int64_t M, int topk, const EpPlace& pl, int64_t rows_per_rank,
                            int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err, cudaStream_t stream);
 cudaError_t launch_ep_dispatch(const uint8_t* q, const float* s, const int32_t* ids, const float* w, int64_t M,
-                               int64_t H, int topk, int num_experts, int G, int64_t rows_per_rank, uint8_t* send,
+                               int64_t H, int topk, const EpPlace& pl, int64_t rows_per_rank, uint8_t* send,
                                int64_t row_bytes, int32_t* pos, int32_t* tok_of, int32_t* counts, int32_t* err,
                                cudaStream_t stream);
 cudaError_t launch_ep_unpack_meta(const uint8_t* rows, int64_t R, int64_t row_bytes, int64_t H, int topk,
@@ -121,7 +146,7 @@ struct EpPeerArgs {
   int32_t epoch;
 };
 cudaError_t launch_ep_pack_peer(const void* hidden, const uint8_t* q, const float* s, const int32_t* ids,
-                                const float* w, int64_t H, int topk, int num_experts, const int32_t* tok_of,
+                                const float* w, int64_t H, int topk, const EpPlace& pl, const int32_t* tok_of,
                                 const int32_t* counts, int64_t row_bytes, const EpPeerArgs& a, int32_t* counter,
                                 cudaStream_t stream);
 cudaError_t launch_ep_unpack_meta_peer(const uint8_t* own, const uint8_t* rows, int64_t R, int64_t row_bytes,

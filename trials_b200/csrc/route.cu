@@ -19,6 +19,7 @@
 // That makes the order stable without sorting.
 #include "common.cuh"
 #include "launch.h"
+#include "router.cuh"
 
 namespace b200moe {
 
@@ -28,6 +29,14 @@ constexpr int kRouteBatch = 8;  // 32-id steps whose loads a warp issues togethe
 constexpr int64_t kRouteMultiMinSlots = 16384;  // flat slots from which routing uses several CTAs
 constexpr int64_t kRouteSlotsPerCta = 2048;
 constexpr int kRouteMaxCtas = 128;
+
+// Loads flat id i. COH: the ids were stored earlier in the same launch (the
+// router part of routing from logits), so they are read through L2, not the
+// read-only path.
+template <bool COH>
+__device__ __forceinline__ int load_id(const AlignArgs& a, int64_t i) {
+  return COH ? __ldcg(&a.topk_ids[i]) : __ldg(&a.topk_ids[i]);
+}
 
 // Maps a raw id to the weight index, -1 = drop. Reports bad ids when `report`.
 __device__ __forceinline__ int map_expert(const AlignArgs& a, int raw, bool report) {
@@ -72,8 +81,9 @@ __device__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
   return excl;
 }
 
-__global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs a) {
-  extern __shared__ int32_t sm[];
+// The one-CTA routing of align_kernel (all 1024 threads of the CTA call it).
+template <bool COH>
+__device__ void align_body(const AlignArgs& a, int32_t* sm) {
   __shared__ int warp_tot[32];
   const int E = a.E;
   int32_t* cnt = sm;                        // [kRouteWarps][E]
@@ -99,7 +109,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
 #pragma unroll
     for (int u = 0; u < kRouteBatch; ++u) {
       const int64_t i = i0 + u * 32 + lane;
-      ev[u] = (i < end) ? map_expert(a, __ldg(&a.topk_ids[i]), true) : -2;
+      ev[u] = (i < end) ? map_expert(a, load_id<COH>(a, i), true) : -2;
     }
 #pragma unroll
     for (int u = 0; u < kRouteBatch; ++u) {
@@ -157,7 +167,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
 #pragma unroll
     for (int u = 0; u < kRouteBatch; ++u) {
       const int64_t i = i0 + u * 32 + lane;
-      ev[u] = (i < end) ? map_expert(a, __ldg(&a.topk_ids[i]), false) : -2;
+      ev[u] = (i < end) ? map_expert(a, load_id<COH>(a, i), false) : -2;
     }
 #pragma unroll
     for (int u = 0; u < kRouteBatch; ++u) {
@@ -216,6 +226,40 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
   }
 }
 
+__global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs a) {
+  extern __shared__ int32_t sm[];
+  align_body<false>(a, sm);
+}
+
+// Router + routing of small batches in one launch: warp w of CTA c routes
+// token 32c + w and stores its ids and weights (a.topk_ids = r.out_ids); the
+// last CTA to finish (a counter, left at zero again) routes every id as
+// align_kernel does, reading the ids the other CTAs stored through L2.
+__global__ void __launch_bounds__(kRouteThreads, 1) router_align_kernel(const AlignArgs a, const RouterArgs r,
+                                                                       int64_t M, int32_t* counter) {
+  extern __shared__ int32_t sm[];
+  __shared__ int last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t = (int64_t)blockIdx.x * kRouteWarps + warp;
+  if (t < M) {
+    int id;
+    float w;
+    route_token_warp(r, t, lane, id, w);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+    if (last) {
+      atomicExch(counter, 0);
+      __threadfence();
+    }
+  }
+  __syncthreads();
+  if (!last) return;
+  align_body<true>(a, sm);
+}
+
 size_t align_smem_bytes(int E) { return (size_t)(kRouteWarps * E + 3 * E + 2) * sizeof(int32_t); }
 
 cudaError_t launch_align(const AlignArgs& a, cudaStream_t stream) {
@@ -245,6 +289,7 @@ int route_ctas(int64_t n) {
 namespace {
 
 // Per-(warp, expert) counts of ids [beg, end) cut into 32 warp segments.
+template <bool COH>
 __device__ void count_segment(const AlignArgs& a, int64_t beg, int64_t end, int32_t* cnt, bool report) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t seg = (end - beg + kRouteWarps - 1) / kRouteWarps;
@@ -255,7 +300,7 @@ __device__ void count_segment(const AlignArgs& a, int64_t beg, int64_t end, int3
 #pragma unroll
     for (int u = 0; u < kRouteBatch; ++u) {
       const int64_t i = i0 + u * 32 + lane;
-      ev[u] = (i < we) ? map_expert(a, __ldg(&a.topk_ids[i]), report) : -2;
+      ev[u] = (i < we) ? map_expert(a, load_id<COH>(a, i), report) : -2;
     }
 #pragma unroll
     for (int u = 0; u < kRouteBatch; ++u) {
@@ -266,13 +311,21 @@ __device__ void count_segment(const AlignArgs& a, int64_t beg, int64_t end, int3
   }
 }
 
-__device__ __forceinline__ void cta_segment(int64_t n, int64_t& beg, int64_t& end) {
-  const int64_t S = (n + gridDim.x - 1) / gridDim.x;
+// CTA segments of the flat ids, whole tokens each when a.seg_align = topk
+// (routing from logits: a CTA routes the tokens whose ids it then counts).
+__device__ __forceinline__ void cta_segment(const AlignArgs& a, int64_t& beg, int64_t& end) {
+  const int64_t n = a.n;
+  const int64_t al = a.seg_align > 1 ? a.seg_align : 1;
+  const int64_t S = ((n + gridDim.x - 1) / gridDim.x + al - 1) / al * al;
   beg = (int64_t)blockIdx.x * S < n ? (int64_t)blockIdx.x * S : n;
   end = beg + S < n ? beg + S : n;
 }
 
-__global__ void __launch_bounds__(kRouteThreads, 1) route_count_kernel(const AlignArgs a, int32_t* scratch) {
+// ROUTER: the CTA first routes the tokens of its segment (a.seg_align = topk,
+// a.topk_ids = r.out_ids) and counts the ids it just stored.
+template <bool ROUTER>
+__global__ void __launch_bounds__(kRouteThreads, 1) route_count_kernel(const AlignArgs a, int32_t* scratch,
+                                                                      const RouterArgs r) {
   extern __shared__ int32_t sm[];
   const int E = a.E;
   int32_t* cnt = sm;  // [kRouteWarps][E]
@@ -282,10 +335,18 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_count_kernel(const Ali
          i += (int64_t)gridDim.x * kRouteThreads)
       a.chunk_ready[i] = 0;
   for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) cnt[i] = 0;
-  __syncthreads();
   int64_t beg, end;
-  cta_segment(a.n, beg, end);
-  count_segment(a, beg, end, cnt, true);
+  cta_segment(a, beg, end);
+  if (ROUTER) {
+    const int lane = tid & 31;
+    for (int64_t t = beg / r.topk + (tid >> 5); t < end / r.topk; t += kRouteWarps) {
+      int id;
+      float w;
+      route_token_warp(r, t, lane, id, w);
+    }
+  }
+  __syncthreads();
+  count_segment<ROUTER>(a, beg, end, cnt, true);
   __syncthreads();
   for (int e = tid; e < E; e += kRouteThreads) {
     int t = 0;
@@ -361,8 +422,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_scatter_kernel(const A
   for (int64_t i = total_rows + gtid; i < a.sorted_cap; i += gstride) a.sorted_ids[i] = a.sentinel;
 
   int64_t beg, end;
-  cta_segment(a.n, beg, end);
-  count_segment(a, beg, end, cnt, false);
+  cta_segment(a, beg, end);
+  count_segment<false>(a, beg, end, cnt, false);
   __syncthreads();
   if (tid < E) {
     int t = 0;
@@ -450,19 +511,48 @@ int64_t route_scratch_ints(int64_t n, int E) {
   return C > 1 ? (int64_t)C * E : 0;
 }
 
-cudaError_t launch_route(const AlignArgs& a, int32_t* scratch, int64_t scratch_ints, cudaStream_t stream) {
-  const int C = route_ctas(a.n);
-  if (C == 1 || !scratch || scratch_ints < (int64_t)C * a.E) return launch_align(a, stream);
+namespace {
+
+template <bool ROUTER>
+cudaError_t launch_route_multi(const AlignArgs& a, const RouterArgs& r, int C, int32_t* scratch,
+                               cudaStream_t stream) {
   const size_t smem1 = (size_t)kRouteWarps * a.E * sizeof(int32_t);
   const size_t smem2 = (size_t)(kRouteWarps * a.E + 5 * a.E + 2) * sizeof(int32_t);
-  cudaError_t err = cudaFuncSetAttribute(route_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+  cudaError_t err =
+      cudaFuncSetAttribute(route_count_kernel<ROUTER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
   if (err == cudaSuccess)
     err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
   if (err != cudaSuccess) return err;
-  route_count_kernel<<<C, kRouteThreads, smem1, stream>>>(a, scratch);
+  route_count_kernel<ROUTER><<<C, kRouteThreads, smem1, stream>>>(a, scratch, r);
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   route_scatter_kernel<<<C, kRouteThreads, smem2, stream>>>(a, scratch);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_route(const AlignArgs& a, int32_t* scratch, int64_t scratch_ints, cudaStream_t stream) {
+  const int C = route_ctas(a.n);
+  if (C == 1 || !scratch || scratch_ints < (int64_t)C * a.E) return launch_align(a, stream);
+  return launch_route_multi<false>(a, RouterArgs{}, C, scratch, stream);
+}
+
+int64_t route_logits_scratch_ints(int64_t n, int E) { return kRouteLogitsCounterInts + route_scratch_ints(n, E); }
+
+cudaError_t launch_route_logits(const AlignArgs& a_in, const RouterArgs& r, int64_t M, int32_t* counter,
+                                int32_t* counts, cudaStream_t stream) {
+  AlignArgs a = a_in;
+  a.topk_ids = r.out_ids;
+  a.seg_align = r.topk;
+  const int C = route_ctas(a.n);
+  if (C > 1) return launch_route_multi<true>(a, r, C, counts, stream);
+  const size_t smem = align_smem_bytes(a.E);
+  cudaError_t err =
+      cudaFuncSetAttribute(router_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  const int64_t ctas = M > 0 ? (M + kRouteWarps - 1) / kRouteWarps : 1;
+  router_align_kernel<<<(unsigned)ctas, kRouteThreads, smem, stream>>>(a, r, M, counter);
   return cudaGetLastError();
 }
 

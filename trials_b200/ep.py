@@ -33,13 +33,111 @@ experts elsewhere (:660-668).
 from __future__ import annotations
 
 import ctypes
+from dataclasses import dataclass
 from typing import Optional
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
 from . import _lib
 from .moe import FP8, _ptr, _stream
+
+
+@dataclass
+class Placement:
+    """Where the experts' weights live: G ranks of `slots` physical experts;
+    physical slot p = rank * slots + local index holds logical expert
+    phys_to_logical[p]. A logical expert may have several replicas (EPLB,
+    hot-expert replication); every logical expert has at least one."""
+    num_experts: int
+    G: int
+    slots: int
+    phys_to_logical: np.ndarray
+
+    def __post_init__(self):
+        p2l = np.asarray(self.phys_to_logical, dtype=np.int64)
+        if p2l.shape != (self.G * self.slots,):
+            raise ValueError("phys_to_logical must hold G * slots entries")
+        if p2l.min() < 0 or p2l.max() >= self.num_experts:
+            raise ValueError("phys_to_logical names an expert outside [0, num_experts)")
+        if len(np.unique(p2l)) != self.num_experts:
+            raise ValueError("every logical expert needs at least one physical slot")
+        self.phys_to_logical = p2l
+
+    @staticmethod
+    def identity(num_experts: int, G: int) -> "Placement":
+        if num_experts % G:
+            raise ValueError("num_experts must be a multiple of the world size")
+        return Placement(num_experts, G, num_experts // G, np.arange(num_experts))
+
+    def replicas(self, e: int) -> np.ndarray:
+        return np.nonzero(self.phys_to_logical == e)[0]
+
+    @property
+    def max_replicas(self) -> int:
+        return int(np.bincount(self.phys_to_logical, minlength=self.num_experts).max())
+
+    def table(self) -> np.ndarray:
+        """(E, 1 + max_replicas) int32 rows [n, p_0, .., p_{n-1}, -1..] of the
+        C ABI (b200moe_ep_dispatch's `replicas`)."""
+        m = self.max_replicas
+        t = np.full((self.num_experts, 1 + m), -1, dtype=np.int32)
+        for e in range(self.num_experts):
+            r = self.replicas(e)
+            t[e, 0] = len(r)
+            t[e, 1:1 + len(r)] = r
+        return t
+
+    def local_experts(self, rank: int) -> np.ndarray:
+        """Logical expert of each of rank's slots, in slot order."""
+        return self.phys_to_logical[rank * self.slots:(rank + 1) * self.slots]
+
+    def is_identity(self) -> bool:
+        return self.slots * self.G == self.num_experts and \
+            bool((self.phys_to_logical == np.arange(self.num_experts)).all())
+
+
+def eplb_placement(expert_load, G: int, slots_per_rank: int) -> Placement:
+    """Hot-expert replication and balanced packing (the EPLB the reference
+    plans to enable, moe_placement_glm52_mi355x.md:98-104; the algorithm is
+    DeepSeek's published EPLB: replicate, then pack).
+
+    expert_load (E,): tokens (or any load measure) per logical expert, e.g.
+    counted from recent batches. The G * slots_per_rank - E spare slots go,
+    one at a time, to the expert with the largest load per replica (at most G
+    replicas each). The replicas, heaviest first (load / replicas), are then
+    packed onto the rank with the least load that has a free slot and does not
+    hold that expert yet. Within a rank, slots are in ascending expert order."""
+    load = np.asarray(expert_load, dtype=np.float64)
+    E = len(load)
+    total = G * slots_per_rank
+    if total < E:
+        raise ValueError("G * slots_per_rank must be at least the number of experts")
+    nrep = np.ones(E, dtype=np.int64)
+    for _ in range(total - E):
+        ratio = np.where(nrep < G, load / nrep, -np.inf)
+        if not np.isfinite(ratio).any():
+            ratio = load / nrep
+        nrep[int(np.argmax(ratio))] += 1
+    items = sorted(((load[e] / nrep[e], e) for e in range(E) for _ in range(nrep[e])), key=lambda x: (-x[0], x[1]))
+    rank_load = np.zeros(G)
+    held = [[] for _ in range(G)]
+    for w, e in items:
+        free = [r for r in range(G) if len(held[r]) < slots_per_rank]
+        fresh = [r for r in free if e not in held[r]]
+        cand = fresh or free
+        r = min(cand, key=lambda r: (rank_load[r], r))
+        held[r].append(e)
+        rank_load[r] += w
+    p2l = np.concatenate([np.sort(np.asarray(h, dtype=np.int64)) for h in held])
+    return Placement(E, G, slots_per_rank, p2l)
+
+
+def place_experts(w: torch.Tensor, placement: Placement, rank: int) -> torch.Tensor:
+    """The (slots, ...) weights of rank `rank` from the (E, ...) weights of every expert."""
+    idx = torch.as_tensor(placement.local_experts(rank), device=w.device)
+    return w.index_select(0, idx).contiguous()
 
 
 class CudaEPOps:
@@ -53,11 +151,16 @@ class CudaEPOps:
         _lib.check(_lib.lib().b200moe_quant_1x128(_ptr(hidden), M, H, H, _ptr(q), H, _ptr(s), H // 128, 1,
                                                   _stream(hidden.device)), "ep quant")
 
-    def dispatch(self, q, s, topk_ids, topk_weights, num_experts, G, rows_per_rank, send, pos, tok_of, counts, err):
+    def dispatch(self, q, s, topk_ids, topk_weights, num_experts, G, rows_per_rank, send, pos, tok_of, counts, err,
+                 rank=0, placement=None):
+        """placement: None (experts split evenly) or (table (E, 1+max_rep) int32
+        device tensor, Placement)."""
         M, H = q.shape
         topk = topk_ids.shape[1]
+        table, pl = placement if placement is not None else (None, None)
         _lib.check(_lib.lib().b200moe_ep_dispatch(
-            _ptr(q), _ptr(s), _ptr(topk_ids), _ptr(topk_weights), M, H, topk, num_experts, G, rows_per_rank,
+            _ptr(q), _ptr(s), _ptr(topk_ids), _ptr(topk_weights), M, H, topk, num_experts, G, rank, _ptr(table),
+            pl.max_replicas if pl else 0, pl.slots if pl else 0, rows_per_rank,
             _ptr(send), _ptr(pos), _ptr(tok_of), _ptr(counts), _ptr(err), _stream(q.device)), "ep_dispatch")
 
     def workspace_bytes(self, R, H, I, E_local, topk) -> int:
@@ -135,16 +238,29 @@ class ExpertParallelMoE:
     None picks "peer" for the CUDA ops and "nccl" otherwise."""
 
     def __init__(self, w13, w13_scale, w2, w2_scale, num_experts: int, rows_per_rank: int,
-                 group: Optional[dist.ProcessGroup] = None, ops=None, device=None, exchange: Optional[str] = None):
+                 group: Optional[dist.ProcessGroup] = None, ops=None, device=None, exchange: Optional[str] = None,
+                 placement: Optional[Placement] = None):
+        """placement: where the experts live (eplb_placement for hot-expert
+        replication); None splits them evenly (num_experts / world_size per
+        rank). w13 ... w2_scale are this rank's slots (place_experts)."""
         self.group = group
         self.G = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        if num_experts % self.G:
-            raise ValueError("num_experts must be a multiple of the world size")
         self.E = num_experts
         self.E_local, self.I2, self.H = w13.shape
-        if self.E_local != num_experts // self.G:
-            raise ValueError("w13 must hold num_experts / world_size experts")
+        if placement is not None and placement.is_identity():
+            placement = None
+        if placement is None:
+            if num_experts % self.G:
+                raise ValueError("num_experts must be a multiple of the world size")
+            if self.E_local != num_experts // self.G:
+                raise ValueError("w13 must hold num_experts / world_size experts")
+        else:
+            if placement.G != self.G or placement.num_experts != num_experts:
+                raise ValueError("placement is for another world size or expert count")
+            if self.E_local != placement.slots:
+                raise ValueError("w13 must hold the placement's slots per rank")
+        self.placement = placement
         self.I = self.I2 // 2
         self.w13, self.w13_scale, self.w2, self.w2_scale = w13, w13_scale.contiguous(), w2, w2_scale.contiguous()
         self.cap = int(rows_per_rank)
@@ -160,6 +276,9 @@ class ExpertParallelMoE:
         self.peer = None
         self.epoch = 0
         self._topk = None
+        self._place = None
+        if placement is not None:
+            self._place = (torch.as_tensor(placement.table(), device=self.device), placement)
 
     def _buffers(self, topk: int):
         if self._topk == topk:
@@ -217,7 +336,7 @@ class ExpertParallelMoE:
         rec(0)
         self.ops.quant(hidden.contiguous(), q, s)
         self.ops.dispatch(q, s, ids, tw, self.E, self.G, self.cap, self.send, self.pos[: M * self.G],
-                          self.tok_of, self.counts, self.err)
+                          self.tok_of, self.counts, self.err, rank=self.rank, placement=self._place)
         rec(1)
         self._all_to_all(self.recv, self.send)
         rec(2)
@@ -243,9 +362,10 @@ class ExpertParallelMoE:
         bases, own = _ptr(self.peer.bases), self.peer.own
         rec(0)
         # the pack kernel quantises each token row on its way to the destinations
+        table, pl = self._place if self._place is not None else (None, None)
         _lib.check(lib.b200moe_ep_dispatch_peer(
-            _ptr(hidden.contiguous()), None, None, _ptr(ids), _ptr(tw), M, H, topk, self.E, G, self.rank, cap, bases,
-            own, self.epoch,
+            _ptr(hidden.contiguous()), None, None, _ptr(ids), _ptr(tw), M, H, topk, self.E, G, self.rank, _ptr(table),
+            pl.max_replicas if pl else 0, pl.slots if pl else 0, cap, bases, own, self.epoch,
             _ptr(self.pos[: M * G]), _ptr(self.tok_of), _ptr(self.counts), _ptr(self.err), st), "ep_dispatch_peer")
         rec(1)
         rec(2)

@@ -50,8 +50,9 @@ def _require_cuda(*tensors: torch.Tensor) -> torch.device:
 
 
 class _Workspaces:
-    """Grow-only per-(device, stream) workspace buffers. The first 4 bytes of
-    each are the device error word, zeroed at allocation."""
+    """Grow-only per-(device, stream) workspace buffers. Their first 256 bytes
+    are zeroed at allocation: the device error word (int 0) and the router's
+    CTA counter of b200moe_layer_logits (int 1, left at zero by every call)."""
 
     def __init__(self):
         self._bufs = {}
@@ -316,6 +317,49 @@ def fused_moe(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, t
                           int(expert_mask.numel()), a1_scale=a1_scale)
     return _run_layer(hidden_states, w1, w1_scale, w2, w2_scale, topk_weight, topk_ids, None, w1.shape[0],
                       a1_scale=a1_scale)
+
+
+def moe_layer_from_logits(hidden_states: torch.Tensor, router_logits: torch.Tensor, w13_fp8: torch.Tensor,
+                          w13_scale: torch.Tensor, w2_fp8: torch.Tensor, w2_scale: torch.Tensor, top_k: int,
+                          scoring_func: str = "sigmoid", correction_bias: Optional[torch.Tensor] = None,
+                          renormalize: bool = True, routed_scaling_factor: float = 1.0,
+                          expert_map: Optional[torch.Tensor] = None):
+    """Router + layer: select_experts(router_logits, ...) followed by
+    moe_decode_megakernel_full, with the router inside routing's first launch
+    (b200moe_layer_logits). Returns (out (M, H) bf16, topk_weights (M, k) f32,
+    topk_ids (M, k) int32), bit-identical to the two calls. expert_map
+    (num_experts,) maps a global id to a local weight index or -1 (the weights
+    then hold only the mapped experts)."""
+    dev = _require_cuda(hidden_states, router_logits, w13_fp8, w2_fp8)
+    if hidden_states.dtype != torch.bfloat16:
+        raise NotImplementedError("moe_layer_from_logits takes bf16 hidden_states")
+    if router_logits.dtype not in (torch.float32, torch.bfloat16):
+        raise NotImplementedError("router logits must be float32 or bfloat16")
+    scoring = {"softmax": 0, "sigmoid": 1}.get(scoring_func)
+    if scoring is None:
+        raise NotImplementedError(f"scoring_func {scoring_func!r}")
+    M, E_router = router_logits.shape
+    tw = torch.empty(M, top_k, dtype=torch.float32, device=dev)
+    ids = torch.empty(M, top_k, dtype=torch.int32, device=dev)
+    _, _, H, I, E_w = _check_layer_args(hidden_states, w13_fp8, w13_scale, w2_fp8, w2_scale, tw, ids)
+    out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    if M == 0:
+        return out, tw, ids
+    if expert_map is not None:
+        expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
+    elif E_w != E_router:
+        raise ValueError("without expert_map the weights must hold every routed expert")
+    bias = None if correction_bias is None else correction_bias.to(device=dev, dtype=torch.float32).contiguous()
+    logits = router_logits.contiguous()
+    L = _lib.lib()
+    ws = _workspaces.get(dev, L.b200moe_layer_workspace_size(M, H, I, E_router, E_w, top_k))
+    _lib.check(L.b200moe_layer_logits(_ptr(hidden_states.contiguous()), M, H, I, E_router, top_k, _ptr(logits),
+                                      int(logits.dtype == torch.bfloat16), scoring, _ptr(bias), int(renormalize),
+                                      float(routed_scaling_factor), _ptr(w13_fp8), _ptr(w13_scale.contiguous()),
+                                      _ptr(w2_fp8), _ptr(w2_scale.contiguous()), _ptr(expert_map), E_w, _ptr(tw),
+                                      _ptr(ids), _ptr(out), _ptr(ws), ws.numel(), _stream(dev)),
+               "b200moe_layer_logits")
+    return out, tw, ids
 
 
 def moe_layer_ep_local(hidden_states, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids, expert_map,

@@ -80,6 +80,41 @@ def route(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, expert_map
     return r
 
 
+def route_logits(logits: torch.Tensor, top_k: int, tile_tokens: int, scoring_func: str = "sigmoid",
+                 correction_bias: Optional[torch.Tensor] = None, renormalize: bool = True,
+                 routed_scaling_factor: float = 1.0, expert_map: Optional[torch.Tensor] = None,
+                 num_local_experts: Optional[int] = None, err: Optional[torch.Tensor] = None):
+    """Router + routing (b200moe_route_logits) -> (Routing, topk_weights (M, k)
+    f32, topk_ids (M, k) int32), equal to select_experts followed by route()."""
+    dev = _require_cuda(logits)
+    logits = logits.contiguous()
+    M, E_router = logits.shape
+    E = num_local_experts if expert_map is not None else E_router
+    L = _lib.lib()
+    numel = M * top_k
+    rows_cap = L.b200moe_route_capacity_rows(numel, E)
+    chunks_cap = L.b200moe_route_capacity_chunks(numel, E, tile_tokens)
+    z = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=dev)  # noqa: E731
+    r = Routing(tile_tokens, rows_cap, chunks_cap, z(rows_cap), z(chunks_cap), z(chunks_cap), z(chunks_cap),
+                torch.zeros(2, dtype=torch.int32, device=dev),
+                err if err is not None else torch.zeros(1, dtype=torch.int32, device=dev), z(chunks_cap + 2), z(numel))
+    tw = torch.empty(M, top_k, dtype=torch.float32, device=dev)
+    ids = torch.empty(M, top_k, dtype=torch.int32, device=dev)
+    if expert_map is not None:
+        expert_map = expert_map.to(device=dev, dtype=torch.int32).contiguous()
+    ns = L.b200moe_route_logits_scratch_ints(numel, E)
+    scratch = torch.zeros(ns, dtype=torch.int32, device=dev)
+    bias = None if correction_bias is None else correction_bias.to(device=dev, dtype=torch.float32).contiguous()
+    scoring = {"softmax": 0, "sigmoid": 1}[scoring_func]
+    _lib.check(L.b200moe_route_logits(_ptr(logits), int(logits.dtype == torch.bfloat16), M, E_router, top_k, scoring,
+                                      _ptr(bias), int(renormalize), float(routed_scaling_factor), _ptr(tw), _ptr(ids),
+                                      _ptr(expert_map), E, tile_tokens, _ptr(r.sorted_ids), rows_cap,
+                                      _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows), chunks_cap,
+                                      _ptr(r.n_chunks), _ptr(r.num_rows), _ptr(r.slot_pos), _ptr(r.chunk_ready),
+                                      _ptr(scratch), ns, _ptr(r.err), _stream(dev)), "route_logits")
+    return r, tw, ids
+
+
 def gather_quant(hidden: torch.Tensor, topk: int, r: Routing):
     """-> (a_q (rows_cap, H) e4m3, a_sT (H/128, ld) f32) in sorted row order."""
     dev = _require_cuda(hidden)
@@ -235,7 +270,10 @@ class LayerPipeline:
 
     def __init__(self, M: int, H: int, I: int, num_experts: int, topk: int, device, tile_tokens: int = 0,
                  expert_map: Optional[torch.Tensor] = None, num_local_experts: Optional[int] = None,
-                 split: bool = False, one_launch: Optional[bool] = None):
+                 split: bool = False, one_launch: Optional[bool] = None, router: Optional[dict] = None):
+        """router: {"scoring_func", "correction_bias", "renormalize",
+        "routed_scaling_factor"} to run the layer from router logits
+        (run_from_logits: the router inside routing's first launch)."""
         self.M, self.H, self.I, self.topk = M, H, I, topk
         self.num_experts = num_experts
         self.E = num_local_experts if expert_map is not None else num_experts
@@ -270,13 +308,47 @@ class LayerPipeline:
         self.pair = torch.zeros(max(self.rows_cap if self.sorted_rows else numel, 1), H, dtype=torch.bfloat16,
                                 device=device)
         self.out = torch.zeros(M, H, dtype=torch.bfloat16, device=device)
+        self.router = None
+        if router is not None:
+            r = dict(router)
+            bias = r.get("correction_bias")
+            self.router = (({"softmax": 0, "sigmoid": 1}[r.get("scoring_func", "sigmoid")]),
+                           None if bias is None else bias.to(device=device, dtype=torch.float32).contiguous(),
+                           int(r.get("renormalize", True)), float(r.get("routed_scaling_factor", 1.0)))
+            self.topk_weights = torch.zeros(M, topk, dtype=torch.float32, device=device)
+            self.topk_ids = torch.zeros(M, topk, dtype=torch.int32, device=device)
+            self.lscratch_ints = L.b200moe_route_logits_scratch_ints(numel, self.E)
+            self.lscratch = z(self.lscratch_ints)  # zeroed: its first int is the router's CTA counter
+
+    def run_from_logits(self, hidden, logits, w13, w13_scale, w2, w2_scale, events=None, grid_ctas: int = 0):
+        """The layer from router logits: b200moe_route_logits (router + routing),
+        then the same launches as run(). The selected ids and weights are left
+        in self.topk_ids / self.topk_weights."""
+        if self.router is None:
+            raise ValueError("LayerPipeline was built without a router")
+        L = _lib.lib()
+        st = _stream(self.device)
+        ev = events or [None] * (len(self.stages) + 1)
+        rec = lambda i: ev[i].record() if ev[i] is not None else None  # noqa: E731
+        scoring, bias, renorm, scale = self.router
+        cnt = _ptr(self.counts)
+        rec(0)
+        _lib.check(L.b200moe_route_logits(_ptr(logits), int(logits.dtype == torch.bfloat16), self.M, self.num_experts,
+                                          self.topk, scoring, _ptr(bias), renorm, scale, _ptr(self.topk_weights),
+                                          _ptr(self.topk_ids), _ptr(self.expert_map), self.E, self.tile,
+                                          _ptr(self.sorted_ids), self.rows_cap, _ptr(self.ce), _ptr(self.cr0),
+                                          _ptr(self.crows), self.chunks_cap, cnt, cnt + 4, _ptr(self.slot_pos),
+                                          _ptr(self.ready), _ptr(self.lscratch), self.lscratch_ints, _ptr(self.err),
+                                          st), "route_logits")
+        rec(1)
+        return self._after_route(hidden, self.topk_weights, w13, w13_scale, w2, w2_scale, rec, grid_ctas)
 
     def run(self, hidden, topk_ids, topk_weights, w13, w13_scale, w2, w2_scale, events=None, grid_ctas: int = 0):
         L = _lib.lib()
         st = _stream(self.device)
         ev = events or [None] * (len(self.stages) + 1)
         rec = lambda i: ev[i].record() if ev[i] is not None else None  # noqa: E731
-        M, H, I, topk, E = self.M, self.H, self.I, self.topk, self.E
+        M, topk, E = self.M, self.topk, self.E
         cnt = _ptr(self.counts)
         rows = cnt + 4
         rec(0)
@@ -286,6 +358,13 @@ class LayerPipeline:
                                    _ptr(self.ready), _ptr(self.rscratch), self.rscratch_ints, _ptr(self.err), st),
                    "route")
         rec(1)
+        return self._after_route(hidden, topk_weights, w13, w13_scale, w2, w2_scale, rec, grid_ctas)
+
+    def _after_route(self, hidden, topk_weights, w13, w13_scale, w2, w2_scale, rec, grid_ctas):
+        L = _lib.lib()
+        st = _stream(self.device)
+        M, H, I, topk, E = self.M, self.H, self.I, self.topk, self.E
+        cnt = _ptr(self.counts)
         if self.one_launch:
             _lib.check(L.b200moe_experts_fused(_ptr(hidden), M, topk, _ptr(self.slot_pos), _ptr(self.a1), _ptr(self.a1s),
                                                self.ld, self.rows_cap, _ptr(w13), _ptr(w13_scale), _ptr(w2),
