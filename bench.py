@@ -75,6 +75,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-sweep", action="store_true", help="N=1: skip the sweep record")
     ap.add_argument("--no-config5", action="store_true", help="N>1: skip the config5 record")
     ap.add_argument("--no-parity", action="store_true", help="N>1: skip the parity record")
+    ap.add_argument("--no-eplb", action="store_true", help="N>1: skip the hot-expert replication record")
     return ap.parse_args(argv)
 
 
@@ -400,6 +401,7 @@ CONFIG5_TOKENS = 8192  # expert-parallel configuration: tokens in total, split e
 def run_ep(args, shape, config):
     """N > 1: expert-parallel layer, E/N experts and M tokens per GPU, plus the
     parity and config5 records."""
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -419,6 +421,19 @@ def run_ep(args, shape, config):
     ref = full(hidden, tw, ids) if check else None
     ref5 = full(h5, tw5, ids5) if (check and run5) else None
     shards = [ep.shard_experts(t, rank, ws) for t in (L.w13, L.w13_scale, L.w2, L.w2_scale)]
+    # config5 with 16 hot experts: the even split against hot-expert replication
+    # (eplb_placement from the load of this batch's ids over all ranks; in
+    # service the load would come from recent batches).
+    run_hot = run5 and not args.no_eplb
+    if run_hot:
+        hh, htw, hids = layer_inputs(shape, M5, 16, args.seed + 5000 + rank, dev)
+        parts = [torch.empty_like(hids) for _ in range(ws)]
+        dist.all_gather(parts, hids)
+        load = torch.bincount(torch.cat(parts).reshape(-1).long(), minlength=shape.E).cpu().numpy()
+        spare = max(1, shape.E // (4 * ws))
+        placement = ep.eplb_placement(load, ws, shape.E // ws + spare)
+        placed = [ep.place_experts(t, placement, rank) for t in (L.w13, L.w13_scale, L.w2, L.w2_scale)]
+        refh = full(hh, htw, hids) if check else None
     del L, full
     torch.cuda.empty_cache()
     model = ep.ExpertParallelMoE(*shards, num_experts=shape.E, rows_per_rank=shape.M, exchange=args.exchange)
@@ -547,6 +562,25 @@ def run_ep(args, shape, config):
         errs |= model5.device_errors()
         model5.close()
 
+    hot = None
+    if run_hot:
+        hot = {"workload": f"glm_ep_M{CONFIG5_TOKENS}_total_hot16", "tokens_total": M5 * ws, "tokens_per_gpu": M5,
+               "router": "+2.0 on the logits of experts 0..15", "steps": args.sweep_steps, "warmup": 3}
+        for name, w, pl in (("even_split", shards, None), ("eplb", placed, placement)):
+            m = ep.ExpertParallelMoE(*w, num_experts=shape.E, rows_per_rank=M5, exchange=args.exchange, placement=pl)
+            msh, sth = timed(m, hh, htw, hids, args.sweep_steps, 3, "config5")
+            rec = {"ms_per_step": msh, "value": M5 * ws / (msh / 1e3), "unit": "tokens/s", "stage_ms": sth}
+            if pl is not None:
+                rec.update(slots_per_rank=pl.slots, max_replicas=pl.max_replicas,
+                           replicated_experts=int((np.bincount(pl.phys_to_logical, minlength=shape.E) > 1).sum()))
+            if check:
+                out = m(hh, htw, hids)
+                rel = max_over_ranks(rel_l2(out, refh))
+                rec["parity"] = {"rel_l2_max_over_ranks": rel, "tol": 5e-3, "ok": rel <= 5e-3}
+            errs |= m.device_errors()
+            m.close()
+            hot[name] = rec
+
     clk = clocks.stop()
     worst_active = int(max_over_ranks(local_active))
     if rank == 0:
@@ -572,6 +606,8 @@ def run_ep(args, shape, config):
             line["parity"] = par
         if c5 is not None:
             line["config5"] = c5
+        if hot is not None:
+            line["config5_hot16"] = hot
         if errs:
             line["device_errors"] = errs
         print(json.dumps(line), flush=True)

@@ -115,32 +115,60 @@ def test_prequantised_input_is_bit_identical(cuda_device):
                                        g["topk_ids"], a1_scale=torch.ones(q.shape[0], device=cuda_device))
 
 
-def _all_to_all_form(G, cap, toks, W, dev):
+def _rank_weights(W, G, placement=None):
+    """Each rank's (w13, w13_scale, w2, w2_scale): an even split, or the
+    placement's slots."""
+    keys = ["w13", "w13_scale", "w2", "w2_scale"]
+    if placement is None:
+        per = SHAPE.E // G
+        return [[W[k][d * per:(d + 1) * per].contiguous() for k in keys] for d in range(G)]
+    return [[ep.place_experts(W[k], placement, d) for k in keys] for d in range(G)]
+
+
+def _all_to_all_form(G, cap, toks, W, dev, placement=None, check_bytes=False):
     """Outputs of the all-to-all form (dispatch buffers re-sliced in place of
-    the exchange) for G simulated ranks' tokens."""
+    the exchange) for G simulated ranks' tokens; with check_bytes, every
+    rank's dispatch buffer is compared with the oracle's."""
     ops = ep.CudaEPOps()
-    H, I, topk, per = SHAPE.H, SHAPE.I, SHAPE.topk, SHAPE.E // G
+    H, I, topk = SHAPE.H, SHAPE.I, SHAPE.topk
     rb = ops.row_bytes(H, topk)
+    table = None if placement is None else torch.as_tensor(placement.table(), device=dev)
+    E_local = SHAPE.E // G if placement is None else placement.slots
     sends, poss = [], []
-    for hidden, tw, ids in toks:
+    for r, (hidden, tw, ids) in enumerate(toks):
         M = hidden.shape[0]
         q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
         s = torch.empty(M, H // 128, dtype=torch.float32, device=dev)
         ops.quant(hidden, q, s)
         send = torch.zeros(G * cap * rb, dtype=torch.uint8, device=dev)
         pos = torch.empty(M * G, dtype=torch.int32, device=dev)
+        counts = torch.empty(G, dtype=torch.int32, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        pl_arg = None if placement is None else (table, placement)
         ops.dispatch(q, s, ids, tw, SHAPE.E, G, cap, send, pos, torch.empty(G * cap, dtype=torch.int32, device=dev),
-                     torch.empty(G, dtype=torch.int32, device=dev), torch.zeros(1, dtype=torch.int32, device=dev))
+                     counts, err, rank=r, placement=pl_arg)
+        if check_bytes:
+            o_send = torch.zeros(G * cap * rb, dtype=torch.uint8)
+            o_pos = torch.empty(M * G, dtype=torch.int32)
+            o_cnt = torch.empty(G, dtype=torch.int32)
+            ep_oracle.OracleEPOps().dispatch(q.cpu(), s.cpu(), ids.cpu(), tw.cpu(), SHAPE.E, G, cap, o_send, o_pos,
+                                             torch.empty(G * cap, dtype=torch.int32), o_cnt, None, rank=r,
+                                             placement=None if placement is None else (table.cpu(), placement))
+            assert torch.equal(counts.cpu(), o_cnt) and torch.equal(pos.cpu(), o_pos)
+            got, ref = send.cpu().view(G * cap, rb), o_send.view(G * cap, rb)
+            for d in range(G):
+                n = int(o_cnt[d])
+                assert torch.equal(got[d * cap:d * cap + n], ref[d * cap:d * cap + n]), (r, d)
+            assert moe.read_device_error(err) == 0
         sends.append(send.view(G, cap * rb))
         poss.append(pos)
     local = []
+    weights = _rank_weights(W, G, placement)
     for d in range(G):
         recv = torch.cat([sends[r][d] for r in range(G)]).contiguous()
         out_d = torch.empty(G * cap, H, dtype=torch.bfloat16, device=dev)
-        ws = torch.zeros(max(ops.workspace_bytes(G * cap, H, I, per, topk), 256), dtype=torch.uint8, device=dev)
-        sl = slice(d * per, (d + 1) * per)
-        ops.layer_packed(recv, G * cap, H, I, per, topk, W["w13"][sl].contiguous(), W["w13_scale"][sl].contiguous(),
-                         W["w2"][sl].contiguous(), W["w2_scale"][sl].contiguous(), out_d, ws, num_ranks=G)
+        ws = torch.zeros(max(ops.workspace_bytes(G * cap, H, I, E_local, topk), 256), dtype=torch.uint8, device=dev)
+        ops.layer_packed(recv, G * cap, H, I, E_local, topk, *weights[d], out_d, ws, num_ranks=G)
         local.append(out_d.view(G, cap, H))
     outs = []
     for r, (hidden, _, _) in enumerate(toks):
@@ -302,3 +330,94 @@ def test_peer_waits_end_with_timeout_when_a_rank_never_dispatches(cuda_device):
     # the context still runs work
     x = torch.arange(1024, device=dev, dtype=torch.float32)
     assert float(x.sum().item()) == 1023 * 1024 / 2
+
+
+def _skewed_tokens(G, cap, dev, hot=4, seed=300):
+    toks = []
+    for r in range(G):
+        g = torch.Generator().manual_seed(seed + r)
+        logits = torch.randn(cap - 2 * r, SHAPE.E, generator=g)
+        logits[:, :hot] += 2.0
+        tw, ids = synth.make_router(logits, SHAPE.topk, SHAPE.scoring)
+        hidden = torch.randn(cap - 2 * r, SHAPE.H, generator=g).to(torch.bfloat16)
+        toks.append((hidden.to(dev), tw.to(dev), ids.to(dev)))
+    return toks
+
+
+def _peer_call(lib, G, cap, bases, table_ptr, ws, toks, weights, epoch, dev, placement=None):
+    """One call of the peer exchange for G simulated ranks in one process:
+    every dispatch, then every layer, then every combine (no wait depends on a
+    later launch)."""
+    from trials_b200 import _lib
+
+    H, I, topk = SHAPE.H, SHAPE.I, SHAPE.topk
+    st = torch.cuda.current_stream(dev).cuda_stream
+    ptable = None if placement is None else torch.as_tensor(placement.table(), device=dev)
+    E_local = SHAPE.E // G if placement is None else placement.slots
+    state = []
+    for r, (hidden, tw, ids) in enumerate(toks):
+        M = hidden.shape[0]
+        pos = torch.empty(M * G, dtype=torch.int32, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        _lib.check(lib.b200moe_ep_dispatch_peer(
+            hidden.data_ptr(), None, None, ids.data_ptr(), tw.data_ptr(), M, H, topk, SHAPE.E, G, r,
+            None if ptable is None else ptable.data_ptr(), 0 if placement is None else placement.max_replicas,
+            0 if placement is None else placement.slots, cap, table_ptr, bases[r], epoch, pos.data_ptr(),
+            torch.empty(G * cap, dtype=torch.int32, device=dev).data_ptr(),
+            torch.empty(G, dtype=torch.int32, device=dev).data_ptr(), err.data_ptr(), st), "dispatch_peer")
+        state.append((pos, err))
+    for d in range(G):
+        w13, w13s, w2, w2s = weights[d]
+        _lib.check(lib.b200moe_layer_packed_peer(bases[d], table_ptr, G, d, cap, epoch, H, I, E_local, topk,
+                                                 w13.data_ptr(), w13s.data_ptr(), w2.data_ptr(), w2s.data_ptr(),
+                                                 ws[d].data_ptr(), ws[d].numel(), st), "layer_packed_peer")
+    outs = []
+    for r, (hidden, _, _) in enumerate(toks):
+        out = torch.empty(hidden.shape[0], H, dtype=torch.bfloat16, device=dev)
+        pos, err = state[r]
+        _lib.check(lib.b200moe_ep_combine_peer(bases[r], pos.data_ptr(), hidden.shape[0], H, topk, G, cap, epoch,
+                                               out.data_ptr(), err.data_ptr(), st), "combine_peer")
+        outs.append((out, err))
+    torch.cuda.synchronize(dev)
+    for r in range(G):
+        assert moe.read_device_error(outs[r][1]) == 0
+        assert moe.read_device_error(ws[r][:4].view(torch.int32)) == 0
+    return [o for o, _ in outs]
+
+
+@pytest.mark.parametrize("G", [2, 4, 8])
+def test_replicated_hot_experts_both_exchange_forms(cuda_device, G):
+    """A skewed router (experts 0-3 hot) with eplb_placement's replicas (two
+    spare slots per rank): the dispatch bytes equal the oracle's replica
+    choice, the peer exchange equals the all-to-all form bit for bit over two
+    calls (both buffer parities), and both equal the single-GPU layer up to
+    the bf16 rounding of each rank's partial sum."""
+    from trials_b200 import _lib
+
+    dev = cuda_device
+    L = synth.make_layer(SHAPE, orc.per_block_quant_fp8, seed=6)
+    W = {k: getattr(L, k).to(dev) for k in ["w13", "w13_scale", "w2", "w2_scale"]}
+    cap = SHAPE.M
+    lib = _lib.lib()
+    H, I, topk = SHAPE.H, SHAPE.I, SHAPE.topk
+    toks0 = _skewed_tokens(G, cap, dev)
+    load = sum(torch.bincount(ids.reshape(-1).cpu(), minlength=SHAPE.E) for _, _, ids in toks0)
+    pl = ep.eplb_placement(load.numpy(), G, SHAPE.E // G + 2)
+    assert pl.max_replicas > 1
+    weights = _rank_weights(W, G, pl)
+    nbytes = lib.b200moe_ep_peer_bytes(cap, H, topk, G)
+    bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(G)]
+    bases = [b.data_ptr() for b in bufs]
+    table = torch.tensor(bases, dtype=torch.int64, device=dev)
+    R = G * cap
+    ws = [torch.zeros(max(lib.b200moe_layer_packed_workspace_size(R, H, I, pl.slots, topk), 256), dtype=torch.uint8,
+                      device=dev) for _ in range(G)]
+    for epoch in (1, 2):
+        toks = toks0 if epoch == 1 else _skewed_tokens(G, cap, dev, seed=400)
+        ref = _all_to_all_form(G, cap, toks, W, dev, placement=pl, check_bytes=(epoch == 1))
+        outs = _peer_call(lib, G, cap, bases, table.data_ptr(), ws, toks, weights, epoch, dev, placement=pl)
+        for r, (hidden, tw, ids) in enumerate(toks):
+            assert torch.equal(outs[r], ref[r]), (epoch, r)
+            single = moe.moe_decode_megakernel_full(hidden, W["w13"], W["w13_scale"], W["w2"], W["w2_scale"], tw, ids)
+            assert orc.rel_l2(outs[r], single) < EP_TOL
+    torch.cuda.synchronize(dev)
