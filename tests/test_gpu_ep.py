@@ -208,6 +208,7 @@ def test_peer_exchange_simulated_ranks_bit_identical_to_all_to_all(cuda_device, 
     R = G * cap
     ws = [torch.zeros(max(ops.workspace_bytes(R, H, I, per, topk), 256), dtype=torch.uint8, device=dev)
           for _ in range(G)]
+    rank_w = _rank_weights(W, G)
     st = torch.cuda.current_stream(dev).cuda_stream
     try:
         for epoch in (1, 2, 3):
@@ -231,12 +232,10 @@ def test_peer_exchange_simulated_ranks_bit_identical_to_all_to_all(cuda_device, 
                     err.data_ptr(), st), "dispatch_peer")
                 state.append((pos, err))
             for d in range(G):
-                sl = slice(d * per, (d + 1) * per)
+                w13, w13s, w2, w2s = rank_w[d]
                 _lib.check(lib.b200moe_layer_packed_peer(
-                    bases[d], table.data_ptr(), G, d, cap, epoch, H, I, per, topk,
-                    W["w13"][sl].contiguous().data_ptr(), W["w13_scale"][sl].contiguous().data_ptr(),
-                    W["w2"][sl].contiguous().data_ptr(), W["w2_scale"][sl].contiguous().data_ptr(), ws[d].data_ptr(),
-                    ws[d].numel(), st), "layer_packed_peer")
+                    bases[d], table.data_ptr(), G, d, cap, epoch, H, I, per, topk, w13.data_ptr(), w13s.data_ptr(),
+                    w2.data_ptr(), w2s.data_ptr(), ws[d].data_ptr(), ws[d].numel(), st), "layer_packed_peer")
             outs = []
             for r, (hidden, _, _) in enumerate(toks):
                 M = hidden.shape[0]
@@ -359,13 +358,16 @@ def _peer_call(lib, G, cap, bases, table_ptr, ws, toks, weights, epoch, dev, pla
         M = hidden.shape[0]
         pos = torch.empty(M * G, dtype=torch.int32, device=dev)
         err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # named (not temporaries): a tensor whose data_ptr() alone is passed would
+        # be freed, and its memory handed to the next allocation, before the kernels run
+        tok_of = torch.empty(G * cap, dtype=torch.int32, device=dev)
+        counts = torch.empty(G, dtype=torch.int32, device=dev)
         _lib.check(lib.b200moe_ep_dispatch_peer(
             hidden.data_ptr(), None, None, ids.data_ptr(), tw.data_ptr(), M, H, topk, SHAPE.E, G, r,
             None if ptable is None else ptable.data_ptr(), 0 if placement is None else placement.max_replicas,
             0 if placement is None else placement.slots, cap, table_ptr, bases[r], epoch, pos.data_ptr(),
-            torch.empty(G * cap, dtype=torch.int32, device=dev).data_ptr(),
-            torch.empty(G, dtype=torch.int32, device=dev).data_ptr(), err.data_ptr(), st), "dispatch_peer")
-        state.append((pos, err))
+            tok_of.data_ptr(), counts.data_ptr(), err.data_ptr(), st), "dispatch_peer")
+        state.append((pos, err, tok_of, counts))
     for d in range(G):
         w13, w13s, w2, w2s = weights[d]
         _lib.check(lib.b200moe_layer_packed_peer(bases[d], table_ptr, G, d, cap, epoch, H, I, E_local, topk,
@@ -374,7 +376,7 @@ def _peer_call(lib, G, cap, bases, table_ptr, ws, toks, weights, epoch, dev, pla
     outs = []
     for r, (hidden, _, _) in enumerate(toks):
         out = torch.empty(hidden.shape[0], H, dtype=torch.bfloat16, device=dev)
-        pos, err = state[r]
+        pos, err = state[r][:2]
         _lib.check(lib.b200moe_ep_combine_peer(bases[r], pos.data_ptr(), hidden.shape[0], H, topk, G, cap, epoch,
                                                out.data_ptr(), err.data_ptr(), st), "combine_peer")
         outs.append((out, err))

@@ -363,8 +363,9 @@ class ExpertParallelMoE:
         rec(0)
         # the pack kernel quantises each token row on its way to the destinations
         table, pl = self._place if self._place is not None else (None, None)
+        hidden = hidden.contiguous()  # held through the call
         _lib.check(lib.b200moe_ep_dispatch_peer(
-            _ptr(hidden.contiguous()), None, None, _ptr(ids), _ptr(tw), M, H, topk, self.E, G, self.rank, _ptr(table),
+            _ptr(hidden), None, None, _ptr(ids), _ptr(tw), M, H, topk, self.E, G, self.rank, _ptr(table),
             pl.max_replicas if pl else 0, pl.slots if pl else 0, cap, bases, own, self.epoch,
             _ptr(self.pos[: M * G]), _ptr(self.tok_of), _ptr(self.counts), _ptr(self.err), st), "ep_dispatch_peer")
         rec(1)

@@ -214,15 +214,19 @@ def _run_layer(hidden, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids, exp
     n_local = E_w
     ws_bytes = L.b200moe_layer_workspace_size(M, H, I, num_experts, n_local, topk)
     ws = _workspaces.get(dev, ws_bytes)
+    # Contiguous copies are bound to names so that they live until the call
+    # returns: a copy whose pointer alone were passed could be freed, and its
+    # memory reused by the next copy, before the kernels read it.
+    w13_scale, w2_scale = w13_scale.contiguous(), w2_scale.contiguous()
     if hidden.dtype == FP8:
         a1 = a1_scale.to(torch.float32).contiguous()
         _lib.check(L.b200moe_layer_quantized(_ptr(hidden), _ptr(a1), M, H, I, num_experts, topk, _ptr(w13),
-                                             _ptr(w13_scale.contiguous()), _ptr(w2), _ptr(w2_scale.contiguous()),
+                                             _ptr(w13_scale), _ptr(w2), _ptr(w2_scale),
                                              _ptr(tw), _ptr(ids), _ptr(expert_map), n_local, _ptr(out), _ptr(ws),
                                              ws.numel(), _stream(dev)), "b200moe_layer_quantized")
         return out
-    _lib.check(L.b200moe_layer(_ptr(hidden), M, H, I, num_experts, topk, _ptr(w13), _ptr(w13_scale.contiguous()),
-                               _ptr(w2), _ptr(w2_scale.contiguous()), _ptr(tw), _ptr(ids), _ptr(expert_map),
+    _lib.check(L.b200moe_layer(_ptr(hidden), M, H, I, num_experts, topk, _ptr(w13), _ptr(w13_scale),
+                               _ptr(w2), _ptr(w2_scale), _ptr(tw), _ptr(ids), _ptr(expert_map),
                                n_local, _ptr(out), _ptr(ws), ws.numel(), _stream(dev)), "b200moe_layer")
     return out
 
@@ -351,12 +355,14 @@ def moe_layer_from_logits(hidden_states: torch.Tensor, router_logits: torch.Tens
         raise ValueError("without expert_map the weights must hold every routed expert")
     bias = None if correction_bias is None else correction_bias.to(device=dev, dtype=torch.float32).contiguous()
     logits = router_logits.contiguous()
+    hidden = hidden_states.contiguous()
+    w13_scale, w2_scale = w13_scale.contiguous(), w2_scale.contiguous()  # held through the call
     L = _lib.lib()
     ws = _workspaces.get(dev, L.b200moe_layer_workspace_size(M, H, I, E_router, E_w, top_k))
-    _lib.check(L.b200moe_layer_logits(_ptr(hidden_states.contiguous()), M, H, I, E_router, top_k, _ptr(logits),
+    _lib.check(L.b200moe_layer_logits(_ptr(hidden), M, H, I, E_router, top_k, _ptr(logits),
                                       int(logits.dtype == torch.bfloat16), scoring, _ptr(bias), int(renormalize),
-                                      float(routed_scaling_factor), _ptr(w13_fp8), _ptr(w13_scale.contiguous()),
-                                      _ptr(w2_fp8), _ptr(w2_scale.contiguous()), _ptr(expert_map), E_w, _ptr(tw),
+                                      float(routed_scaling_factor), _ptr(w13_fp8), _ptr(w13_scale),
+                                      _ptr(w2_fp8), _ptr(w2_scale), _ptr(expert_map), E_w, _ptr(tw),
                                       _ptr(ids), _ptr(out), _ptr(ws), ws.numel(), _stream(dev)),
                "b200moe_layer_logits")
     return out, tw, ids

@@ -150,8 +150,9 @@ def gemm1_silu(a1_q, a1_sT, w13, w13_scale, r: Routing, grid_ctas: int = 0):
     ld = r.a_s_ld()
     a2_q = torch.zeros(r.rows_cap, I, dtype=FP8, device=dev)
     a2_sT = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
+    w13_scale = w13_scale.contiguous()  # held until the call returns (the kernel reads it later)
     _lib.check(_lib.lib().b200moe_gemm1_silu(
-        _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13), _ptr(w13_scale.contiguous()), E, H, I,
+        _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13), _ptr(w13_scale), E, H, I,
         _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows), _ptr(r.n_chunks), r.chunks_cap,
         r.tile_tokens, _ptr(a2_q), _ptr(a2_sT), _ptr(r.err), grid_ctas, _stream(dev)), "gemm1_silu")
     return a2_q, a2_sT
@@ -167,8 +168,9 @@ def gemm2_combine(a2_q, a2_sT, w2, w2_scale, r: Routing, topk_weights: torch.Ten
     tw = topk_weights.to(torch.float32).contiguous()
     if out_pair is None:
         out_pair = torch.zeros(r.pair_rows(M, topk), H, dtype=torch.bfloat16, device=dev)
+    w2_scale = w2_scale.contiguous()
     _lib.check(_lib.lib().b200moe_gemm2_combine(
-        _ptr(a2_q), _ptr(a2_sT), r.a_s_ld(), r.rows_cap, _ptr(w2), _ptr(w2_scale.contiguous()), E, H, I,
+        _ptr(a2_q), _ptr(a2_sT), r.a_s_ld(), r.rows_cap, _ptr(w2), _ptr(w2_scale), E, H, I,
         _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows), _ptr(r.n_chunks), r.chunks_cap,
         r.tile_tokens, _ptr(r.sorted_ids), _ptr(tw), M, topk, _ptr(out_pair), _ptr(r.err), grid_ctas,
         _stream(dev)), "gemm2_combine")
@@ -190,9 +192,10 @@ def experts(a1_q, a1_sT, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights:
     tw = topk_weights.to(torch.float32).contiguous()
     if out_pair is None:
         out_pair = torch.zeros(r.pair_rows(M, topk), H, dtype=torch.bfloat16, device=dev)
+    w13_scale, w2_scale = w13_scale.contiguous(), w2_scale.contiguous()
     _lib.check(_lib.lib().b200moe_experts(
-        _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13), _ptr(w13_scale.contiguous()), _ptr(w2),
-        _ptr(w2_scale.contiguous()), E, H, I, _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows),
+        _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13), _ptr(w13_scale), _ptr(w2),
+        _ptr(w2_scale), E, H, I, _ptr(r.chunk_expert), _ptr(r.chunk_row0), _ptr(r.chunk_rows),
         _ptr(r.n_chunks), r.chunks_cap, _ptr(r.chunk_ready), r.tile_tokens, _ptr(a2_q), _ptr(a2_sT),
         _ptr(r.sorted_ids), _ptr(tw), M, topk, _ptr(out_pair), _ptr(r.err), grid_ctas, _stream(dev)), "experts")
     return a2_q, a2_sT, out_pair
@@ -217,9 +220,10 @@ def experts_fused(hidden, w13, w13_scale, w2, w2_scale, r: Routing, topk_weights
     out_pair = torch.zeros(M * topk, H, dtype=torch.bfloat16, device=dev)
     out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
     tw = topk_weights.to(torch.float32).contiguous()
+    w13_scale, w2_scale = w13_scale.contiguous(), w2_scale.contiguous()
     _lib.check(_lib.lib().b200moe_experts_fused(
         _ptr(hidden), M, topk, _ptr(r.slot_pos), _ptr(a1_q), _ptr(a1_sT), ld, r.rows_cap, _ptr(w13),
-        _ptr(w13_scale.contiguous()), _ptr(w2), _ptr(w2_scale.contiguous()), E, H, I, _ptr(r.chunk_expert),
+        _ptr(w13_scale), _ptr(w2), _ptr(w2_scale), E, H, I, _ptr(r.chunk_expert),
         _ptr(r.chunk_row0), _ptr(r.chunk_rows), _ptr(r.n_chunks), r.chunks_cap, _ptr(r.chunk_ready), r.tile_tokens,
         _ptr(a2_q), _ptr(a2_sT), _ptr(r.sorted_ids), _ptr(tw), _ptr(out_pair), _ptr(out), _ptr(r.err), grid_ctas,
         _stream(dev)), "experts_fused")
