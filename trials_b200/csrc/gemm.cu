@@ -55,10 +55,11 @@ cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const G
 template <int EPI>
 cudaError_t launch_tok(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p, int grid,
                        cudaStream_t stream) {
+  using C = TokCfgE<EPI>;
   auto kernel = moe_grouped_gemm_tok_kernel<EPI>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TokCfg::SMEM_BYTES);
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (err != cudaSuccess) return err;
-  kernel<<<grid, TokCfg::THREADS, TokCfg::SMEM_BYTES, stream>>>(tm_w, tm_a, p);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_a, p);
   return cudaGetLastError();
 }
 

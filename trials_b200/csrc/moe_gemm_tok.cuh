@@ -22,10 +22,23 @@
 
 namespace b200moe {
 
-struct TokCfg {
+// Epilogue warps of the stage-1 (SiLU) token-major kernel: 8 (two per SM
+// sub-partition, 128 weight-row columns per thread) or 16 (four per
+// sub-partition, 64 columns per thread, to hide more of the TMEM-load and FMA
+// latencies of the per-K-block promotion). 16 measured 3% slower at 4,096
+// and 8,192 tokens (96 registers a thread, some spilled), so 8 it is. Stage 2
+// keeps 8 either way: its store transpose buffers would cost a pipeline stage.
+#ifndef B200MOE_TOK_EW_SILU
+#define B200MOE_TOK_EW_SILU 8
+#endif
+
+template <int EW_, bool XPOSE_>
+struct TokCfgT {
   static constexpr int TM = 128;                 // routed rows per unit (MMA M)
   static constexpr int UNIT_ROWS = 256;          // weight rows per unit (MMA N)
-  static constexpr int EW = 8;                   // epilogue warps
+  static constexpr int EW = EW_;                 // epilogue warps: 4 lane quarters x CQ column groups
+  static constexpr int CQ = EW / 4;              // column groups
+  static constexpr int COLS = UNIT_ROWS / CQ;    // weight-row columns per epilogue thread
   static constexpr int THREADS = 64 + 32 * EW;
   static constexpr int A_BYTES = TM * 128;
   static constexpr int W_BYTES = UNIT_ROWS * 128;
@@ -33,19 +46,26 @@ struct TokCfg {
   static constexpr int S_BYTES = TM * 4;
   static constexpr int NBUF = 2;                 // TMEM partial buffers of 256 columns
   static constexpr int TMEM_COLS = 512;
-  static constexpr int RED = 2 * 2 * TM * 4;     // amax exchange, double-buffered by unit parity
+  static constexpr int RED = 2 * CQ * TM * 4;    // amax exchange, double-buffered by unit parity
   static constexpr int SMEM_LIMIT = 232448;
   static constexpr int MAX_STAGE = 6;
-  static constexpr int XPOSE = EW * 32 * 20 * 4;  // stage-2 store transpose blocks
+  static constexpr int XPOSE = XPOSE_ ? EW * 32 * 20 * 4 : 0;  // stage-2 store transpose blocks
   static constexpr int NU = 4;                    // unit hand-off ring (producer -> MMA, epilogue)
   static constexpr int FIXED = 1024 + RED + (MAX_STAGE + NBUF) * S_BYTES + 1024 + XPOSE;
   static constexpr int NSTAGE_RAW = (SMEM_LIMIT - FIXED) / TILE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > MAX_STAGE ? MAX_STAGE : NSTAGE_RAW;
   static constexpr int NSLOT = NSTAGE + NBUF;
   static constexpr int SMEM_BYTES = FIXED + NSTAGE * TILE_BYTES;
+  static_assert(EW == 8 || EW == 16, "8 or 16 epilogue warps");
+  static_assert(COLS % 32 == 0 && COLS <= 128, "a thread's columns lie in one 128-row scale block");
   static_assert(NSTAGE >= 2, "shared memory too small");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
 };
+
+// The configuration of each token-major stage kernel.
+template <int EPI>
+using TokCfgE = TokCfgT<EPI == EPI_SILU ? B200MOE_TOK_EW_SILU : 8, EPI != EPI_SILU>;
+using TokCfg = TokCfgT<8, true>;
 
 
 // Router-weighted fp32 rows of a token-major unit, in sorted row order. The
@@ -110,11 +130,12 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
 #endif
 
 template <int EPI>
-__global__ void __launch_bounds__(TokCfg::THREADS, 1)
+__global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
     moe_grouped_gemm_tok_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                                 const GemmParams p) {
-  using C = TokCfg;
+  using C = TokCfgE<EPI>;
   constexpr int EW = C::EW;
+  constexpr int COLS = C::COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;                                                       // NSTAGE * (A | W)
@@ -317,9 +338,10 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;
     const int q = warp & 3;          // TMEM lane quarter = routed rows 32q..32q+31
-    const int h = ew >> 2;           // column half = weight rows 128h..128h+127 of the unit
+    const int cq = ew >> 2;          // column group = weight rows COLS*cq .. COLS*cq+COLS-1 of the unit
+    const int h = (cq * COLS) >> 7;  // its 128-row scale block
     const int r = q * 32 + lane;     // this thread's routed row within the chunk
-    const uint32_t taddr0 = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 128);
+    const uint32_t taddr0 = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(cq * COLS);
     int slot = 0, buf = 0;
     uint32_t sphase = 0, bphase = 0;
     bool ok = true;
@@ -363,9 +385,9 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
       const bool live = q * 32 < rows;  // warp-uniform
       const float* wsp = ws_row(e, nt);
 
-      float acc[128];
+      float acc[COLS];
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int j = 0; j < COLS; ++j) acc[j] = 0.f;
 
       for (int kb = 0; kb < NKB && ok; ++kb) {
         const float wsh = __shfl_sync(0xffffffffu, kb < 32 ? ws0 : ws1, kb & 31);
@@ -382,9 +404,9 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
         if (live) {
           const float sc = ws * sscale[slot * C::TM + r];
           const uint32_t taddr = taddr0 + (uint32_t)(buf * C::UNIT_ROWS);
-          constexpr int LB = B200MOE_TOK_LD_BATCH;
+          constexpr int LB = COLS == 128 ? B200MOE_TOK_LD_BATCH : 1;
 #pragma unroll
-          for (int c0 = 0; c0 < 8; c0 += LB) {
+          for (int c0 = 0; c0 < COLS / 16; c0 += LB) {
             uint32_t v[LB][16];
 #pragma unroll
             for (int b = 0; b < LB; ++b) tmem_ld16(taddr + (c0 + b) * 16, v[b]);
@@ -431,37 +453,42 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
       if (nu >= 0) load_ws(nu);
 
       if constexpr (EPI == EPI_SILU) {
-        // inter column i of this half = silu(acc[2i]) * acc[2i+1]; group of 128
-        // inter columns = both halves of this unit.
+        // inter column i of this column group = silu(acc[2i]) * acc[2i+1],
+        // column NI*cq + i of the unit's 128 (the 1x128 requant group = all
+        // CQ column groups of this row).
+        constexpr int NI = COLS / 2;
         float m = 0.f;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < NI; ++i) {
           acc[i] = silu_f32(acc[2 * i]) * acc[2 * i + 1];
           m = fmaxf(m, fabsf(acc[i]));
         }
-        float* rb = red + parity * 2 * C::TM;
-        rb[h * C::TM + r] = m;
+        float* rb = red + parity * C::CQ * C::TM;
+        rb[cq * C::TM + r] = m;
         if (threadIdx.x == 64) *stop_sh = *abort_flag;
         named_bar_sync(1, EW * 32);
         // All epilogue warps read the value one thread stored before the
         // barrier; the store for the next unit comes after the second barrier.
         const bool stop = *stop_sh != 0;
-        const float scale = group_scale(fmaxf(rb[r], rb[C::TM + r]));
+        float amax = rb[r];
+#pragma unroll
+        for (int g = 1; g < C::CQ; ++g) amax = fmaxf(amax, rb[g * C::TM + r]);
+        const float scale = group_scale(amax);
         named_bar_sync(1, EW * 32);
         if (stop) break;
         if (r < rows) {
-          uint32_t w[16];
+          uint32_t w[NI / 4];
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
+          for (int k = 0; k < NI / 4; ++k) {
             uint32_t b = 0;
 #pragma unroll
             for (int t = 0; t < 4; ++t) b |= (uint32_t)quant_e4m3(acc[4 * k + t], scale) << (8 * t);
             w[k] = b;
           }
-          uint4* dst = reinterpret_cast<uint4*>(p.out_q + (int64_t)(p0 + r) * p.out_q_ld + nt * 128 + h * 64);
+          uint4* dst = reinterpret_cast<uint4*>(p.out_q + (int64_t)(p0 + r) * p.out_q_ld + nt * 128 + cq * NI);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-          if (h == 0) p.out_sT[(int64_t)nt * p.out_s_ld + p0 + r] = scale;
+          for (int k = 0; k < NI / 16; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          if (cq == 0) p.out_sT[(int64_t)nt * p.out_s_ld + p0 + r] = scale;
         }
       } else {
         if (!ok) break;
@@ -473,7 +500,7 @@ __global__ void __launch_bounds__(TokCfg::THREADS, 1)
           const float w = f < p.sentinel ? __ldg(&p.topk_w[f]) : 0.f;
           const unsigned valid = __ballot_sync(0xffffffffu, f < p.sentinel);
           store_sorted_rows(acc, w, valid, xpose + ew * (32 * 20), lane, q * 32,
-                            p.out_pair + (int64_t)p0 * p.Nw + nt * C::UNIT_ROWS + h * 128, p.Nw);
+                            p.out_pair + (int64_t)p0 * p.Nw + nt * C::UNIT_ROWS + cq * COLS, p.Nw);
         }
       }
     }
