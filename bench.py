@@ -648,6 +648,8 @@ def run_sweep(args, shape, L, dev, clocks, peak):
 
     recs = []
     for kind, M, hot in SWEEP:
+        # each workload starts from an idle GPU, not from the power state the previous one left
+        time.sleep(0.5)
         h, tw, ids = layer_inputs(shape, M, hot, args.seed + 3000 + M + hot, dev)
         pipe = stages.LayerPipeline(M, shape.H, shape.I, shape.E, shape.topk, dev)
         w = (L.w13, L.w13_scale, L.w2, L.w2_scale)
@@ -678,11 +680,13 @@ def run_sweep(args, shape, L, dev, clocks, peak):
                      "value": M / (ms / 1e3), "unit": "tokens/s", "active_experts": active, "pairs": pairs,
                      "layer_hbm_gbs": layer_bytes(synth.glm(M), active, pairs) / (ms / 1e3) / 1e9,
                      "stage_ms": stage_ms, "roofline": roof, "device_error": err,
+                     "heavy_experts_list": bool(pipe.heavy_rows),
                      "gpu_launches": (len(pipe.stages) + (1 if pipe.tile > 64 else 0) +
-                                      (1 if pipe.rscratch_ints > 0 else 0)) * steps})
+                                      (1 if pipe.rscratch_ints > 0 else 0) + (2 if pipe.heavy_rows else 0)) * steps})
         del pipe, h, tw, ids
         torch.cuda.empty_cache()
     return {"steps": args.sweep_steps, "warmup": 3, "records": recs, "clocks": clocks.summary("sweep"),
+            "pause_s_before_each": 0.5,
             "l2": "no flush: every step streams the active experts' weights (>= 8 GB)",
             "peaks": {"hbm_gbs": peak, "fp8_tflops": FP8_PEAK_TFLOPS}}
 
@@ -855,7 +859,8 @@ def run_ours(args, shape, config):
         traffic_name = f"gemm1_silu_glm_decode_m{shape.M}{hot}"
     achieved = k_bytes / (k_ms / 1e3) / 1e9
     launches = (len(pipe.stages) + (1 if not args.split and pipe.tile > 64 else 0) +
-                (1 if pipe.rscratch_ints > 0 else 0))  # routing on several CTAs: two launches
+                (1 if pipe.rscratch_ints > 0 else 0) +  # routing on several CTAs: two launches
+                (2 if pipe.heavy_rows else 0))          # the token-major stages of the heavy-expert list
     step_bytes = layer_bytes(shape, active, pairs)
     roof = {"kernel": k_name, "bound": "hbm", "achieved": achieved,
             "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -341,6 +341,32 @@ B200MOE_API int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int 
                   int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
                   int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream);
 
+/* Mixed work lists for skewed decode batches (what b200moe_layer does by
+ * itself): with tiles of 16..64 tokens, experts with more than heavy_rows
+ * padded rows (a skewed router's hot experts) are laid out after all the
+ * others and cut into chunks of at most 128 rows in a second list, which
+ * b200moe_experts_heavy runs with the token-major stages; the rest form the
+ * usual tile_tokens list for b200moe_experts. The device decides per expert
+ * after routing: no host synchronisation. counts (4 ints) receives
+ * [light chunks, total rows, heavy chunks, first heavy row]; heavy_counters
+ * (2 ints) is zeroed for b200moe_experts_heavy; heavy_chunks_capacity >=
+ * b200moe_route_capacity_chunks(M*topk, E, 128). Below 16,384 routed slots
+ * only (one-CTA routing). b200moe_heavy_rows(M, topk, tile) returns the
+ * threshold the layer uses (128), or 0 when the layer does not split (M <=
+ * 128: no expert can have more rows; tiles of 128/256; 16,384 slots or more).
+ * Replaces nothing in the reference, whose kernels take one tile size per
+ * launch (moe_decode_megakernel.py:88-123); sorted_ids keeps its meaning,
+ * but the experts' order within it is light experts first. */
+B200MOE_API int b200moe_heavy_rows(int64_t M, int topk, int tile_tokens);
+B200MOE_API int b200moe_route_mixed(const int32_t* topk_ids, int64_t M, int topk, int num_experts,
+                                    const int32_t* expert_map, int num_local_experts, int tile_tokens,
+                                    int heavy_rows, int32_t* sorted_ids, int64_t rows_capacity,
+                                    int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows,
+                                    int64_t chunks_capacity, int32_t* heavy_chunk_expert, int32_t* heavy_chunk_row0,
+                                    int32_t* heavy_chunk_rows, int64_t heavy_chunks_capacity, int32_t* counts,
+                                    int32_t* slot_pos, int32_t* chunk_ready, int32_t* heavy_counters,
+                                    int32_t* err_word, void* stream);
+
 /* b200moe_route starting from router logits (the router of b200moe_router_topk
  * fused into routing's first launch; ids and weights stored to topk_ids /
  * topk_weights, then routed): results equal b200moe_router_topk followed by
@@ -422,6 +448,19 @@ B200MOE_API int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t
                     int64_t chunks_capacity, int32_t* chunk_ready, int tile_tokens, uint8_t* a2_q, float* a2_sT,
                     const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, void* out_pair,
                     int32_t* err_word, int grid_ctas, void* stream);
+
+/* The heavy list of b200moe_route_mixed through the token-major stages
+ * (stage 1 then stage 2, units from heavy_counters), writing stage-2 rows by
+ * slot into the same out_pair (M*topk rows) as b200moe_experts does for the
+ * light list, so one b200moe_combine_reduce (sorted_rows = 0) sums both. */
+B200MOE_API int b200moe_experts_heavy(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld,
+                                      int64_t rows_capacity, const uint8_t* w13, const float* w13_scale,
+                                      const uint8_t* w2, const float* w2_scale, int num_local_experts, int64_t H,
+                                      int64_t I, const int32_t* heavy_chunk_expert, const int32_t* heavy_chunk_row0,
+                                      const int32_t* heavy_chunk_rows, const int32_t* n_heavy_chunks,
+                                      int64_t heavy_chunks_capacity, int32_t* heavy_counters, uint8_t* a2_q,
+                                      float* a2_sT, const int32_t* sorted_ids, const float* topk_weights, int64_t M,
+                                      int topk, void* out_pair, int32_t* err_word, int grid_ctas, void* stream);
 
 /* Everything after b200moe_route for small batches (tiles of 16..64 tokens),
  * in one persistent launch (the single-launch layer the reference deferred,

@@ -66,6 +66,9 @@ SIGNATURES = {
     "b200moe_route_capacity_chunks": (_L, [_L, _I, _I]),
     "b200moe_route_scratch_ints": (_L, [_L, _I]),
     "b200moe_route": (_I, [_P, _L, _I, _I, _P, _I, _I, _P, _L, _P, _P, _P, _L, _P, _P, _P, _P, _P, _L, _P, _P]),
+    "b200moe_heavy_rows": (_I, [_L, _I, _I]),
+    "b200moe_route_mixed": (_I, [_P, _L, _I, _I, _P, _I, _I, _I, _P, _L, _P, _P, _P, _L, _P, _P, _P, _L, _P, _P, _P,
+                                 _P, _P, _P]),
     "b200moe_route_logits_scratch_ints": (_L, [_L, _I]),
     "b200moe_route_logits": (_I, [_P, _I, _L, _I, _I, _I, _P, _I, ctypes.c_float, _P, _P, _P, _I, _I, _P, _L, _P, _P,
                                   _P, _L, _P, _P, _P, _P, _P, _L, _P, _P]),
@@ -76,6 +79,8 @@ SIGNATURES = {
                                    _P, _P, _I, _P]),
     "b200moe_experts": (_I, [_P, _P, _L, _L, _P, _P, _P, _P, _I, _L, _L, _P, _P, _P, _P, _L, _P, _I, _P, _P, _P, _P,
                              _L, _I, _P, _P, _I, _P]),
+    "b200moe_experts_heavy": (_I, [_P, _P, _L, _L, _P, _P, _P, _P, _I, _L, _L, _P, _P, _P, _P, _L, _P, _P, _P, _P,
+                                   _P, _L, _I, _P, _P, _I, _P]),
     "b200moe_experts_fused": (_I, [_P, _L, _I, _P, _P, _P, _L, _L, _P, _P, _P, _P, _I, _L, _L, _P, _P, _P, _P, _L,
                                    _P, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P]),
     "b200moe_combine_reduce": (_I, [_P, _P, _I, _L, _I, _L, _P, _P]),

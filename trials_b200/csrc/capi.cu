@@ -117,11 +117,22 @@ bool fan_out_tokens(int64_t numel, int topk) { return numel >= kFanOutMinPairs &
 // write rows in sorted order, the swap-AB tiles one row per slot.
 int pair_sorted_rows(int tile_tokens) { return tile_tokens > 64 ? 1 : 0; }
 
+// Mixed work lists: with tiles of 16..64 tokens, experts whose padded rows
+// exceed this many (a skewed router's hot experts) are cut into 128-row
+// chunks for the token-major stages instead, in the same layer call. An
+// expert has at most M rows, so this needs M > kHeavyRows, and the one-CTA
+// routing (below 16,384 routed slots), which builds the two lists.
+constexpr int kHeavyRows = 128;
+int heavy_rows_for(int64_t M, int64_t numel, int tile) {
+  return (tile <= 64 && M > kHeavyRows && route_ctas(numel) == 1) ? kHeavyRows : 0;
+}
+
 struct LayerPlan {
   int tile_tokens;
-  int64_t rows_cap, chunks_cap, as_ld;
+  int heavy_rows;  // > 0: mixed work lists (second list in off_ce2.., counters in off_ready2)
+  int64_t rows_cap, chunks_cap, chunks_cap2, as_ld;
   size_t off_sorted, off_pos, off_ce, off_cr0, off_crows, off_ready, off_counts, off_a1, off_a1s, off_a2, off_a2s,
-      off_pair, off_rscratch, total;
+      off_pair, off_rscratch, off_ce2, off_cr0_2, off_crows2, off_ready2, total;
   int64_t rscratch_ints;  // routing on several CTAs (large batches)
 };
 
@@ -130,8 +141,10 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk, int
   LayerPlan p{};
   const int64_t numel = M * topk;
   p.tile_tokens = tile > 0 ? tile : pick_tile_tokens(numel, E_local);
+  p.heavy_rows = heavy_rows_for(M, numel, p.tile_tokens);
   p.rows_cap = b200moe_route_capacity_rows(numel, E_local);
   p.chunks_cap = b200moe_route_capacity_chunks(numel, E_local, p.tile_tokens);
+  p.chunks_cap2 = p.heavy_rows ? b200moe_route_capacity_chunks(numel, E_local, kHeavyTile) : 0;
   p.as_ld = round_up(p.rows_cap + 256, 64);
   size_t off = 256;  // device error word
   auto take = [&](size_t bytes) {
@@ -154,6 +167,12 @@ LayerPlan plan_layer(int64_t M, int64_t H, int64_t I, int E_local, int topk, int
   p.off_pair = take(sizeof(__nv_bfloat16) * (size_t)(pair_sorted_rows(p.tile_tokens) ? p.rows_cap : numel) * H);
   p.rscratch_ints = route_scratch_ints(numel, E_local);
   if (p.rscratch_ints > 0) p.off_rscratch = take(sizeof(int32_t) * (size_t)p.rscratch_ints);
+  if (p.heavy_rows) {
+    p.off_ce2 = take(sizeof(int32_t) * p.chunks_cap2);
+    p.off_cr0_2 = take(sizeof(int32_t) * p.chunks_cap2);
+    p.off_crows2 = take(sizeof(int32_t) * p.chunks_cap2);
+    p.off_ready2 = take(sizeof(int32_t) * 2);
+  }
   p.total = off;
   return p;
 }
@@ -330,6 +349,18 @@ int64_t b200moe_route_scratch_ints(int64_t numel, int num_local_experts) {
 
 namespace {
 
+// The second (heavy) work list of mixed routing.
+struct MixedLists {
+  int heavy_rows;
+  int32_t* chunk_expert;
+  int32_t* chunk_row0;
+  int32_t* chunk_rows;
+  int64_t chunks_cap;
+  int32_t* n_chunks;
+  int32_t* heavy_row0;
+  int32_t* counters;  // 2 ints, zeroed: the unit counters of the two token-major stages
+};
+
 // b200moe_route, and b200moe_route_logits when `router` is set (topk_ids then
 // names the router's id output, which routing reads after the router stored it).
 int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
@@ -337,7 +368,7 @@ int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, co
                int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
                int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
                int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream,
-               const RouterArgs* router, int32_t* router_counter) {
+               const RouterArgs* router, int32_t* router_counter, const MixedLists* mixed = nullptr) {
   if (M < 0 || topk <= 0 || num_experts <= 0 || !valid_tile(tile_tokens) || !sorted_ids || !chunk_expert ||
       !chunk_row0 || !chunk_rows || !n_chunks || !num_rows || !err_word || (M > 0 && !topk_ids))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_route: bad argument%s");
@@ -369,6 +400,21 @@ int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, co
   a.chunk_ready = chunk_ready;
   a.slot_pos = slot_pos;
   a.err = err_word;
+  if (mixed && mixed->heavy_rows > 0) {
+    if (route_ctas(numel) != 1 || tile_tokens > 64 || !mixed->chunk_expert || !mixed->chunk_row0 ||
+        !mixed->chunk_rows || !mixed->n_chunks || !mixed->heavy_row0 || !mixed->counters ||
+        mixed->chunks_cap < b200moe_route_capacity_chunks(numel, E, kHeavyTile))
+      return fail(B200MOE_ERR_INVALID_ARG, "mixed work lists: bad argument (tiles of 16..64 tokens, below 16,384 "
+                                           "routed slots, heavy list capacity)%s");
+    a.heavy_rows = mixed->heavy_rows;
+    a.chunk_expert2 = mixed->chunk_expert;
+    a.chunk_row0_2 = mixed->chunk_row0;
+    a.chunk_rows2 = mixed->chunk_rows;
+    a.chunks_cap2 = mixed->chunks_cap;
+    a.n_chunks2 = mixed->n_chunks;
+    a.heavy_row0 = mixed->heavy_row0;
+    a.counters2 = mixed->counters;
+  }
   if (router) {
     // The CTA counter: router_counter, or the first ints of route_scratch.
     int32_t* counts = router_counter ? route_scratch : route_scratch + kRouteLogitsCounterInts;
@@ -394,6 +440,27 @@ int b200moe_route(const int32_t* topk_ids, int64_t M, int topk, int num_experts,
   return route_impl(topk_ids, M, topk, num_experts, expert_map, num_local_experts, tile_tokens, sorted_ids,
                     rows_capacity, chunk_expert, chunk_row0, chunk_rows, chunks_capacity, n_chunks, num_rows,
                     slot_pos, chunk_ready, route_scratch, route_scratch_ints, err_word, stream, nullptr, nullptr);
+}
+
+int b200moe_heavy_rows(int64_t M, int topk, int tile_tokens) {
+  if (M < 0 || topk <= 0) return 0;
+  return heavy_rows_for(M, M * topk, tile_tokens);
+}
+
+int b200moe_route_mixed(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
+                        int num_local_experts, int tile_tokens, int heavy_rows, int32_t* sorted_ids,
+                        int64_t rows_capacity, int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows,
+                        int64_t chunks_capacity, int32_t* heavy_chunk_expert, int32_t* heavy_chunk_row0,
+                        int32_t* heavy_chunk_rows, int64_t heavy_chunks_capacity, int32_t* counts,
+                        int32_t* slot_pos, int32_t* chunk_ready, int32_t* heavy_counters, int32_t* err_word,
+                        void* stream) {
+  if (heavy_rows <= 0 || !counts)
+    return fail(B200MOE_ERR_INVALID_ARG, "b200moe_route_mixed: heavy_rows must be positive%s");
+  const MixedLists mx{heavy_rows, heavy_chunk_expert, heavy_chunk_row0, heavy_chunk_rows, heavy_chunks_capacity,
+                      counts + 2, counts + 3, heavy_counters};
+  return route_impl(topk_ids, M, topk, num_experts, expert_map, num_local_experts, tile_tokens, sorted_ids,
+                    rows_capacity, chunk_expert, chunk_row0, chunk_rows, chunks_capacity, counts, counts + 1,
+                    slot_pos, chunk_ready, nullptr, 0, err_word, stream, nullptr, nullptr, &mx);
 }
 
 int64_t b200moe_route_logits_scratch_ints(int64_t numel, int num_local_experts) {
@@ -509,7 +576,8 @@ int gemm2_combine_core(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, 
                        const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,
                        const int32_t* n_chunks, int64_t chunks_capacity, int tile_tokens,
                        const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk,
-                       void* out_pair, int32_t* err_word, int grid_ctas, void* stream, int32_t* unit_counter) {
+                       void* out_pair, int32_t* err_word, int grid_ctas, void* stream, int32_t* unit_counter,
+                       int rows_by_slot = 0) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (!valid_tile(tile_tokens) || num_local_experts <= 0 || rows_capacity <= 0 || M < 0 || topk <= 0 ||
@@ -524,11 +592,31 @@ int gemm2_combine_core(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, 
   p.topk_w = topk_weights;
   p.sentinel = (int32_t)(M * topk);
   p.out_pair = static_cast<__nv_bfloat16*>(out_pair);
+  p.rows_by_slot = rows_by_slot;
   p.err = err_word;
   p.unit_counter = unit_counter;
   return run_gemm(EPI_COMBINE, a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I,
                   chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, tile_tokens, p, grid_ctas,
                   (cudaStream_t)stream);
+}
+
+// The token-major stages on the heavy list of mixed routing (128-row chunks,
+// units from the two counters), stage-2 rows by slot like the swap-AB tiles.
+int experts_heavy_core(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
+                       const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                       int num_local_experts, int64_t H, int64_t I, const int32_t* chunk_expert,
+                       const int32_t* chunk_row0, const int32_t* chunk_rows, const int32_t* n_chunks,
+                       int64_t chunks_capacity, int32_t* counters, uint8_t* a2_q, float* a2_sT,
+                       const int32_t* sorted_ids, const float* topk_weights, int64_t M, int topk, void* out_pair,
+                       int32_t* err_word, int grid_ctas, void* stream) {
+  if (!counters) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_experts_heavy: null counters%s");
+  int st = gemm1_silu_core(a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, num_local_experts, H, I,
+                           chunk_expert, chunk_row0, chunk_rows, n_chunks, chunks_capacity, kHeavyTile, a2_q, a2_sT,
+                           err_word, grid_ctas, stream, counters);
+  if (st) return st;
+  return gemm2_combine_core(a2_q, a2_sT, a_s_ld, rows_capacity, w2, w2_scale, num_local_experts, H, I, chunk_expert,
+                            chunk_row0, chunk_rows, n_chunks, chunks_capacity, kHeavyTile, sorted_ids, topk_weights,
+                            M, topk, out_pair, err_word, grid_ctas, stream, counters + 1, /*rows_by_slot=*/1);
 }
 
 }  // namespace
@@ -611,6 +699,19 @@ int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int
   return cuda_status(launch_grouped_gemm_fused(tile_tokens, tw1, ta1, p1, tw2, ta2, p2, (int)grid,
                                                (cudaStream_t)stream),
                      "experts");
+}
+
+int b200moe_experts_heavy(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
+                          const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                          int num_local_experts, int64_t H, int64_t I, const int32_t* heavy_chunk_expert,
+                          const int32_t* heavy_chunk_row0, const int32_t* heavy_chunk_rows,
+                          const int32_t* n_heavy_chunks, int64_t heavy_chunks_capacity, int32_t* heavy_counters,
+                          uint8_t* a2_q, float* a2_sT, const int32_t* sorted_ids, const float* topk_weights,
+                          int64_t M, int topk, void* out_pair, int32_t* err_word, int grid_ctas, void* stream) {
+  return experts_heavy_core(a1_q, a1_sT, a_s_ld, rows_capacity, w13, w13_scale, w2, w2_scale, num_local_experts, H,
+                            I, heavy_chunk_expert, heavy_chunk_row0, heavy_chunk_rows, n_heavy_chunks,
+                            heavy_chunks_capacity, heavy_counters, a2_q, a2_sT, sorted_ids, topk_weights, M, topk,
+                            out_pair, err_word, grid_ctas, stream);
 }
 
 int b200moe_experts_fused(const void* hidden, int64_t M, int topk, const int32_t* slot_pos, uint8_t* a1_q,
@@ -751,9 +852,17 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   int32_t* rscratch = pl.rscratch_ints > 0 ? reinterpret_cast<int32_t*>(wl + pl.off_rscratch) : nullptr;
   // Routing from router logits: the router's CTA counter is int 1 of the
   // workspace header (zeroed with the error word; every call leaves it zero).
+  // Mixed work lists (decode batches with heavy experts): counts[2] = heavy
+  // chunks, counts[3] = first heavy row.
+  MixedLists mx{};
+  if (pl.heavy_rows) {
+    mx = MixedLists{pl.heavy_rows, reinterpret_cast<int32_t*>(wl + pl.off_ce2),
+                    reinterpret_cast<int32_t*>(wl + pl.off_cr0_2), reinterpret_cast<int32_t*>(wl + pl.off_crows2),
+                    pl.chunks_cap2, counts + 2, counts + 3, reinterpret_cast<int32_t*>(wl + pl.off_ready2)};
+  }
   st = route_impl(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0, crows,
                   pl.chunks_cap, counts, counts + 1, pos, ready, rscratch, pl.rscratch_ints, err, stream, router,
-                  router ? err + 1 : nullptr);
+                  router ? err + 1 : nullptr, pl.heavy_rows ? &mx : nullptr);
   if (st) return st;
   const LayerInput& src = in;
   if (src.hidden) {
@@ -769,6 +878,12 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
                        pl.chunks_cap, ready, pl.tile_tokens, a2, a2s, sorted, topk_weights, M, topk, pair, err, 0,
                        stream);
   if (st) return st;
+  if (pl.heavy_rows) {
+    st = experts_heavy_core(a1, a1s, pl.as_ld, pl.rows_cap, w13, w13_scale, w2, w2_scale, E, H, I, mx.chunk_expert,
+                            mx.chunk_row0, mx.chunk_rows, mx.n_chunks, mx.chunks_cap, mx.counters, a2, a2s, sorted,
+                            topk_weights, M, topk, pair, err, 0, stream);
+    if (st) return st;
+  }
   if (peer_out)  // results straight into the source ranks' return areas
     return cuda_status(launch_ep_reduce_peer(pair, pos, pair_sorted_rows(pl.tile_tokens), topk, H, *peer_out,
                                              peer_counter, (cudaStream_t)stream),

@@ -33,7 +33,22 @@ struct AlignArgs {
   int32_t* slot_pos;       // nullable: sorted position of each flat slot (n entries), -1 if dropped
   int32_t* err;
   int seg_align;           // multi-CTA segments: multiple of this many ids (0/1 = any)
+  // Mixed work lists (one-CTA routing only; 0 = off): experts with more than
+  // heavy_rows padded rows are laid out after all the others and cut into
+  // chunks of at most 128 rows in a second list (for the token-major stages);
+  // the rest form the tile_tokens list as usual. *heavy_row0 receives the
+  // first row of the heavy experts (= the light experts' rows), *n_chunks2
+  // the heavy list's length; counters2 (2 ints) is zeroed.
+  int heavy_rows;
+  int32_t* chunk_expert2;
+  int32_t* chunk_row0_2;
+  int32_t* chunk_rows2;
+  int64_t chunks_cap2;
+  int32_t* n_chunks2;
+  int32_t* heavy_row0;
+  int32_t* counters2;
 };
+constexpr int kHeavyTile = 128;  // chunk rows of the heavy list
 
 size_t align_smem_bytes(int E);
 cudaError_t launch_align(const AlignArgs& a, cudaStream_t stream);

@@ -87,8 +87,9 @@ struct GemmParams {
   const float* topk_w;
   int32_t sentinel;   // M * topk
   // bf16 rows of Nw (router weight applied): row f = slot (tiles <= 64) or
-  // sorted row p (tiles >= 128)
+  // sorted row p (tiles >= 128, unless rows_by_slot)
   __nv_bfloat16* out_pair;
+  int rows_by_slot;   // token-major stage 2: write row f (slot) instead of sorted row p
   // EPI_FUSED: per-chunk count of finished stage-1 units (zeroed by routing),
   // followed by two phase counters (CTAs done with phase 0 / with all units)
   int32_t* chunk_ready;

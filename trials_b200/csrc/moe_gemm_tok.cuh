@@ -163,6 +163,9 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int NKB = p.K >> 7;
   const int NT = p.Nw / C::UNIT_ROWS;
+  // An empty work list (the heavy list of a batch without heavy experts)
+  // ends the launch before any set-up.
+  if (*p.n_chunks == 0) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
@@ -498,9 +501,25 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
         if (live) {
           const int f = r < rows ? __ldg(&p.sorted_ids[p0 + r]) : p.sentinel;
           const float w = f < p.sentinel ? __ldg(&p.topk_w[f]) : 0.f;
-          const unsigned valid = __ballot_sync(0xffffffffu, f < p.sentinel);
-          store_sorted_rows(acc, w, valid, xpose + ew * (32 * 20), lane, q * 32,
-                            p.out_pair + (int64_t)p0 * p.Nw + nt * C::UNIT_ROWS + cq * COLS, p.Nw);
+          if (p.rows_by_slot) {
+            // Row f (the slot), as the swap-AB tiles write it: COLS contiguous
+            // bf16 per thread (few heavy experts of a decode batch take this path).
+            if (f < p.sentinel) {
+              uint4* dst = reinterpret_cast<uint4*>(p.out_pair + (int64_t)f * p.Nw + nt * C::UNIT_ROWS + cq * COLS);
+#pragma unroll
+              for (int k = 0; k < COLS / 8; ++k) {
+                __nv_bfloat162 b[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                  b[t] = __floats2bfloat162_rn(w * acc[8 * k + 2 * t], w * acc[8 * k + 2 * t + 1]);
+                dst[k] = *reinterpret_cast<const uint4*>(b);
+              }
+            }
+          } else {
+            const unsigned valid = __ballot_sync(0xffffffffu, f < p.sentinel);
+            store_sorted_rows(acc, w, valid, xpose + ew * (32 * 20), lane, q * 32,
+                              p.out_pair + (int64_t)p0 * p.Nw + nt * C::UNIT_ROWS + cq * COLS, p.Nw);
+          }
         }
       }
     }

@@ -90,9 +90,12 @@ __device__ void align_body(const AlignArgs& a, int32_t* sm) {
   int32_t* base = cnt + kRouteWarps * E;    // [E + 1] padded row offsets
   int32_t* padded = base + E + 1;           // [E]
   int32_t* chbase = padded + E;             // [E + 1] chunk offsets
+  int32_t* chbase2 = chbase + E + 1;        // [E + 1] heavy-list chunk offsets (mixed lists)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool mixed = a.heavy_rows > 0;
   if (a.chunk_ready)  // per-chunk counters and the two phase counters after them
     for (int64_t i = tid; i < a.chunks_cap + 2; i += kRouteThreads) a.chunk_ready[i] = 0;
+  if (mixed && tid < 2) a.counters2[tid] = 0;
 
   for (int i = tid; i < kRouteWarps * E; i += kRouteThreads) cnt[i] = 0;
   __syncthreads();
@@ -131,26 +134,43 @@ __device__ void align_body(const AlignArgs& a, int32_t* sm) {
   }
   const int bm = a.block_m;
   const int pad = tid < E ? (tot + bm - 1) / bm * bm : 0;
-  int total_rows = 0;
-  const int off = block_exclusive_scan(pad, warp_tot, &total_rows);
-  int nch = 0;
+  // Mixed lists: heavy experts (more than heavy_rows padded rows) after all
+  // the light ones, each group in expert order.
+  const bool heavy = mixed && pad > a.heavy_rows;
+  int total_rows = 0, total_heavy = 0;
+  const int off = block_exclusive_scan(heavy ? 0 : pad, warp_tot, &total_rows);
+  const int off_h = mixed ? block_exclusive_scan(heavy ? pad : 0, warp_tot, &total_heavy) : 0;
+  const int total_light = total_rows;
+  total_rows += total_heavy;
+  int nch = 0, nch2 = 0;
   if (tid < E) {
-    base[tid] = off;
+    base[tid] = heavy ? total_light + off_h : off;
     padded[tid] = pad;
-    if (a.tile_tokens > 0) nch = (pad + a.tile_tokens - 1) / a.tile_tokens;
+    if (heavy) nch2 = (pad + kHeavyTile - 1) / kHeavyTile;
+    else if (a.tile_tokens > 0) nch = (pad + a.tile_tokens - 1) / a.tile_tokens;
   }
-  int total_chunks = 0;
+  int total_chunks = 0, total_chunks2 = 0;
   const int choff = block_exclusive_scan(nch, warp_tot, &total_chunks);
-  if (tid < E) chbase[tid] = choff;
+  const int choff2 = mixed ? block_exclusive_scan(nch2, warp_tot, &total_chunks2) : 0;
+  if (tid < E) {
+    chbase[tid] = choff;
+    chbase2[tid] = choff2;
+  }
   if (tid == 0) {
     base[E] = total_rows;
     chbase[E] = total_chunks;
+    chbase2[E] = total_chunks2;
   }
-  const bool overflow = total_rows > a.sorted_cap || (a.tile_tokens > 0 && total_chunks > a.chunks_cap);
+  const bool overflow = total_rows > a.sorted_cap || (a.tile_tokens > 0 && total_chunks > a.chunks_cap) ||
+                        (mixed && total_chunks2 > a.chunks_cap2);
   if (tid == 0) {
     if (overflow) atomicOr(a.err, ERR_DEV_CAPACITY);
     *a.ntp = overflow ? 0 : total_rows;
     if (a.n_chunks) *a.n_chunks = overflow ? 0 : total_chunks;
+    if (mixed) {
+      *a.n_chunks2 = overflow ? 0 : total_chunks2;
+      *a.heavy_row0 = overflow ? 0 : total_light;
+    }
   }
   // Defined contents everywhere: sentinel ids (and no position for any slot)
   // first, then the scatter below.
@@ -207,19 +227,25 @@ __device__ void align_body(const AlignArgs& a, int32_t* sm) {
   }
 
   // GEMM work list: each expert's rows cut into nearly equal chunks of at
-  // most tile_tokens rows (multiples of block_m).
+  // most tile_tokens rows (multiples of block_m); heavy experts of mixed
+  // lists into chunks of at most kHeavyTile rows in the second list.
   if (a.tile_tokens > 0 && tid < E) {
     const int P = padded[tid];
+    const bool hv = mixed && P > a.heavy_rows;
     if (P > 0) {
+      const int* cb = hv ? chbase2 : chbase;
+      int32_t* ce = hv ? a.chunk_expert2 : a.chunk_expert;
+      int32_t* cr0 = hv ? a.chunk_row0_2 : a.chunk_row0;
+      int32_t* crw = hv ? a.chunk_rows2 : a.chunk_rows;
       const int blocks = P / bm;
-      const int nc = chbase[tid + 1] - chbase[tid];
+      const int nc = cb[tid + 1] - cb[tid];
       const int per = blocks / nc, extra = blocks % nc;
       int row0 = base[tid];
       for (int c = 0; c < nc; ++c) {
         const int rows = (per + (c < extra ? 1 : 0)) * bm;
-        a.chunk_expert[chbase[tid] + c] = tid;
-        a.chunk_row0[chbase[tid] + c] = row0;
-        a.chunk_rows[chbase[tid] + c] = rows;
+        ce[cb[tid] + c] = tid;
+        cr0[cb[tid] + c] = row0;
+        crw[cb[tid] + c] = rows;
         row0 += rows;
       }
     }
@@ -260,7 +286,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) router_align_kernel(const Al
   align_body<true>(a, sm);
 }
 
-size_t align_smem_bytes(int E) { return (size_t)(kRouteWarps * E + 3 * E + 2) * sizeof(int32_t); }
+size_t align_smem_bytes(int E) { return (size_t)(kRouteWarps * E + 4 * E + 3) * sizeof(int32_t); }
 
 cudaError_t launch_align(const AlignArgs& a, cudaStream_t stream) {
   const size_t smem = align_smem_bytes(a.E);
@@ -534,7 +560,8 @@ cudaError_t launch_route_multi(const AlignArgs& a, const RouterArgs& r, int C, i
 
 cudaError_t launch_route(const AlignArgs& a, int32_t* scratch, int64_t scratch_ints, cudaStream_t stream) {
   const int C = route_ctas(a.n);
-  if (C == 1 || !scratch || scratch_ints < (int64_t)C * a.E) return launch_align(a, stream);
+  // mixed work lists are built by the one-CTA kernel only
+  if (C == 1 || a.heavy_rows > 0 || !scratch || scratch_ints < (int64_t)C * a.E) return launch_align(a, stream);
   return launch_route_multi<false>(a, RouterArgs{}, C, scratch, stream);
 }
 
@@ -546,7 +573,7 @@ cudaError_t launch_route_logits(const AlignArgs& a_in, const RouterArgs& r, int6
   a.topk_ids = r.out_ids;
   a.seg_align = r.topk;
   const int C = route_ctas(a.n);
-  if (C > 1) return launch_route_multi<true>(a, r, C, counts, stream);
+  if (C > 1 && a.heavy_rows == 0) return launch_route_multi<true>(a, r, C, counts, stream);
   const size_t smem = align_smem_bytes(a.E);
   cudaError_t err =
       cudaFuncSetAttribute(router_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

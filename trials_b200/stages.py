@@ -115,6 +115,31 @@ def route_logits(logits: torch.Tensor, top_k: int, tile_tokens: int, scoring_fun
     return r, tw, ids
 
 
+def route_mixed(topk_ids: torch.Tensor, num_experts: int, tile_tokens: int, heavy_rows: int = 128):
+    """Mixed work lists (b200moe_route_mixed) -> (Routing of the light list,
+    heavy list dict {chunk_expert, chunk_row0, chunk_rows, counters, cap},
+    counts (4,) = [light chunks, rows, heavy chunks, first heavy row])."""
+    dev = _require_cuda(topk_ids)
+    ids = topk_ids.to(torch.int32).contiguous()
+    M, topk = ids.shape
+    L = _lib.lib()
+    rows_cap = L.b200moe_route_capacity_rows(M * topk, num_experts)
+    chunks_cap = L.b200moe_route_capacity_chunks(M * topk, num_experts, tile_tokens)
+    cap2 = L.b200moe_route_capacity_chunks(M * topk, num_experts, 128)
+    z = lambda n: torch.full((max(n, 1),), -7, dtype=torch.int32, device=dev)  # noqa: E731
+    counts = torch.zeros(4, dtype=torch.int32, device=dev)
+    r = Routing(tile_tokens, rows_cap, chunks_cap, z(rows_cap), z(chunks_cap), z(chunks_cap), z(chunks_cap),
+                counts[:2], torch.zeros(1, dtype=torch.int32, device=dev), z(chunks_cap + 2), z(M * topk))
+    heavy = {"chunk_expert": z(cap2), "chunk_row0": z(cap2), "chunk_rows": z(cap2), "counters": z(2), "cap": cap2}
+    _lib.check(L.b200moe_route_mixed(_ptr(ids), M, topk, num_experts, None, num_experts, tile_tokens, heavy_rows,
+                                     _ptr(r.sorted_ids), rows_cap, _ptr(r.chunk_expert), _ptr(r.chunk_row0),
+                                     _ptr(r.chunk_rows), chunks_cap, _ptr(heavy["chunk_expert"]),
+                                     _ptr(heavy["chunk_row0"]), _ptr(heavy["chunk_rows"]), cap2, _ptr(counts),
+                                     _ptr(r.slot_pos), _ptr(r.chunk_ready), _ptr(heavy["counters"]), _ptr(r.err),
+                                     _stream(dev)), "route_mixed")
+    return r, heavy, counts
+
+
 def gather_quant(hidden: torch.Tensor, topk: int, r: Routing):
     """-> (a_q (rows_cap, H) e4m3, a_sT (H/128, ld) f32) in sorted row order."""
     dev = _require_cuda(hidden)
@@ -311,6 +336,14 @@ class LayerPipeline:
         self.sorted_rows = 1 if self.tile > 64 else 0
         self.pair = torch.zeros(max(self.rows_cap if self.sorted_rows else numel, 1), H, dtype=torch.bfloat16,
                                 device=device)
+        # Mixed work lists (the C layer's rule): a skewed decode batch's heavy
+        # experts go through the token-major stages in the same step.
+        self.heavy_rows = 0 if (split or self.one_launch) else L.b200moe_heavy_rows(M, topk, self.tile)
+        if self.heavy_rows:
+            self.chunks_cap2 = L.b200moe_route_capacity_chunks(numel, self.E, 128)
+            self.ce2, self.cr02, self.crows2 = z(self.chunks_cap2), z(self.chunks_cap2), z(self.chunks_cap2)
+            self.counters2 = z(2)
+            self.counts = z(4)
         self.out = torch.zeros(M, H, dtype=torch.bfloat16, device=device)
         self.router = None
         if router is not None:
@@ -356,11 +389,19 @@ class LayerPipeline:
         cnt = _ptr(self.counts)
         rows = cnt + 4
         rec(0)
-        _lib.check(L.b200moe_route(_ptr(topk_ids), M, topk, self.num_experts, _ptr(self.expert_map), E, self.tile,
-                                   _ptr(self.sorted_ids), self.rows_cap, _ptr(self.ce), _ptr(self.cr0),
-                                   _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.slot_pos),
-                                   _ptr(self.ready), _ptr(self.rscratch), self.rscratch_ints, _ptr(self.err), st),
-                   "route")
+        if self.heavy_rows:
+            _lib.check(L.b200moe_route_mixed(_ptr(topk_ids), M, topk, self.num_experts, _ptr(self.expert_map), E,
+                                             self.tile, self.heavy_rows, _ptr(self.sorted_ids), self.rows_cap,
+                                             _ptr(self.ce), _ptr(self.cr0), _ptr(self.crows), self.chunks_cap,
+                                             _ptr(self.ce2), _ptr(self.cr02), _ptr(self.crows2), self.chunks_cap2,
+                                             cnt, _ptr(self.slot_pos), _ptr(self.ready), _ptr(self.counters2),
+                                             _ptr(self.err), st), "route_mixed")
+        else:
+            _lib.check(L.b200moe_route(_ptr(topk_ids), M, topk, self.num_experts, _ptr(self.expert_map), E, self.tile,
+                                       _ptr(self.sorted_ids), self.rows_cap, _ptr(self.ce), _ptr(self.cr0),
+                                       _ptr(self.crows), self.chunks_cap, cnt, rows, _ptr(self.slot_pos),
+                                       _ptr(self.ready), _ptr(self.rscratch), self.rscratch_ints, _ptr(self.err), st),
+                       "route")
         rec(1)
         return self._after_route(hidden, topk_weights, w13, w13_scale, w2, w2_scale, rec, grid_ctas)
 
@@ -389,6 +430,13 @@ class LayerPipeline:
                                          self.tile, _ptr(self.a2), _ptr(self.a2s), _ptr(self.sorted_ids),
                                          _ptr(topk_weights), M, topk, _ptr(self.pair), _ptr(self.err), grid_ctas,
                                          st), "experts")
+            if self.heavy_rows:
+                _lib.check(L.b200moe_experts_heavy(_ptr(self.a1), _ptr(self.a1s), self.ld, self.rows_cap, _ptr(w13),
+                                                   _ptr(w13_scale), _ptr(w2), _ptr(w2_scale), E, H, I,
+                                                   _ptr(self.ce2), _ptr(self.cr02), _ptr(self.crows2), cnt + 8,
+                                                   self.chunks_cap2, _ptr(self.counters2), _ptr(self.a2),
+                                                   _ptr(self.a2s), _ptr(self.sorted_ids), _ptr(topk_weights), M, topk,
+                                                   _ptr(self.pair), _ptr(self.err), grid_ctas, st), "experts_heavy")
             rec(3)
             _lib.check(L.b200moe_combine_reduce(_ptr(self.pair), _ptr(self.slot_pos), self.sorted_rows, M, topk, H,
                                                 _ptr(self.out), st),
