@@ -257,20 +257,23 @@ __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs
   align_body<false>(a, sm);
 }
 
-// Router + routing of small batches in one launch: warp w of CTA c routes
-// token 32c + w and stores its ids and weights (a.topk_ids = r.out_ids); the
-// last CTA to finish (a counter, left at zero again) routes every id as
-// align_kernel does, reading the ids the other CTAs stored through L2.
+// Router + routing of small batches in one launch: warp w < tpc of CTA c
+// routes token tpc*c + w and stores its ids and weights (a.topk_ids =
+// r.out_ids); the last CTA to finish (a counter, left at zero again) routes
+// every id as align_kernel does, reading the ids the other CTAs stored
+// through L2. Few tokens per CTA (one up to 128 tokens) spread the router's
+// per-token work over many SMs.
+template <int PER>
 __global__ void __launch_bounds__(kRouteThreads, 1) router_align_kernel(const AlignArgs a, const RouterArgs r,
-                                                                       int64_t M, int32_t* counter) {
+                                                                       int64_t M, int tpc, int32_t* counter) {
   extern __shared__ int32_t sm[];
   __shared__ int last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t t = (int64_t)blockIdx.x * kRouteWarps + warp;
-  if (t < M) {
+  const int64_t t = (int64_t)blockIdx.x * tpc + warp;
+  if (warp < tpc && t < M) {
     int id;
     float w;
-    route_token_warp(r, t, lane, id, w);
+    route_token_warp<PER>(r, t, lane, id, w);
   }
   __threadfence();
   __syncthreads();
@@ -349,7 +352,7 @@ __device__ __forceinline__ void cta_segment(const AlignArgs& a, int64_t& beg, in
 
 // ROUTER: the CTA first routes the tokens of its segment (a.seg_align = topk,
 // a.topk_ids = r.out_ids) and counts the ids it just stored.
-template <bool ROUTER>
+template <bool ROUTER, int PER>
 __global__ void __launch_bounds__(kRouteThreads, 1) route_count_kernel(const AlignArgs a, int32_t* scratch,
                                                                       const RouterArgs r) {
   extern __shared__ int32_t sm[];
@@ -368,7 +371,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_count_kernel(const Ali
     for (int64_t t = beg / r.topk + (tid >> 5); t < end / r.topk; t += kRouteWarps) {
       int id;
       float w;
-      route_token_warp(r, t, lane, id, w);
+      route_token_warp<PER>(r, t, lane, id, w);
     }
   }
   __syncthreads();
@@ -539,17 +542,17 @@ int64_t route_scratch_ints(int64_t n, int E) {
 
 namespace {
 
-template <bool ROUTER>
+template <bool ROUTER, int PER>
 cudaError_t launch_route_multi(const AlignArgs& a, const RouterArgs& r, int C, int32_t* scratch,
                                cudaStream_t stream) {
   const size_t smem1 = (size_t)kRouteWarps * a.E * sizeof(int32_t);
   const size_t smem2 = (size_t)(kRouteWarps * a.E + 5 * a.E + 2) * sizeof(int32_t);
-  cudaError_t err =
-      cudaFuncSetAttribute(route_count_kernel<ROUTER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+  cudaError_t err = cudaFuncSetAttribute(route_count_kernel<ROUTER, PER>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
   if (err == cudaSuccess)
     err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
   if (err != cudaSuccess) return err;
-  route_count_kernel<ROUTER><<<C, kRouteThreads, smem1, stream>>>(a, scratch, r);
+  route_count_kernel<ROUTER, PER><<<C, kRouteThreads, smem1, stream>>>(a, scratch, r);
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   route_scatter_kernel<<<C, kRouteThreads, smem2, stream>>>(a, scratch);
@@ -562,7 +565,7 @@ cudaError_t launch_route(const AlignArgs& a, int32_t* scratch, int64_t scratch_i
   const int C = route_ctas(a.n);
   // mixed work lists are built by the one-CTA kernel only
   if (C == 1 || a.heavy_rows > 0 || !scratch || scratch_ints < (int64_t)C * a.E) return launch_align(a, stream);
-  return launch_route_multi<false>(a, RouterArgs{}, C, scratch, stream);
+  return launch_route_multi<false, 8>(a, RouterArgs{}, C, scratch, stream);
 }
 
 int64_t route_logits_scratch_ints(int64_t n, int E) { return kRouteLogitsCounterInts + route_scratch_ints(n, E); }
@@ -573,13 +576,21 @@ cudaError_t launch_route_logits(const AlignArgs& a_in, const RouterArgs& r, int6
   a.topk_ids = r.out_ids;
   a.seg_align = r.topk;
   const int C = route_ctas(a.n);
-  if (C > 1 && a.heavy_rows == 0) return launch_route_multi<true>(a, r, C, counts, stream);
+  const int per = router_per_lane(r.E);
+  if (C > 1 && a.heavy_rows == 0) {
+    if (per == 8) return launch_route_multi<true, 8>(a, r, C, counts, stream);
+    if (per == 16) return launch_route_multi<true, 16>(a, r, C, counts, stream);
+    return launch_route_multi<true, 32>(a, r, C, counts, stream);
+  }
   const size_t smem = align_smem_bytes(a.E);
-  cudaError_t err =
-      cudaFuncSetAttribute(router_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // tokens per CTA: one up to 128 tokens, then as many as keep 128 CTAs (at most 32)
+  int tpc = M <= 128 ? 1 : (int)((M + 127) / 128);
+  if (tpc > kRouteWarps) tpc = kRouteWarps;
+  const int64_t ctas = M > 0 ? (M + tpc - 1) / tpc : 1;
+  auto kernel = per == 8 ? router_align_kernel<8> : (per == 16 ? router_align_kernel<16> : router_align_kernel<32>);
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  const int64_t ctas = M > 0 ? (M + kRouteWarps - 1) / kRouteWarps : 1;
-  router_align_kernel<<<(unsigned)ctas, kRouteThreads, smem, stream>>>(a, r, M, counter);
+  kernel<<<(unsigned)ctas, kRouteThreads, smem, stream>>>(a, r, M, tpc, counter);
   return cudaGetLastError();
 }
 

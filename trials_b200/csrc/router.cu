@@ -11,13 +11,14 @@ namespace {
 
 constexpr int kRouterWarps = 4;
 
+template <int PER>
 __global__ void __launch_bounds__(kRouterWarps * 32) router_topk_kernel(const RouterArgs r, int64_t M) {
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
   if (t >= M) return;
   int id;
   float w;
-  route_token_warp(r, t, lane, id, w);
+  route_token_warp<PER>(r, t, lane, id, w);
 }
 
 }  // namespace
@@ -28,7 +29,16 @@ cudaError_t launch_router_topk(const void* logits, int bf16, int64_t M, int E, i
   if (M <= 0) return cudaSuccess;
   const unsigned blocks = (unsigned)((M + kRouterWarps - 1) / kRouterWarps);
   const RouterArgs r{logits, bf16, E, topk, scoring, renormalize, bias, scaling, out_w, out_ids};
-  router_topk_kernel<<<blocks, kRouterWarps * 32, 0, stream>>>(r, M);
+  switch (router_per_lane(E)) {
+    case 8:
+      router_topk_kernel<8><<<blocks, kRouterWarps * 32, 0, stream>>>(r, M);
+      break;
+    case 16:
+      router_topk_kernel<16><<<blocks, kRouterWarps * 32, 0, stream>>>(r, M);
+      break;
+    default:
+      router_topk_kernel<32><<<blocks, kRouterWarps * 32, 0, stream>>>(r, M);
+  }
   return cudaGetLastError();
 }
 

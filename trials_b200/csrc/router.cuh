@@ -20,8 +20,7 @@
 
 namespace b200moe {
 
-constexpr int kRouterMaxPerLane = 32;  // E <= 1024
-constexpr int kRouterMaxTopk = 16;
+constexpr int kRouterMaxTopk = 16;  // E <= 1024 (32 values per lane)
 
 struct RouterArgs {
   const void* logits;  // (M, E) f32, or bf16 when bf16 != 0
@@ -39,37 +38,40 @@ __device__ __forceinline__ float router_logit(const RouterArgs& r, int64_t t, in
 }
 
 // Warp-wide: routes token t; lane j < topk returns the j-th id and weight and
-// also stores them to r.out_ids / r.out_w. All 32 lanes must call it.
+// also stores them to r.out_ids / r.out_w. All 32 lanes must call it. PER =
+// values per lane (expert e = lane + 32 i, i < PER): 8 for E <= 256, 16 for
+// E <= 512, 32 for E <= 1024 (router_per_lane), so the logits stay in
+// registers; the selected id and weight of round k stay in lane k.
+template <int PER>
 __device__ __forceinline__ void route_token_warp(const RouterArgs& r, int64_t t, int lane, int& id_out,
                                                  float& w_out) {
   const int E = r.E, topk = r.topk;
-  const int per = (E + 31) / 32;  // values per lane: expert e = lane + 32 * i
-  float x[kRouterMaxPerLane], sel[kRouterMaxPerLane];
+  float x[PER], sel[PER];
 #pragma unroll
-  for (int i = 0; i < kRouterMaxPerLane; ++i) {
+  for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
-    x[i] = (i < per && e < E) ? router_logit(r, t, e) : -INFINITY;
+    x[i] = e < E ? router_logit(r, t, e) : -INFINITY;
   }
   float denom = 1.f, xmax = 0.f;
   if (r.scoring == 0) {
     float m = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kRouterMaxPerLane; ++i) m = fmaxf(m, x[i]);
+    for (int i = 0; i < PER; ++i) m = fmaxf(m, x[i]);
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float sum = 0.f;
 #pragma unroll
-    for (int i = 0; i < kRouterMaxPerLane; ++i)
-      if (i < per && lane + 32 * i < E) sum += expf(x[i] - m);
+    for (int i = 0; i < PER; ++i)
+      if (lane + 32 * i < E) sum += expf(x[i] - m);
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     denom = sum;
     xmax = m;
   }
 #pragma unroll
-  for (int i = 0; i < kRouterMaxPerLane; ++i) {
+  for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
-    if (i < per && e < E) {
+    if (e < E) {
       if (r.scoring == 0) {
         sel[i] = x[i];  // softmax is monotone in the logit
       } else {
@@ -81,17 +83,14 @@ __device__ __forceinline__ void route_token_warp(const RouterArgs& r, int64_t t,
       sel[i] = -INFINITY;
     }
   }
-  float wsum = 0.f;
-  float wk[kRouterMaxTopk];
-  int idk[kRouterMaxTopk];
-#pragma unroll
-  for (int k = 0; k < kRouterMaxTopk; ++k) {
-    if (k >= topk) break;
+  float wsum = 0.f, my_w = 0.f;
+  int my_id = 0;
+  for (int k = 0; k < topk; ++k) {
     // lane-local best, then warp argmax (larger value, then lower id)
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
-    for (int i = 0; i < kRouterMaxPerLane; ++i) {
+    for (int i = 0; i < PER; ++i) {
       const int e = lane + 32 * i;
       if (sel[i] > bv || (sel[i] == bv && e < bi && sel[i] != -INFINITY)) {
         bv = sel[i];
@@ -112,31 +111,32 @@ __device__ __forceinline__ void route_token_warp(const RouterArgs& r, int64_t t,
     if ((bi & 31) == lane) {
       const int i = bi >> 5;
 #pragma unroll
-      for (int ii = 0; ii < kRouterMaxPerLane; ++ii)
+      for (int ii = 0; ii < PER; ++ii)
         if (ii == i) {
           w = r.scoring == 0 ? expf(x[ii] - xmax) / denom : x[ii];
           sel[ii] = -INFINITY;
         }
     }
     w = __shfl_sync(0xffffffffu, w, bi & 31);
-    wk[k] = w;
-    idk[k] = bi;
+    if (lane == k) {
+      my_w = w;
+      my_id = bi;
+    }
     wsum += w;
   }
   id_out = 0;
   w_out = 0.f;
   if (lane < topk) {
-#pragma unroll
-    for (int k = 0; k < kRouterMaxTopk; ++k)
-      if (k == lane) {
-        w_out = wk[k];
-        id_out = idk[k];
-      }
+    w_out = my_w;
+    id_out = my_id;
     if (r.renormalize) w_out = w_out / wsum;
     w_out *= r.scaling;
     r.out_w[t * topk + lane] = w_out;
     r.out_ids[t * topk + lane] = id_out;
   }
 }
+
+// Values per lane for E experts (see route_token_warp).
+__host__ __device__ __forceinline__ int router_per_lane(int E) { return E <= 256 ? 8 : (E <= 512 ? 16 : 32); }
 
 }  // namespace b200moe
