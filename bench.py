@@ -681,8 +681,7 @@ def run_sweep(args, shape, L, dev, clocks, peak):
                      "layer_hbm_gbs": layer_bytes(synth.glm(M), active, pairs) / (ms / 1e3) / 1e9,
                      "stage_ms": stage_ms, "roofline": roof, "device_error": err,
                      "heavy_experts_list": bool(pipe.heavy_rows),
-                     "gpu_launches": (len(pipe.stages) + (1 if pipe.tile > 64 else 0) +
-                                      (1 if pipe.rscratch_ints > 0 else 0) + (2 if pipe.heavy_rows else 0)) * steps})
+                     "gpu_launches": pipe.launches * steps})
         del pipe, h, tw, ids
         torch.cuda.empty_cache()
     return {"steps": args.sweep_steps, "warmup": 3, "records": recs, "clocks": clocks.summary("sweep"),
@@ -738,12 +737,85 @@ def run_router_record(args, shape, L, dev, clocks):
             clocks.window(t0, clocks.mark(), "sweep")
             best[name] = min(best[name], start.elapsed_time(end) / args.sweep_steps)
     for name, _, router_launches in forms:
-        launches = router_launches + len(sep.stages) + (1 if sep.tile > 64 else 0) + (1 if sep.rscratch_ints > 0 else 0)
+        launches = router_launches + sep.launches
         rec[name] = {"ms_per_step": best[name], "gpu_launches_per_step": launches, "steps": args.sweep_steps}
     rec["bit_equal"] = bool(torch.equal(separate(), fused()) and torch.equal(fus.topk_ids, moe.select_experts(
         logits, shape.topk, "sigmoid", bias, True, 2.5)[1]))
     rec["device_error"] = int(sep.err.item()) | int(fus.err.item())
     return rec
+
+
+def run_whole_record(args, shape, L, dev, clocks):
+    """The layer call (b200moe_layer) as one cooperative launch (routing,
+    gather, both GEMM stages, top-k reduce) against the default separate
+    launches, at 1, 64 and 128 tokens on the same weights. Each form is a CUDA
+    graph of 10 calls (no host work timed); the forms alternate over 8 rounds
+    of 3 replays; the record has each form's median step time, the launches
+    per call and whether the outputs are equal bit for bit."""
+    import statistics
+
+    import torch
+
+    from trials_b200 import _lib
+
+    lib = _lib.lib()
+    st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    recs = []
+    prev = lib.b200moe_set_layer_launch(0)
+    try:
+        for M in (1, 64, 128):
+            hidden, tw, ids = layer_inputs(shape, M, 0, args.seed + 5000 + M, dev)
+            n = lib.b200moe_layer_workspace_size(M, shape.H, shape.I, shape.E, 0, shape.topk)
+            forms = {1: "one_launch", 2: "separate"}
+            ws = {m: torch.zeros(n, dtype=torch.uint8, device=dev) for m in forms}
+            out = {m: torch.empty(M, shape.H, dtype=torch.bfloat16, device=dev) for m in forms}
+
+            def call(m):
+                _lib.check(lib.b200moe_layer(hidden.data_ptr(), M, shape.H, shape.I, shape.E, shape.topk,
+                                             L.w13.data_ptr(), L.w13_scale.data_ptr(), L.w2.data_ptr(),
+                                             L.w2_scale.data_ptr(), tw.data_ptr(), ids.data_ptr(), None, 0,
+                                             out[m].data_ptr(), ws[m].data_ptr(), ws[m].numel(), st()), "layer")
+
+            graphs, launches = {}, {}
+            for m in forms:
+                lib.b200moe_set_layer_launch(m)
+                launches[m] = lib.b200moe_layer_launches(M, shape.H, shape.I, shape.E, 0, shape.topk)
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    for _ in range(3):
+                        call(m)
+                torch.cuda.current_stream().wait_stream(side)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for _ in range(10):
+                        call(m)
+                graphs[m] = g
+            times = {m: [] for m in forms}
+            for rnd in range(8):
+                for m in ((1, 2) if rnd % 2 == 0 else (2, 1)):
+                    graphs[m].replay()
+                    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    t0 = clocks.mark()
+                    start.record()
+                    for _ in range(3):
+                        graphs[m].replay()
+                    end.record()
+                    torch.cuda.synchronize()
+                    clocks.window(t0, clocks.mark(), "sweep")
+                    times[m].append(start.elapsed_time(end) / 30)
+            del graphs
+            errs = [int(ws[m][:4].view(torch.int32).item()) for m in forms]
+            rec = {"tokens": M, "bit_equal": bool(torch.equal(out[1], out[2])), "device_error": errs[0] | errs[1]}
+            for m, name in forms.items():
+                rec[name] = {"ms_per_step": statistics.median(times[m]), "gpu_launches_per_step": launches[m]}
+            rec["one_launch_over_separate"] = statistics.median([a / b for a, b in zip(times[1], times[2])])
+            recs.append(rec)
+    finally:
+        lib.b200moe_set_layer_launch(prev)
+    return {"workload": "glm_decode_layer_call_one_launch_vs_separate",
+            "timing": "CUDA graphs of 10 calls per form, 8 alternating rounds of 3 replays, medians",
+            "default": "separate launches (b200moe_set_layer_launch(0))", "points": recs}
 
 
 def run_ours(args, shape, config):
@@ -828,8 +900,10 @@ def run_ours(args, shape, config):
     sweep = None
     if ws == 1 and not args.no_sweep:
         router_rec = run_router_record(args, shape, L, dev, clocks)  # before the power-capped prefill points
+        whole_rec = run_whole_record(args, shape, L, dev, clocks)
         sweep = run_sweep(args, shape, L, dev, clocks, peak)
         sweep["router_fused"] = router_rec
+        sweep["one_launch_layer"] = whole_rec
     clk = clocks.stop()
 
     # ---- CPU baseline (rank 0, one GPU only), with the GPU layer on the same sample
@@ -858,9 +932,7 @@ def run_ours(args, shape, config):
             stage_ms["gemm1_silu"]
         traffic_name = f"gemm1_silu_glm_decode_m{shape.M}{hot}"
     achieved = k_bytes / (k_ms / 1e3) / 1e9
-    launches = (len(pipe.stages) + (1 if not args.split and pipe.tile > 64 else 0) +
-                (1 if pipe.rscratch_ints > 0 else 0) +  # routing on several CTAs: two launches
-                (2 if pipe.heavy_rows else 0))          # the token-major stages of the heavy-expert list
+    launches = pipe.launches
     step_bytes = layer_bytes(shape, active, pairs)
     roof = {"kernel": k_name, "bound": "hbm", "achieved": achieved,
             "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -133,7 +133,15 @@ B200MOE_API int b200moe_quant_block128(const void* w, int64_t E, int64_t N, int6
  * slots whose id is -1 or maps to -1 contribute nothing.
  * Requirements: H % 256 == 0, I % 128 == 0, num_experts <= 1024.
  * workspace: b200moe_layer_workspace_size() bytes, 256-byte aligned; its first
- * 4 bytes are the device error word and must be zeroed once by the caller.
+ * 256 bytes (the device error word, then counters that every call leaves at
+ * zero) must be zeroed once by the caller, and again after a call reported
+ * B200MOE_DEVERR_TIMEOUT.
+ * Launches: 4 to 7 (routing, gather + quantise, both GEMM stages, top-k
+ * reduce). Small batches (tiles of 16..64 tokens, fewer than 16,384 routed
+ * slots, no mixed work lists) can instead run the whole layer as ONE
+ * cooperative launch (the reference's deferred single-launch layer,
+ * phase8_findings.md:77-81), same results bit for bit:
+ * b200moe_set_layer_launch / b200moe_layer_launches below.
  * No host synchronisation: the call can be captured in a CUDA graph.
  * ---------------------------------------------------------------------- */
 B200MOE_API size_t b200moe_layer_workspace_size(int64_t M, int64_t H, int64_t I, int num_experts, int num_local_experts,
@@ -142,6 +150,18 @@ B200MOE_API int b200moe_layer(const void* hidden, int64_t M, int64_t H, int64_t 
                   const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
                   const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map,
                   int num_local_experts, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Launch policy of b200moe_layer, b200moe_layer_logits and
+ * b200moe_layer_quantized (process-wide): 0 (default) = the form measured
+ * faster for the shape (so far the separate launches for every shape: the
+ * one-launch layer measured 3-4% slower on the GLM decode layer), 1 = the
+ * whole layer in one launch wherever it applies, 2 = never. Returns the
+ * previous mode, or B200MOE_ERR_INVALID_ARG. */
+B200MOE_API int b200moe_set_layer_launch(int mode);
+/* Kernel launches one call of those entry points makes for this shape under
+ * the current policy (1 = the whole-layer launch); 0 for an empty batch. */
+B200MOE_API int b200moe_layer_launches(int64_t M, int64_t H, int64_t I, int num_experts, int num_local_experts,
+                                       int topk);
 
 /* Same layer starting from the router: router_logits (M, num_experts) f32
  * (logits_bf16 = 0) or bf16 (1) go through the router of b200moe_router_topk

@@ -167,3 +167,33 @@ def test_peer_wait_limit_setting():
     assert L.b200moe_ep_peer_wait_limit_us(10**12) == 20_000      # clamped to 60 s
     assert L.b200moe_ep_peer_wait_limit_us(default) == 60_000_000
     assert L.b200moe_ep_peer_wait_limit_us(0) == default
+
+
+def test_layer_launch_policy():
+    """The whole layer in one launch where it applies (tiles of 16..64, one-CTA
+    routing, no mixed lists) under policy 1; separate launches under the
+    default policy (measured faster) and policy 2."""
+    L = _lib.lib()
+    H, I, E, k = 6144, 2048, 256, 8
+    prev = L.b200moe_set_layer_launch(0)
+    try:
+        assert L.b200moe_layer_launches(64, H, I, E, 0, k) == 4
+        assert L.b200moe_layer_launches(1, H, I, E, 0, k) == 4
+        assert L.b200moe_layer_launches(128, H, I, E, 0, k) == 4
+        # above 128 tokens: mixed work lists (route, gather, experts, 2 heavy stages, reduce)
+        assert L.b200moe_layer_launches(256, H, I, E, 0, k) == 6
+        # prefill: two routing launches, gather, two token-major stages, reduce
+        assert L.b200moe_layer_launches(8192, H, I, E, 0, k) == 6
+        assert L.b200moe_layer_launches(0, H, I, E, 0, k) == 0
+        assert L.b200moe_set_layer_launch(2) == 0
+        assert L.b200moe_layer_launches(64, H, I, E, 0, k) == 4
+        assert L.b200moe_set_layer_launch(1) == 2
+        assert L.b200moe_layer_launches(64, H, I, E, 0, k) == 1
+        assert L.b200moe_layer_launches(1, H, I, E, 0, k) == 1
+        assert L.b200moe_layer_launches(128, H, I, E, 0, k) == 1
+        assert L.b200moe_layer_launches(256, H, I, E, 0, k) == 6  # mixed lists: not applicable
+        assert L.b200moe_layer_launches(8192, H, I, E, 0, k) == 6  # not applicable: token-major tiles
+        assert L.b200moe_set_layer_launch(3) < 0
+        assert L.b200moe_set_layer_launch(-1) < 0
+    finally:
+        L.b200moe_set_layer_launch(prev)

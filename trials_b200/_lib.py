@@ -41,6 +41,8 @@ SIGNATURES = {
     "b200moe_quant_1x128": (_I, [_P, _L, _L, _L, _P, _L, _P, _L, _L, _P]),
     "b200moe_quant_block128": (_I, [_P, _L, _L, _L, _P, _P, _P]),
     "b200moe_layer_workspace_size": (_S, [_L, _L, _L, _I, _I, _I]),
+    "b200moe_set_layer_launch": (_I, [_I]),
+    "b200moe_layer_launches": (_I, [_L, _L, _L, _I, _I, _I]),
     "b200moe_layer": (_I, [_P, _L, _L, _L, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _S, _P]),
     "b200moe_layer_logits": (_I, [_P, _L, _L, _L, _I, _I, _P, _I, _I, _P, _I, ctypes.c_float, _P, _P, _P, _P, _P, _I,
                                   _P, _P, _P, _P, _S, _P]),

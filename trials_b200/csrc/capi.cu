@@ -127,6 +127,23 @@ int heavy_rows_for(int64_t M, int64_t numel, int tile) {
   return (tile <= 64 && M > kHeavyRows && route_ctas(numel) == 1) ? kHeavyRows : 0;
 }
 
+// The whole layer in one launch (the routing, the gather, both GEMM stages and
+// the top-k reduce: EPI_WHOLE) applies with tiles of 16..64 tokens, one-CTA
+// routing, no mixed lists and local results. Policy (b200moe_set_layer_launch):
+// 0 = the form measured faster, 1 = one launch wherever it applies, 2 = never.
+// Measured on the GLM layer (CUDA graphs, alternating): one launch 91 vs 83 us
+// at 1 token, 3-4% slower at 64 and 128 tokens. Its routing and gather phases
+// take 20 and 15 us inside the launch (one 352-thread CTA routes, on code and
+// rows fetched cold after the weight stream), against 9 and 7 us as launches
+// of their own; so the default (0) keeps the separate launches everywhere.
+std::atomic<int> g_layer_launch{0};
+constexpr int64_t kWholeAutoTokens = 0;  // batches up to this many tokens take one launch under policy 0
+bool whole_layer_for(int64_t M, int64_t numel, int tile, int heavy_rows, bool peer) {
+  const int mode = g_layer_launch.load();
+  if (mode == 2 || tile > 64 || heavy_rows > 0 || route_ctas(numel) != 1 || peer) return false;
+  return mode == 1 || M <= kWholeAutoTokens;
+}
+
 struct LayerPlan {
   int tile_tokens;
   int heavy_rows;  // > 0: mixed work lists (second list in off_ce2.., counters in off_ready2)
@@ -361,14 +378,13 @@ struct MixedLists {
   int32_t* counters;  // 2 ints, zeroed: the unit counters of the two token-major stages
 };
 
-// b200moe_route, and b200moe_route_logits when `router` is set (topk_ids then
-// names the router's id output, which routing reads after the router stored it).
-int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
+// The AlignArgs of one routing call, after the checks every routing entry
+// point shares.
+int make_align(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
                int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
                int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
-               int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
-               int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream,
-               const RouterArgs* router, int32_t* router_counter, const MixedLists* mixed = nullptr) {
+               int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready, int32_t* err_word,
+               const MixedLists* mixed, AlignArgs& a) {
   if (M < 0 || topk <= 0 || num_experts <= 0 || !valid_tile(tile_tokens) || !sorted_ids || !chunk_expert ||
       !chunk_row0 || !chunk_rows || !n_chunks || !num_rows || !err_word || (M > 0 && !topk_ids))
     return fail(B200MOE_ERR_INVALID_ARG, "b200moe_route: bad argument%s");
@@ -379,7 +395,7 @@ int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, co
   if (rows_capacity < b200moe_route_capacity_rows(numel, E) ||
       chunks_capacity < b200moe_route_capacity_chunks(numel, E, tile_tokens))
     return fail(B200MOE_ERR_WORKSPACE, "b200moe_route: capacity too small%s");
-  AlignArgs a{};
+  a = AlignArgs{};
   a.topk_ids = topk_ids;
   a.n = numel;
   a.num_experts = num_experts;
@@ -415,6 +431,24 @@ int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, co
     a.heavy_row0 = mixed->heavy_row0;
     a.counters2 = mixed->counters;
   }
+  return B200MOE_OK;
+}
+
+// b200moe_route, and b200moe_route_logits when `router` is set (topk_ids then
+// names the router's id output, which routing reads after the router stored it).
+int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, const int32_t* expert_map,
+               int num_local_experts, int tile_tokens, int32_t* sorted_ids, int64_t rows_capacity,
+               int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
+               int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
+               int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream,
+               const RouterArgs* router, int32_t* router_counter, const MixedLists* mixed = nullptr) {
+  AlignArgs a;
+  const int st = make_align(topk_ids, M, topk, num_experts, expert_map, num_local_experts, tile_tokens, sorted_ids,
+                            rows_capacity, chunk_expert, chunk_row0, chunk_rows, chunks_capacity, n_chunks, num_rows,
+                            slot_pos, chunk_ready, err_word, mixed, a);
+  if (st) return st;
+  const int E = a.E;
+  const int64_t numel = a.n;
   if (router) {
     // The CTA counter: router_counter, or the first ints of route_scratch.
     int32_t* counts = router_counter ? route_scratch : route_scratch + kRouteLogitsCounterInts;
@@ -791,6 +825,24 @@ int b200moe_combine_reduce(const void* out_pair, const int32_t* slot_pos, int so
                      "combine_reduce");
 }
 
+int b200moe_set_layer_launch(int mode) {
+  if (mode < 0 || mode > 2) return fail(B200MOE_ERR_INVALID_ARG, "b200moe_set_layer_launch: mode 0, 1 or 2%s");
+  return g_layer_launch.exchange(mode);
+}
+
+int b200moe_layer_launches(int64_t M, int64_t H, int64_t I, int num_experts, int num_local_experts, int topk) {
+  if (M <= 0 || H <= 0 || I <= 0 || topk <= 0 || num_experts <= 0) return 0;
+  const int E = num_local_experts > 0 ? num_local_experts : num_experts;
+  const LayerPlan pl = plan_layer(M, H, I, E, topk);
+  const int64_t numel = M * topk;
+  if (whole_layer_for(M, numel, pl.tile_tokens, pl.heavy_rows, false)) return 1;
+  int n = (route_ctas(numel) > 1 && pl.heavy_rows == 0) ? 2 : 1;  // routing (with the router from logits)
+  n += 1;                                                          // gather + quantise
+  n += pl.tile_tokens > 64 ? 2 : 1;                                // both GEMM stages
+  if (pl.heavy_rows) n += 2;                                       // the heavy list's token-major stages
+  return n + 1;                                                    // top-k reduce
+}
+
 size_t b200moe_layer_workspace_size(int64_t M, int64_t H, int64_t I, int num_experts, int num_local_experts,
                                     int topk) {
   if (M < 0 || H <= 0 || I <= 0 || topk <= 0) return 0;
@@ -811,6 +863,98 @@ struct LayerInput {
   const float* s;
   int64_t lds;
 };
+
+// The layer as one cooperative launch (EPI_WHOLE) on the workspace regions of
+// plan pl at wl: routing (after the router, when router is set) in one CTA
+// while the others wait, then the gather of the routed rows, both GEMM stages
+// and the top-k reduce (as b200moe_experts_fused). The launch's sync words are
+// ints 1..3 of the workspace header (int 1 is also the router counter of the
+// separate routing launch; every call leaves them zero).
+int whole_layer(const char* name, const LayerInput& in, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
+                const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
+                const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map, int E, void* out,
+                const LayerPlan& pl, uint8_t* wl, int32_t* err, const RouterArgs* router, void* stream) {
+  int32_t* sorted = reinterpret_cast<int32_t*>(wl + pl.off_sorted);
+  int32_t* pos = reinterpret_cast<int32_t*>(wl + pl.off_pos);
+  int32_t* ce = reinterpret_cast<int32_t*>(wl + pl.off_ce);
+  int32_t* cr0 = reinterpret_cast<int32_t*>(wl + pl.off_cr0);
+  int32_t* crows = reinterpret_cast<int32_t*>(wl + pl.off_crows);
+  int32_t* ready = reinterpret_cast<int32_t*>(wl + pl.off_ready);
+  int32_t* counts = reinterpret_cast<int32_t*>(wl + pl.off_counts);
+  uint8_t* a1 = wl + pl.off_a1;
+  float* a1s = reinterpret_cast<float*>(wl + pl.off_a1s);
+  uint8_t* a2 = wl + pl.off_a2;
+  float* a2s = reinterpret_cast<float*>(wl + pl.off_a2s);
+  __nv_bfloat16* pair = reinterpret_cast<__nv_bfloat16*>(wl + pl.off_pair);
+  if (!in.hidden && (!aligned16(in.q) || in.ldq % 16 != 0 || in.ldq < H || in.lds < H / 128 || !in.s))
+    return fail(B200MOE_ERR_UNSUPPORTED, "%s: fp8 rows must be 16-byte aligned with scales per row", name);
+  if (!aligned16(out) || (in.hidden && !aligned16(in.hidden)))
+    return fail(B200MOE_ERR_UNSUPPORTED, "%s: 16-byte alignment required", name);
+  GemmParams p1{}, p2{};
+  int st = make_align(router ? router->out_ids : topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens,
+                      sorted, pl.rows_cap, ce, cr0, crows, pl.chunks_cap, counts, counts + 1, pos, ready, err, nullptr,
+                      p1.ra);
+  if (st) return st;
+  CUtensorMap tw1, ta1, tw2, ta2;
+  st = prep_gemm(a1, a1s, pl.as_ld, pl.rows_cap, w13, w13_scale, E, 2 * I, H, ce, cr0, crows, counts,
+                 pl.tile_tokens, p1, tw1, ta1);
+  if (st) return st;
+  st = prep_gemm(a2, a2s, pl.as_ld, pl.rows_cap, w2, w2_scale, E, H, I, ce, cr0, crows, counts, pl.tile_tokens, p2,
+                 tw2, ta2);
+  if (st) return st;
+  p1.out_q = a2;
+  p1.out_q_ld = I;
+  p1.out_sT = a2s;
+  p1.out_s_ld = pl.as_ld;
+  p1.chunk_ready = ready;
+  p1.phase_count = ready + pl.chunks_cap;
+  p1.err = err;
+  p1.route_sync = err + 1;
+  if (router) {
+    p1.rr = *router;
+    p1.router = 1;
+  }
+  // gather: as b200moe_gather_quant / b200moe_gather_rows, slot positions
+  // read through L2 (the routing of this launch wrote them)
+  QuantArgs& g = p1.q0;
+  if (in.hidden) {
+    g.x = in.hidden;
+    g.ldx = H;
+  } else {
+    g.xq = in.q;
+    g.ldxq = in.ldq;
+    g.xs = in.s;
+    g.ldxs = in.lds;
+  }
+  g.K = H;
+  const bool fan = fan_out_tokens(M * topk, topk);
+  g.rows = fan ? M : M * topk;
+  g.fanout = fan ? 1 : 0;
+  g.slot_pos = pos;
+  g.topk = topk;
+  g.sentinel = (int32_t)(M * topk);
+  g.meta_l2 = 1;
+  g.q = a1;
+  g.ldq = H;
+  g.s = a1s;
+  g.s_row = 1;
+  g.s_grp = pl.as_ld;
+  p1.red_slot_pos = pos;
+  p1.red_out = static_cast<__nv_bfloat16*>(out);
+  p1.red_M = M;
+  p1.red_topk = topk;
+  p2.sorted_ids = sorted;
+  p2.topk_w = router ? router->out_w : topk_weights;
+  p2.sentinel = (int32_t)(M * topk);
+  p2.out_pair = pair;
+  p2.err = err;
+  const int64_t units_cap = pl.chunks_cap * ((2 * I) / 256 + H / 256);
+  int64_t grid = sm_count();
+  if (grid > units_cap) grid = units_cap;
+  return cuda_status(launch_grouped_gemm_fused(pl.tile_tokens, tw1, ta1, p1, tw2, ta2, p2, (int)grid,
+                                               (cudaStream_t)stream),
+                     name);
+}
 
 int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int64_t I, int num_experts, int topk,
                const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
@@ -854,6 +998,9 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   // workspace header (zeroed with the error word; every call leaves it zero).
   // Mixed work lists (decode batches with heavy experts): counts[2] = heavy
   // chunks, counts[3] = first heavy row.
+  if (whole_layer_for(M, M * topk, pl.tile_tokens, pl.heavy_rows, peer_out != nullptr))
+    return whole_layer(name, in, M, H, I, num_experts, topk, w13, w13_scale, w2, w2_scale, topk_weights, topk_ids,
+                       expert_map, E, out, pl, wl, err, router, stream);
   MixedLists mx{};
   if (pl.heavy_rows) {
     mx = MixedLists{pl.heavy_rows, reinterpret_cast<int32_t*>(wl + pl.off_ce2),

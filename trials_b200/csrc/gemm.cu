@@ -134,15 +134,18 @@ cudaError_t launch_grouped_gemm_fused(int tile_tokens, const CUtensorMap& tm_w1,
                                       const GemmParams& p1, const CUtensorMap& tm_w2, const CUtensorMap& tm_a2,
                                       const GemmParams& p2, int grid, cudaStream_t stream) {
   if (grid <= 0) return cudaSuccess;
-  const bool phases = p1.q0.rows > 0;
+  // routing in the launch (route_sync set), gather + reduce phases (q0.rows > 0), or neither
+  const int epi = p1.route_sync ? EPI_WHOLE : (p1.q0.rows > 0 ? EPI_LAYER : EPI_FUSED);
   switch (tile_tokens) {
     case 16:
     case 32:
-      return phases ? launch_cfg<32, 1, EPI_LAYER>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream)
-                    : launch_cfg<32, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
+      if (epi == EPI_WHOLE) return launch_cfg<32, 1, EPI_WHOLE>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
+      return epi == EPI_LAYER ? launch_cfg<32, 1, EPI_LAYER>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream)
+                              : launch_cfg<32, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
     case 64:
-      return phases ? launch_cfg<64, 1, EPI_LAYER>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream)
-                    : launch_cfg<64, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
+      if (epi == EPI_WHOLE) return launch_cfg<64, 1, EPI_WHOLE>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
+      return epi == EPI_LAYER ? launch_cfg<64, 1, EPI_LAYER>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream)
+                              : launch_cfg<64, 1, EPI_FUSED>(tm_w1, tm_a1, p1, tm_w2, tm_a2, p2, grid, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -92,6 +92,9 @@ struct QuantArgs {
   // With slot_pos: row r of the launch is token r instead (rows = M), written
   // to every one of its slots' rows slot_pos[r*topk + j] (topk <= 32).
   int fanout;
+  // slot_pos / sorted_ids were written earlier in the same launch: read them
+  // through L2 instead of the read-only path.
+  int meta_l2;
   int32_t sentinel;
   uint8_t* q;
   int64_t ldq;

@@ -35,14 +35,19 @@
 
 #include <cuda_fp8.h>
 
+#include "align.cuh"
 #include "common.cuh"
 #include "launch.h"
 #include "ptx.cuh"
+#include "router.cuh"
 #include "rowops.cuh"
 
 // Weight tiles stream once per launch. An evict_first L2 hint on them measured
 // slower than no hint on a pure TMA read stream (6.9 vs 7.0 TB/s) and no faster
-// in this kernel, so it is off unless this is set to 1.
+// in this kernel, so it is off unless this is set to 1 - except in the
+// whole-layer launch (EPI_WHOLE), whose routing and gather phases run on code
+// and rows that the previous call's weight stream would otherwise have evicted
+// from L2 (measured: one token, 114 -> 91 us per layer).
 #ifndef B200MOE_W_EVICT_FIRST
 #define B200MOE_W_EVICT_FIRST 0
 #endif
@@ -53,6 +58,7 @@
 #ifndef B200MOE_EPI_KR
 #define B200MOE_EPI_KR 2
 #endif
+
 // SiLU with the fast (2 ulp) division; 0 selects IEEE division.
 #ifndef B200MOE_FAST_SILU
 #define B200MOE_FAST_SILU 1
@@ -61,8 +67,9 @@
 namespace b200moe {
 
 // EPI_LAYER: EPI_FUSED plus the in-launch phases (gather + quantise first,
-// top-k reduce last) set up in GemmParams.q0 / red_*.
-enum { EPI_SILU = 0, EPI_COMBINE = 1, EPI_FUSED = 2, EPI_LAYER = 3 };
+// top-k reduce last) set up in GemmParams.q0 / red_*. EPI_WHOLE: EPI_LAYER
+// with the routing (and optionally the router) at the start of the launch.
+enum { EPI_SILU = 0, EPI_COMBINE = 1, EPI_FUSED = 2, EPI_LAYER = 3, EPI_WHOLE = 4 };
 
 struct GemmParams {
   // routing: chunk list produced by the route kernel (device memory)
@@ -107,6 +114,14 @@ struct GemmParams {
   // token-major kernels: a zeroed counter from which CTAs take their next unit
   // (dynamic queue); nullptr = static round-robin over the grid
   int32_t* unit_counter;
+  // EPI_WHOLE: the one-CTA routing run inside the launch (ra), after the
+  // router top-k of every token (rr, when router != 0; ra.topk_ids =
+  // rr.out_ids); route_sync: 3 ints that are zero between launches (router
+  // CTA counter, routing done, CTAs past the routing wait).
+  AlignArgs ra;
+  RouterArgs rr;
+  int router;
+  int32_t* route_sync;
   // diagnostics
   int32_t* err;
   uint64_t timeout_ns;
@@ -188,6 +203,17 @@ __device__ __forceinline__ int ld_acquire_gpu(const int32_t* ptr) {
   return v;
 }
 
+// Routing metadata (chunk lists, sorted ids, router weights): read-only for
+// the launch unless the launch wrote it itself (EPI_WHOLE), then through L2.
+template <bool COH>
+__device__ __forceinline__ int32_t ld_meta(const int32_t* ptr) {
+  return COH ? __ldcg(ptr) : __ldg(ptr);
+}
+template <bool COH>
+__device__ __forceinline__ float ld_meta(const float* ptr) {
+  return COH ? __ldcg(ptr) : __ldg(ptr);
+}
+
 // Waits until *counter >= target (bounded like every wait in this library);
 // then orders the following async-proxy (TMA) reads after the acquire.
 __device__ __forceinline__ bool wait_count_bounded(const int32_t* counter, int target, uint64_t limit_ns,
@@ -215,6 +241,67 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
   return true;
 }
 
+// EPI_WHOLE, first phase (every thread of every CTA). With a router, token t
+// is routed by warp t / G of CTA t % G (G CTAs) and the last CTA to finish its
+// tokens (counter sync[0]) runs the routing; without, CTA 0 does. The routing
+// CTA releases sync[1] = 1 and the others wait for it (bounded). Every CTA then
+// counts itself past (sync[2]); the last one clears sync[1..2] (every CTA is
+// past the wait by then), so the words are zero again for the next launch.
+// sm: shared memory for align_body. Returns false after a timeout.
+template <int NTHR>
+__device__ bool route_phase(const GemmParams& p, int32_t* sm, volatile int* abort_flag, volatile int* flag_sh) {
+  constexpr int NW = NTHR / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int32_t* sync = p.route_sync;
+  bool aligner = blockIdx.x == 0;
+  if (p.router) {
+    const int64_t M = p.ra.n / p.rr.topk;
+    const int per = router_per_lane(p.rr.E);
+    for (int64_t t = blockIdx.x + (int64_t)gridDim.x * warp; t < M; t += (int64_t)gridDim.x * NW) {
+      int id;
+      float w;
+      if (per == 8) route_token_warp<8>(p.rr, t, lane, id, w);
+      else if (per == 16) route_token_warp<16>(p.rr, t, lane, id, w);
+      else route_token_warp<32>(p.rr, t, lane, id, w);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const bool last = atomicAdd(&sync[0], 1) == (int)gridDim.x - 1;
+      if (last) {
+        sync[0] = 0;
+        __threadfence();
+      }
+      *flag_sh = last ? 1 : 0;
+    }
+    __syncthreads();
+    aligner = *flag_sh != 0;
+  }
+  if (aligner) {
+    if (p.router) align_body<true, NTHR>(p.ra, sm);
+    else align_body<false, NTHR>(p.ra, sm);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(&sync[1]), "r"(1) : "memory");
+    }
+  } else if (threadIdx.x == 0) {
+    if (!wait_count_bounded(&sync[1], 1, p.timeout_ns, abort_flag)) {
+      atomicOr(p.err, ERR_DEV_TIMEOUT);
+      *abort_flag = 1;
+    }
+  }
+  if (threadIdx.x == 0 && atomicAdd(&sync[2], 1) == (int)gridDim.x - 1) {
+    sync[1] = 0;
+    sync[2] = 0;
+  }
+  // The routing's shared memory becomes the TMA ring: order its generic
+  // writes before the async-proxy writes and reads that follow.
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncthreads();
+  return *abort_flag == 0;
+}
+
 // The kernel runs one stage (EPI_SILU / EPI_COMBINE: parameters p, tensor
 // maps tm_w / tm_a; the *2 copies are unused) or both (EPI_FUSED): units
 // [0, n1) are stage-1 units with p, units [n1, n1 + n2) stage-2 units with
@@ -233,8 +320,9 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
                             const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ GemmParams p2) {
   using C = GemmCfg<T, CS>;
   constexpr int EW = C::EW;
-  constexpr bool FUSED = EPI == EPI_FUSED || EPI == EPI_LAYER;
-  constexpr bool PHASES = EPI == EPI_LAYER;
+  constexpr bool FUSED = EPI >= EPI_FUSED;
+  constexpr bool PHASES = EPI >= EPI_LAYER;
+  constexpr bool ROUTE = EPI == EPI_WHOLE;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled TMA tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -256,6 +344,8 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
   // EPI_FUSED hand-off of finished stage-1 units to the publisher warp:
   // pub[0..1] filled by the epilogue warps, pub[2..3] released by the publisher.
   uint64_t* pub = reinterpret_cast<uint64_t*>(tmem_slot + 4);
+  // EPI_WHOLE: which CTA routes (broadcast from thread 0).
+  volatile int* route_sh = reinterpret_cast<volatile int*>(tmem_slot + 3);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -301,7 +391,17 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int n_chunks = *p.n_chunks;
+  int n_chunks;
+  if constexpr (ROUTE) {
+    // The routing writes the work list the rest of the launch reads; the
+    // tile ring is free until the producer starts.
+    static_assert(align_smem_ints(1024, (C::THREADS + 32) / 32) * 4 <= C::NSTAGE * C::TILE_BYTES,
+                  "routing shared memory");
+    const bool routed = route_phase<C::THREADS + 32>(p, reinterpret_cast<int32_t*>(tiles), abort_flag, route_sh);
+    n_chunks = routed ? __ldcg(p.n_chunks) : 0;
+  } else {
+    n_chunks = *p.n_chunks;
+  }
   const int n1 = n_chunks * NT1;
   const int n_units = n1 + (FUSED ? n_chunks * NT2 : 0);
   // unit -> (stage 2?, chunk, weight-row tile)
@@ -326,8 +426,8 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
         bool s2;
         int c, nt;
         unit_of(u, s2, c, nt);
-        e_n = __ldg(&p.chunk_expert[c]);
-        p0_n = __ldg(&p.chunk_row0[c]);
+        e_n = ld_meta<ROUTE>(&p.chunk_expert[c]);
+        p0_n = ld_meta<ROUTE>(&p.chunk_row0[c]);
       };
       if (blockIdx.x < n_units) meta(blockIdx.x);
       // With phase 0 in the launch (EPI_FUSED, q0.rows > 0) the stage-1
@@ -378,11 +478,10 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
           }
           uint8_t* tile = tiles + stage * C::TILE_BYTES;
           mbar_arrive_expect_tx(&full[stage], C::TILE_BYTES);
-#if B200MOE_W_EVICT_FIRST
-          tma_load_2d(tile, tw, &full[stage], kb * 128, wrow, pol_w);
-#else
-          tma_load_2d(tile, tw, &full[stage], kb * 128, wrow);
-#endif
+          if (B200MOE_W_EVICT_FIRST || ROUTE)
+            tma_load_2d(tile, tw, &full[stage], kb * 128, wrow, pol_w);
+          else
+            tma_load_2d(tile, tw, &full[stage], kb * 128, wrow);
           if (a_ready) {
             tma_load_2d(tile + C::W_BYTES, ta, &full[stage], kb * 128, p0, pol_a);
             mbar_arrive_expect_tx(&sfull[slot], C::S_BYTES);
@@ -435,7 +534,7 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
         bool s2;
         int c, nt;
         unit_of(u, s2, c, nt);
-        return __ldg(&p.chunk_rows[c]);
+        return ld_meta<ROUTE>(&p.chunk_rows[c]);
       };
       int rows_n = blockIdx.x < n_units ? rows_of(blockIdx.x) : 0;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
@@ -534,9 +633,9 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
       bool s2;
       int c, nt;
       unit_of(blockIdx.x, s2, c, nt);
-      e_n = __ldg(&p.chunk_expert[c]);
-      p0_n = __ldg(&p.chunk_row0[c]);
-      rows_n = __ldg(&p.chunk_rows[c]);
+      e_n = ld_meta<ROUTE>(&p.chunk_expert[c]);
+      p0_n = ld_meta<ROUTE>(&p.chunk_row0[c]);
+      rows_n = ld_meta<ROUTE>(&p.chunk_rows[c]);
       load_ws(s2, e_n, nt);
     }
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -552,9 +651,9 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
       int cn = 0, ntn = 0;
       if (un < n_units) {
         unit_of(un, s2n, cn, ntn);
-        e_n = __ldg(&p.chunk_expert[cn]);
-        p0_n = __ldg(&p.chunk_row0[cn]);
-        rows_n = __ldg(&p.chunk_rows[cn]);
+        e_n = ld_meta<ROUTE>(&p.chunk_expert[cn]);
+        p0_n = ld_meta<ROUTE>(&p.chunk_row0[cn]);
+        rows_n = ld_meta<ROUTE>(&p.chunk_rows[cn]);
       }
 
       float acc[C::TC];
@@ -721,8 +820,8 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
           const int c = col0 + g * 32 + lane;
-          fl[g] = c < rows ? __ldg(&pc.sorted_ids[p0 + c]) : pc.sentinel;
-          wl[g] = fl[g] < pc.sentinel ? __ldg(&pc.topk_w[fl[g]]) : 0.f;
+          fl[g] = c < rows ? ld_meta<ROUTE>(&pc.sorted_ids[p0 + c]) : pc.sentinel;
+          wl[g] = fl[g] < pc.sentinel ? ld_meta<ROUTE>(&pc.topk_w[fl[g]]) : 0.f;
         }
         // Row f (the slot) of out_pair; one 64-byte store per column.
         __nv_bfloat16* dst = pc.out_pair + nt * C::UNIT_ROWS + hs * 128 + q * 32 + lane;

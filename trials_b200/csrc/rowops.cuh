@@ -12,6 +12,10 @@ namespace b200moe {
 constexpr int kQuantSegSteps = 4;
 constexpr int kQuantSegCols = 256 * kQuantSegSteps;
 
+__device__ __forceinline__ int32_t ld_index(const QuantArgs& a, const int32_t* p) {
+  return a.meta_l2 ? __ldcg(p) : __ldg(p);
+}
+
 // One warp: launch row `row` of `a` (see QuantArgs), columns seg0 .. seg0+1023.
 // Each lane converts 8 consecutive bf16 per 16-byte load, a half-warp covers
 // one 128-column group, and the warp issues the loads of its four 256-column
@@ -25,12 +29,12 @@ __device__ __forceinline__ void quant_row_segment(const QuantArgs& a, int64_t ro
   const bool fan = a.slot_pos && a.fanout;
   if (fan) {
     src = row;  // lane j holds the row of slot j; consumed after the loads are issued
-    pos = lane < a.topk ? __ldg(&a.slot_pos[row * a.topk + lane]) : -1;
+    pos = lane < a.topk ? ld_index(a, &a.slot_pos[row * a.topk + lane]) : -1;
   } else if (a.slot_pos) {
     src = row / a.topk;
-    pos = __ldg(&a.slot_pos[row]);  // consumed after the row's loads are issued
+    pos = ld_index(a, &a.slot_pos[row]);  // consumed after the row's loads are issued
   } else if (a.sorted_ids) {
-    const int f = __ldg(&a.sorted_ids[row]);
+    const int f = ld_index(a, &a.sorted_ids[row]);
     src = (f >= 0 && f < a.sentinel) ? (int64_t)(f / a.topk) : -1;
     // Padding rows are not written: a padding row only feeds its own MMA
     // column (or row), whose results no epilogue keeps.

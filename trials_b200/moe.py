@@ -51,8 +51,9 @@ def _require_cuda(*tensors: torch.Tensor) -> torch.device:
 
 class _Workspaces:
     """Grow-only per-(device, stream) workspace buffers. Their first 256 bytes
-    are zeroed at allocation: the device error word (int 0) and the router's
-    CTA counter of b200moe_layer_logits (int 1, left at zero by every call)."""
+    are zeroed at allocation: the device error word (int 0), then the router's
+    CTA counter and the whole-layer launch's sync words (ints 1..3, left at
+    zero by every call)."""
 
     def __init__(self):
         self._bufs = {}

@@ -289,20 +289,26 @@ def pick_tile_tokens(numel: int, num_local_experts: int) -> int:
 class LayerPipeline:
     """The launches of the layer on preallocated buffers, with optional CUDA
     events between stages (used by the benchmark to time each kernel on the
-    launching stream). Same kernels and order as b200moe_layer: route,
-    gather_quant, experts (both GEMM stages in one launch), combine_reduce;
-    with split=True the GEMM stages run as two launches instead."""
+    launching stream). Same kernels and order as b200moe_layer: where
+    b200moe_layer runs the whole layer as one launch (small batches, see
+    b200moe_set_layer_launch) the pipeline calls it (one stage, "layer");
+    otherwise route, gather_quant, experts (both GEMM stages in one launch),
+    combine_reduce; with split=True the GEMM stages run as two launches."""
 
-    LAYER_STAGES = ("route", "layer")  # small batches: everything after routing in one launch
+    WHOLE_STAGES = ("layer",)  # routing, gather, both GEMM stages and the reduce in one launch
+    LAYER_STAGES = ("route", "layer")  # everything after routing in one launch (b200moe_experts_fused)
     FUSED_STAGES = ("route", "gather_quant", "experts", "combine_reduce")
     SPLIT_STAGES = ("route", "gather_quant", "gemm1_silu", "gemm2_combine", "combine_reduce")
 
     def __init__(self, M: int, H: int, I: int, num_experts: int, topk: int, device, tile_tokens: int = 0,
                  expert_map: Optional[torch.Tensor] = None, num_local_experts: Optional[int] = None,
-                 split: bool = False, one_launch: Optional[bool] = None, router: Optional[dict] = None):
+                 split: bool = False, one_launch: Optional[bool] = None, router: Optional[dict] = None,
+                 whole: Optional[bool] = None):
         """router: {"scoring_func", "correction_bias", "renormalize",
         "routed_scaling_factor"} to run the layer from router logits
-        (run_from_logits: the router inside routing's first launch)."""
+        (run_from_logits: the router inside routing's first launch).
+        whole: None = the whole-layer launch where b200moe_layer uses it,
+        False = separate launches."""
         self.M, self.H, self.I, self.topk = M, H, I, topk
         self.num_experts = num_experts
         self.E = num_local_experts if expert_map is not None else num_experts
@@ -326,7 +332,10 @@ class LayerPipeline:
         # equal at 64 tokens and 24 us slower at 128 than the three launches.
         eligible = (not split) and self.tile <= 64 and M * topk < FAN_OUT_MIN_PAIRS
         self.one_launch = bool(one_launch) and eligible
-        self.stages = self.SPLIT_STAGES if split else (self.LAYER_STAGES if self.one_launch else self.FUSED_STAGES)
+        self.whole = (not split and not self.one_launch and whole is not False and
+                      L.b200moe_layer_launches(M, H, I, num_experts, self.E, topk) == 1)
+        self.stages = self.SPLIT_STAGES if split else (
+            self.WHOLE_STAGES if self.whole else (self.LAYER_STAGES if self.one_launch else self.FUSED_STAGES))
         self.counts = z(2)
         self.err = z(1)
         self.a1 = torch.zeros(self.rows_cap, H, dtype=FP8, device=device)
@@ -338,13 +347,19 @@ class LayerPipeline:
                                 device=device)
         # Mixed work lists (the C layer's rule): a skewed decode batch's heavy
         # experts go through the token-major stages in the same step.
-        self.heavy_rows = 0 if (split or self.one_launch) else L.b200moe_heavy_rows(M, topk, self.tile)
+        self.heavy_rows = 0 if (split or self.one_launch or self.whole) else L.b200moe_heavy_rows(M, topk, self.tile)
         if self.heavy_rows:
             self.chunks_cap2 = L.b200moe_route_capacity_chunks(numel, self.E, 128)
             self.ce2, self.cr02, self.crows2 = z(self.chunks_cap2), z(self.chunks_cap2), z(self.chunks_cap2)
             self.counters2 = z(2)
             self.counts = z(4)
         self.out = torch.zeros(M, H, dtype=torch.bfloat16, device=device)
+        if self.whole:
+            # b200moe_layer's workspace: header zeroed (error word, counters
+            # every call leaves at zero); the error word is self.err
+            self.ws = torch.zeros(L.b200moe_layer_workspace_size(M, H, I, num_experts, self.E, topk),
+                                  dtype=torch.uint8, device=device)
+            self.err = self.ws[:4].view(torch.int32)
         self.router = None
         if router is not None:
             r = dict(router)
@@ -356,6 +371,14 @@ class LayerPipeline:
             self.topk_ids = torch.zeros(M, topk, dtype=torch.int32, device=device)
             self.lscratch_ints = L.b200moe_route_logits_scratch_ints(numel, self.E)
             self.lscratch = z(self.lscratch_ints)  # zeroed: its first int is the router's CTA counter
+
+    @property
+    def launches(self) -> int:
+        """Kernel launches per run() (run_from_logits: the same)."""
+        if self.whole:
+            return 1
+        return (len(self.stages) + (1 if not self.split and self.tile > 64 else 0) +
+                (1 if self.rscratch_ints > 0 and not self.heavy_rows else 0) + (2 if self.heavy_rows else 0))
 
     def run_from_logits(self, hidden, logits, w13, w13_scale, w2, w2_scale, events=None, grid_ctas: int = 0):
         """The layer from router logits: b200moe_route_logits (router + routing),
@@ -370,6 +393,15 @@ class LayerPipeline:
         scoring, bias, renorm, scale = self.router
         cnt = _ptr(self.counts)
         rec(0)
+        if self.whole:
+            _lib.check(L.b200moe_layer_logits(_ptr(hidden), self.M, self.H, self.I, self.num_experts, self.topk,
+                                              _ptr(logits), int(logits.dtype == torch.bfloat16), scoring, _ptr(bias),
+                                              renorm, scale, _ptr(w13), _ptr(w13_scale), _ptr(w2), _ptr(w2_scale),
+                                              _ptr(self.expert_map), self.E, _ptr(self.topk_weights),
+                                              _ptr(self.topk_ids), _ptr(self.out), _ptr(self.ws), self.ws.numel(),
+                                              st), "layer_logits")
+            rec(1)
+            return self.out
         _lib.check(L.b200moe_route_logits(_ptr(logits), int(logits.dtype == torch.bfloat16), self.M, self.num_experts,
                                           self.topk, scoring, _ptr(bias), renorm, scale, _ptr(self.topk_weights),
                                           _ptr(self.topk_ids), _ptr(self.expert_map), self.E, self.tile,
@@ -389,6 +421,13 @@ class LayerPipeline:
         cnt = _ptr(self.counts)
         rows = cnt + 4
         rec(0)
+        if self.whole:
+            _lib.check(L.b200moe_layer(_ptr(hidden), M, self.H, self.I, self.num_experts, topk, _ptr(w13),
+                                       _ptr(w13_scale), _ptr(w2), _ptr(w2_scale), _ptr(topk_weights), _ptr(topk_ids),
+                                       _ptr(self.expert_map), E, _ptr(self.out), _ptr(self.ws), self.ws.numel(), st),
+                       "layer")
+            rec(1)
+            return self.out
         if self.heavy_rows:
             _lib.check(L.b200moe_route_mixed(_ptr(topk_ids), M, topk, self.num_experts, _ptr(self.expert_map), E,
                                              self.tile, self.heavy_rows, _ptr(self.sorted_ids), self.rows_cap,
