@@ -67,17 +67,25 @@ __device__ __forceinline__ void wait_flags(const int32_t* flags, int G, int32_t 
 
 // Called by every thread of every CTA after its stores: the last CTA to finish
 // raises this rank's flag (at byte offset flag_off of each rank's buffer) to
-// epoch on all G ranks and resets the CTA counter for the next launch.
+// epoch on all G ranks and resets the CTA counter for the next launch. The G
+// flags are raised by G threads at once: each release store waits for the
+// writes before it to reach the system (about 1 us apiece), so one thread
+// raising them in turn cost G of those waits.
 __device__ __forceinline__ void signal_done(const EpPeerArgs& a, int64_t flag_off, int32_t* counter) {
+  __shared__ int last;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
-    if (atomicAdd(counter, 1) == (int)(gridDim.x * gridDim.y) - 1) {
+    last = atomicAdd(counter, 1) == (int)(gridDim.x * gridDim.y) - 1;
+    if (last) {
       atomicExch(counter, 0);
       __threadfence_system();
-      for (int g = 0; g < a.G; ++g)
-        st_release_sys(reinterpret_cast<int32_t*>(a.bases[g] + flag_off) + a.rank, a.epoch);
     }
+  }
+  __syncthreads();
+  if (last) {
+    for (int g = threadIdx.x; g < a.G; g += blockDim.x)
+      st_release_sys(reinterpret_cast<int32_t*>(a.bases[g] + flag_off) + a.rank, a.epoch);
   }
 }
 
