@@ -423,3 +423,59 @@ def test_replicated_hot_experts_both_exchange_forms(cuda_device, G):
             single = moe.moe_decode_megakernel_full(hidden, W["w13"], W["w13_scale"], W["w2"], W["w2_scale"], tw, ids)
             assert orc.rel_l2(outs[r], single) < EP_TOL
     torch.cuda.synchronize(dev)
+
+
+@pytest.mark.parametrize("M,G", [(40, 2), (40, 8), (256, 4), (300, 2), (200, 8)])
+def test_peer_dispatch_plan_matches_all_to_all_form(cuda_device, M, G):
+    """The peer dispatch (the pack quantising the bf16 rows on its way into
+    the destinations' receive areas) leaves the same plan outputs (pos,
+    counts, tok_of of the used rows) and the same row bytes in every
+    destination's receive area as the all-to-all form's dispatch, with dropped
+    (-1) and out-of-range ids among them."""
+    from trials_b200 import _lib
+
+    dev = cuda_device
+    lib = _lib.lib()
+    H, topk, E, cap = 512, 4, 16, M
+    rank = G - 1
+    rb = lib.b200moe_ep_row_bytes(H, topk)
+    g = torch.Generator(device=dev).manual_seed(M * 10 + G)
+    hidden = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
+    tw, ids = synth.make_router(torch.randn(M, E, generator=g, device=dev), topk, "sigmoid")
+    ids[::5, 1] = -1
+    ids[3, 0] = E + 2  # out of range: dropped and reported
+    st = torch.cuda.current_stream(dev).cuda_stream
+    z = lambda n, v=0: torch.full((n,), v, dtype=torch.int32, device=dev)  # noqa: E731
+    # the all-to-all form (plan launch + pack into the send buffer)
+    q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
+    s = torch.empty(M, H // 128, dtype=torch.float32, device=dev)
+    ep.CudaEPOps().quant(hidden, q, s)
+    send = torch.zeros(G * cap * rb, dtype=torch.uint8, device=dev)
+    pos_a, tok_a, cnt_a, err_a = z(M * G), z(G * cap, -7), z(G), z(1)
+    _lib.check(lib.b200moe_ep_dispatch(q.data_ptr(), s.data_ptr(), ids.data_ptr(), tw.data_ptr(), M, H, topk, E, G,
+                                       rank, None, 0, 0, cap, send.data_ptr(), pos_a.data_ptr(), tok_a.data_ptr(),
+                                       cnt_a.data_ptr(), err_a.data_ptr(), st), "dispatch")
+    # the peer form, G exchange buffers in this process, epoch 1
+    nbytes = lib.b200moe_ep_peer_bytes(cap, H, topk, G)
+    bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(G)]
+    table = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=dev)
+    pos_p, tok_p, cnt_p, err_p = z(M * G), z(G * cap, -7), z(G), z(1)
+    _lib.check(lib.b200moe_ep_dispatch_peer(hidden.data_ptr(), None, None, ids.data_ptr(), tw.data_ptr(), M, H, topk,
+                                            E, G, rank, None, 0, 0, cap, table.data_ptr(), bufs[rank].data_ptr(), 1,
+                                            pos_p.data_ptr(), tok_p.data_ptr(), cnt_p.data_ptr(), err_p.data_ptr(),
+                                            st), "dispatch_peer")
+    torch.cuda.synchronize(dev)
+    assert torch.equal(pos_a, pos_p) and torch.equal(cnt_a, cnt_p)
+    recv_bytes = (G * cap * rb + 255) // 256 * 256
+    off = 1024 + recv_bytes  # receive area of epoch 1 (odd parity)
+    rows_a = send.view(G, cap, rb)
+    for d in range(G):
+        n = int(cnt_a[d].item())
+        assert torch.equal(tok_a[d * cap:d * cap + n], tok_p[d * cap:d * cap + n])
+        area = bufs[d][off + rank * cap * rb: off + (rank + 1) * cap * rb].view(cap, rb)
+        assert torch.equal(area[:n], rows_a[d, :n]), d
+        # rows past the count carry no expert (ids -1)
+        meta = area[n:, H + (H // 128) * 4: H + (H // 128) * 4 + 4 * topk].contiguous().view(torch.int32)
+        assert bool((meta == -1).all())
+        assert int(bufs[d][rank * 4:rank * 4 + 4].view(torch.int32).item()) == 1  # this rank's dispatch flag
+    assert moe.read_device_error(err_a) == moe.read_device_error(err_p) != 0
