@@ -441,7 +441,8 @@ int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, co
                int32_t* chunk_expert, int32_t* chunk_row0, int32_t* chunk_rows, int64_t chunks_capacity,
                int32_t* n_chunks, int32_t* num_rows, int32_t* slot_pos, int32_t* chunk_ready,
                int32_t* route_scratch, int64_t route_scratch_ints, int32_t* err_word, void* stream,
-               const RouterArgs* router, int32_t* router_counter, const MixedLists* mixed = nullptr) {
+               const RouterArgs* router, int32_t* router_counter, const MixedLists* mixed = nullptr,
+               const PackedMeta* packed = nullptr) {
   AlignArgs a;
   const int st = make_align(topk_ids, M, topk, num_experts, expert_map, num_local_experts, tile_tokens, sorted_ids,
                             rows_capacity, chunk_expert, chunk_row0, chunk_rows, chunks_capacity, n_chunks, num_rows,
@@ -458,6 +459,20 @@ int route_impl(const int32_t* topk_ids, int64_t M, int topk, int num_experts, co
     if (!counter || counts_ints < need || (need > 0 && !counts))
       return fail(B200MOE_ERR_WORKSPACE, "b200moe_route_logits: route_scratch too small%s");
     return cuda_status(launch_route_logits(a, *router, M, counter, counts, (cudaStream_t)stream), "route_logits");
+  }
+  if (packed) {
+    // Received expert-parallel rows: the routing launch also waits for them and
+    // unpacks their ids and weights; with several routing CTAs the unpack is a
+    // launch of its own first.
+    const int C = route_ctas(numel);
+    if (C == 1 || a.heavy_rows > 0 || !route_scratch || route_scratch_ints < (int64_t)C * E)
+      return cuda_status(launch_align_packed(a, *packed, (cudaStream_t)stream), "route_packed");
+    const int st = cuda_status(launch_ep_unpack_meta_peer(packed->own, packed->rows, packed->R, packed->row_bytes,
+                                                          packed->H, packed->topk, packed->G, packed->epoch,
+                                                          packed->ids, packed->w, err_word, packed->limit_ns,
+                                                          (cudaStream_t)stream),
+                               "ep_unpack_meta_peer");
+    if (st) return st;
   }
   return cuda_status(launch_route(a, route_scratch, route_scratch_ints, (cudaStream_t)stream), "route");
 }
@@ -961,7 +976,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
                const float* topk_weights, const int32_t* topk_ids, const int32_t* expert_map, int num_local_experts,
                void* out, void* workspace, size_t workspace_bytes, size_t workspace_offset, void* stream,
                const EpPeerArgs* peer_out = nullptr, int32_t* peer_counter = nullptr, int64_t tile_numel = -1,
-               const RouterArgs* router = nullptr) {
+               const RouterArgs* router = nullptr, const PackedMeta* packed = nullptr) {
   int st = check_gemm_shapes(H, I);
   if (st) return st;
   if (M < 0 || topk <= 0 || num_experts <= 0) return fail(B200MOE_ERR_INVALID_ARG, "%s: bad argument", name);
@@ -1009,7 +1024,7 @@ int layer_core(const char* name, const LayerInput& in, int64_t M, int64_t H, int
   }
   st = route_impl(topk_ids, M, topk, num_experts, expert_map, E, pl.tile_tokens, sorted, pl.rows_cap, ce, cr0, crows,
                   pl.chunks_cap, counts, counts + 1, pos, ready, rscratch, pl.rscratch_ints, err, stream, router,
-                  router ? err + 1 : nullptr, pl.heavy_rows ? &mx : nullptr);
+                  router ? err + 1 : nullptr, pl.heavy_rows ? &mx : nullptr, packed);
   if (st) return st;
   const LayerInput& src = in;
   if (src.hidden) {
@@ -1297,17 +1312,15 @@ int b200moe_layer_packed_peer(void* own_base, void* const* peer_bases, int num_r
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* ids = reinterpret_cast<int32_t*>(ws + 256);
   float* w = reinterpret_cast<float*>(ids + R * topk);
-  // waits for the G dispatch flags, then unpacks the ids and weights
-  int st = cuda_status(launch_ep_unpack_meta_peer(own, rows, R, rb, H, topk, num_ranks, epoch, ids, w, err,
-                                                  g_peer_wait_ns.load(), s),
-                       "ep_unpack_meta_peer");
-  if (st) return st;
+  // The routing launch waits for the G dispatch flags and unpacks the ids
+  // and weights before it routes them.
+  const PackedMeta pm{own, rows, R, rb, H, topk, num_ranks, epoch, g_peer_wait_ns.load(), ids, w};
   LayerInput in{nullptr, rows, rb, reinterpret_cast<const float*>(rows + H), rb / 4};
   // R*topk counts every id field of the G blocks; about rows_per_rank*topk of
   // them name this rank's experts, which sets the tile size.
   return layer_core("b200moe_layer_packed_peer", in, R, H, I, num_local_experts, topk, w13, w13_scale, w2, w2_scale, w,
                     ids, nullptr, num_local_experts, nullptr, workspace, workspace_bytes, meta, stream, &a, counter,
-                    rows_per_rank * topk);
+                    rows_per_rank * topk, nullptr, &pm);
 }
 
 int b200moe_ep_combine_peer(void* own_base, const int32_t* pos, int64_t M, int64_t H, int topk, int num_ranks,

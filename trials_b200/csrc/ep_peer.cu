@@ -22,6 +22,7 @@
 // B200MOE_DEVERR_TIMEOUT on expiry.
 #include "common.cuh"
 #include "ep_place.cuh"
+#include "ep_wait.cuh"
 #include "launch.h"
 #include "ptx.cuh"
 #include "rowops.cuh"
@@ -29,41 +30,6 @@
 namespace b200moe {
 
 namespace {
-
-__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
-  int32_t v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Threads 0..G-1 wait until flags[thread] >= epoch, then the whole CTA passes
-// a barrier: everything the G writers stored before raising their flags is
-// visible to the CTA (and to later kernels of the stream) afterwards. Once a
-// wait has expired (timeout bit in err), later waits give up after 1 ms, so a
-// many-CTA launch whose peer is gone ends in about one limit, not one per wave.
-__device__ __forceinline__ void wait_flags(const int32_t* flags, int G, int32_t epoch, int32_t* err,
-                                           uint64_t limit_ns) {
-  if ((int)threadIdx.x < G) {
-    const int32_t* f = flags + threadIdx.x;
-    if (ld_acquire_sys(f) < epoch) {
-      const uint64_t t0 = globaltimer_ns();
-      const uint64_t limit =
-          (*reinterpret_cast<volatile int32_t*>(err) & ERR_DEV_TIMEOUT) ? 1000000ull : limit_ns;
-      while (ld_acquire_sys(f) < epoch) {
-        if (globaltimer_ns() - t0 > limit) {
-          atomicOr(err, ERR_DEV_TIMEOUT);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-  }
-  __syncthreads();
-}
 
 // Called by every thread of every CTA after its stores: the last CTA to finish
 // raises this rank's flag (at byte offset flag_off of each rank's buffer) to
@@ -172,7 +138,8 @@ __global__ void __launch_bounds__(256) ep_reduce_peer_kernel(const __nv_bfloat16
     const int64_t r = t - (int64_t)src * a.rows_per_rank;
     __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(a.bases[src] + a.area_off) +
                          ((int64_t)a.rank * a.rows_per_rank + r) * H;
-    reduce_token_cols<B>(pair, slot_pos, sorted_rows, topk, H, t, (idx - t * per_row) * 8, row);
+    // rows past a source's count carry no slot and are never read: not sent
+    reduce_token_cols<B, true>(pair, slot_pos, sorted_rows, topk, H, t, (idx - t * per_row) * 8, row);
   }
   signal_done(a, EpPeerLayout::kCombineFlags, counter);
 }

@@ -167,6 +167,22 @@ cudaError_t launch_ep_pack_peer(const void* hidden, const uint8_t* q, const floa
                                 const float* w, int64_t H, int topk, const EpPlace& pl, const int32_t* tok_of,
                                 const int32_t* counts, int64_t row_bytes, const EpPeerArgs& a, int32_t* counter,
                                 cudaStream_t stream);
+// Received packed rows whose ids and weights the routing launch unpacks
+// itself, after waiting for the G dispatch flags (ep_unpack_meta_peer's work):
+// ids / w (R * topk) receive them; a.topk_ids must be ids.
+struct PackedMeta {
+  const uint8_t* own;   // this rank's exchange buffer (its dispatch flags)
+  const uint8_t* rows;  // receive area of this call
+  int64_t R, row_bytes, H;
+  int topk, G;
+  int32_t epoch;
+  uint64_t limit_ns;
+  int32_t* ids;
+  float* w;
+};
+// One-CTA routing that first waits for and unpacks the received rows' ids and
+// weights (below 16,384 routed slots, or with mixed lists).
+cudaError_t launch_align_packed(const AlignArgs& a, const PackedMeta& pm, cudaStream_t stream);
 cudaError_t launch_ep_unpack_meta_peer(const uint8_t* own, const uint8_t* rows, int64_t R, int64_t row_bytes,
                                        int64_t H, int topk, int G, int32_t epoch, int32_t* ids, float* w,
                                        int32_t* err, uint64_t limit_ns, cudaStream_t stream);

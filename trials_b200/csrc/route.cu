@@ -4,6 +4,7 @@
 // count / scatter kernels below on several CTAs (same result, bit for bit).
 #include "align.cuh"
 #include "common.cuh"
+#include "ep_wait.cuh"
 #include "launch.h"
 #include "router.cuh"
 
@@ -52,7 +53,34 @@ __global__ void __launch_bounds__(kRouteThreads, 1) router_align_kernel(const Al
   align_body<true, kRouteThreads>(a, sm);
 }
 
+// Expert-parallel layer: waits for the G dispatch flags, unpacks the received
+// rows' ids and weights (as ep_unpack_meta_peer_kernel), then routes them as
+// align_kernel does (reading the ids just stored through L2).
+__global__ void __launch_bounds__(kRouteThreads, 1) unpack_align_kernel(const AlignArgs a, const PackedMeta pm) {
+  extern __shared__ int32_t sm[];
+  wait_flags(reinterpret_cast<const int32_t*>(pm.own + EpPeerLayout::kDispatchFlags), pm.G, pm.epoch, a.err,
+             pm.limit_ns);
+  const int64_t n = pm.R * pm.topk;
+  for (int64_t i = threadIdx.x; i < n; i += kRouteThreads) {
+    const int64_t r = i / pm.topk;
+    const int j = (int)(i - r * pm.topk);
+    const int32_t* src = reinterpret_cast<const int32_t*>(pm.rows + r * pm.row_bytes + pm.H + (pm.H / 128) * 4);
+    pm.ids[i] = __ldcg(&src[j]);  // stored by other GPUs during the wait: read through L2
+    pm.w[i] = __ldcg(reinterpret_cast<const float*>(src + pm.topk) + j);
+  }
+  __syncthreads();
+  align_body<true, kRouteThreads>(a, sm);
+}
+
 size_t align_smem_bytes(int E) { return (size_t)align_smem_ints(E, kRouteWarps) * sizeof(int32_t); }
+
+cudaError_t launch_align_packed(const AlignArgs& a, const PackedMeta& pm, cudaStream_t stream) {
+  const size_t smem = align_smem_bytes(a.E);
+  cudaError_t err = cudaFuncSetAttribute(unpack_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  unpack_align_kernel<<<1, kRouteThreads, smem, stream>>>(a, pm);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_align(const AlignArgs& a, cudaStream_t stream) {
   const size_t smem = align_smem_bytes(a.E);

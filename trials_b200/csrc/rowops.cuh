@@ -144,18 +144,23 @@ __device__ __forceinline__ void quant_row_segment(const QuantArgs& a, int64_t ro
 // (-1: dropped); the row is pos (sorted_rows) or t*topk + j. Slots in groups of
 // B: all positions, then all row loads of the group are issued before the
 // sums consume them. Loads go through L2 (the rows may have been written by
-// other CTAs of the same launch).
-template <int B>
+// other CTAs of the same launch). SKIP_EMPTY: a row with no routed slot is not
+// stored (rows nobody reads: unused rows of an expert-parallel exchange block).
+template <int B, bool SKIP_EMPTY = false>
 __device__ __forceinline__ void reduce_token_cols(const __nv_bfloat16* pair, const int32_t* slot_pos, int sorted_rows,
                                                   int topk, int64_t H, int64_t t, int64_t c,
                                                   __nv_bfloat16* out_row) {
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  bool any = false;
   for (int j0 = 0; j0 < topk; j0 += B) {
     int pos[B];
 #pragma unroll
-    for (int j = 0; j < B; ++j) pos[j] = j0 + j < topk ? __ldcg(&slot_pos[t * topk + j0 + j]) : -1;
+    for (int j = 0; j < B; ++j) {
+      pos[j] = j0 + j < topk ? __ldcg(&slot_pos[t * topk + j0 + j]) : -1;
+      any |= pos[j] >= 0;
+    }
     uint4 x[B];
 #pragma unroll
     for (int j = 0; j < B; ++j) {
@@ -176,6 +181,7 @@ __device__ __forceinline__ void reduce_token_cols(const __nv_bfloat16* pair, con
       }
     }
   }
+  if (SKIP_EMPTY && !any) return;
   __nv_bfloat162 o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) o[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
