@@ -456,11 +456,13 @@ B200MOE_API int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, i
  * starts as soon as the stage-1 units of that chunk have written their rows,
  * which they count in chunk_ready (zeroed by b200moe_route for this call), so
  * the weight stream does not stop between the stages. Tiles of 16..64 tokens
- * run fused (cooperative launch, one CTA per SM); 128 and 256 run the two
- * stage kernels back to back, whose CTAs take their work units from the two
- * counters after the chunks_capacity per-chunk entries of chunk_ready. Either
- * way chunk_ready must be the one b200moe_route zeroed for this call: a second
- * call on the same routing needs a new b200moe_route first. */
+ * run fused (cooperative launch, one CTA per SM; each CTA takes its next work
+ * unit from the counter after the chunks_capacity per-chunk entries of
+ * chunk_ready when it is free for one); 128 and 256 run the two stage kernels
+ * back to back, whose CTAs take their work units from the two counters after
+ * the per-chunk entries. Either way chunk_ready must be the one b200moe_route
+ * zeroed for this call: a second call on the same routing needs a new
+ * b200moe_route first. */
 B200MOE_API int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int64_t rows_capacity,
                     const uint8_t* w13, const float* w13_scale, const uint8_t* w2, const float* w2_scale,
                     int num_local_experts, int64_t H, int64_t I, const int32_t* chunk_expert,

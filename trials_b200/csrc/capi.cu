@@ -736,6 +736,7 @@ int b200moe_experts(const uint8_t* a1_q, const float* a1_sT, int64_t a_s_ld, int
   p1.out_sT = a2_sT;
   p1.out_s_ld = a_s_ld;
   p1.chunk_ready = chunk_ready;
+  p1.unit_counter = chunk_ready + chunks_capacity;  // zeroed by routing with the per-chunk entries
   p1.err = err_word;
   p2.sorted_ids = sorted_ids;
   p2.topk_w = topk_weights;

@@ -346,6 +346,18 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
   uint64_t* pub = reinterpret_cast<uint64_t*>(tmem_slot + 4);
   // EPI_WHOLE: which CTA routes (broadcast from thread 0).
   volatile int* route_sh = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  // EPI_FUSED: units come from a counter (p.unit_counter, zeroed by routing)
+  // in the order CTAs become free for them; the producer hands each one with
+  // its chunk metadata {unit, expert, first row, rows} to the MMA thread and
+  // the epilogue warps through a ring of kUnitRing slots (-1: no more units),
+  // and the epilogue hands the chunk of each finished stage-1 unit to the
+  // publisher in pub_chunk (-1: no more).
+  constexpr bool DYN = EPI == EPI_FUSED;
+  constexpr int kUnitRing = 4;
+  uint64_t* ufull = pub + 4;
+  uint64_t* uempty = ufull + kUnitRing;
+  int4* uring = reinterpret_cast<int4*>(uempty + kUnitRing);
+  volatile int* pub_chunk = reinterpret_cast<volatile int*>(uring + kUnitRing);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -372,6 +384,11 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
       mbar_init(&pub[2], 1);
       mbar_init(&pub[3], 1);
     }
+    if (DYN)
+      for (int s = 0; s < kUnitRing; ++s) {
+        mbar_init(&ufull[s], 1);
+        mbar_init(&uempty[s], 1 + EW);  // the MMA thread and every epilogue warp
+      }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -429,7 +446,7 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
         e_n = ld_meta<ROUTE>(&p.chunk_expert[c]);
         p0_n = ld_meta<ROUTE>(&p.chunk_row0[c]);
       };
-      if (blockIdx.x < n_units) meta(blockIdx.x);
+      if (!DYN && blockIdx.x < n_units) meta(blockIdx.x);
       // With phase 0 in the launch (EPI_FUSED, q0.rows > 0) the stage-1
       // activation rows are written by the epilogue warps of every CTA first:
       // until all CTAs are done, stage-1 tiles get only their weight half, and
@@ -451,12 +468,42 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
         a_ready = true;
         return got;
       };
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        bool s2;
-        int chunk, nt;
-        unit_of(u, s2, chunk, nt);
-        const int e = e_n, p0 = p0_n;
-        if (u + (int)gridDim.x < n_units) meta(u + gridDim.x);
+      int uslot = 0;
+      uint32_t uphase = 0;
+      for (int k = 0, u = blockIdx.x; ok; ++k) {
+        bool s2 = false;
+        int chunk = 0, nt = 0, e = 0, p0 = 0;
+        if (DYN) {
+          // take the next unit (round-robin without a counter) and hand it
+          // on with its metadata
+          u = p.unit_counter ? atomicAdd(p.unit_counter, 1) : (int)blockIdx.x + k * (int)gridDim.x;
+          if (u >= n_units) u = -1;
+          int rows = 0;
+          if (u >= 0) {
+            unit_of(u, s2, chunk, nt);
+            e = __ldg(&p.chunk_expert[chunk]);
+            p0 = __ldg(&p.chunk_row0[chunk]);
+            rows = __ldg(&p.chunk_rows[chunk]);
+          }
+          if (*abort_flag || !mbar_wait_bounded(&uempty[uslot], uphase ^ 1, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          uring[uslot] = make_int4(u, e, p0, rows);
+          mbar_arrive(&ufull[uslot]);
+          if (++uslot == kUnitRing) {
+            uslot = 0;
+            uphase ^= 1;
+          }
+          if (u < 0) break;
+        } else {
+          if (k > 0) u += gridDim.x;
+          if (u >= n_units) break;
+          unit_of(u, s2, chunk, nt);
+          e = e_n;
+          p0 = p0_n;
+          if (u + (int)gridDim.x < n_units) meta(u + gridDim.x);
+        }
         const GemmParams& q = s2 ? p2 : p;
         const CUtensorMap* tw = s2 ? &tm_w2 : &tm_w;
         const CUtensorMap* ta = s2 ? &tm_a2 : &tm_a;
@@ -536,10 +583,31 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
         unit_of(u, s2, c, nt);
         return ld_meta<ROUTE>(&p.chunk_rows[c]);
       };
-      int rows_n = blockIdx.x < n_units ? rows_of(blockIdx.x) : 0;
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const int rows = rows_n;
-        if (u + (int)gridDim.x < n_units) rows_n = rows_of(u + gridDim.x);
+      int rows_n = !DYN && blockIdx.x < n_units ? rows_of(blockIdx.x) : 0;
+      int uslot = 0;
+      uint32_t uphase = 0;
+      for (int k = 0, u = blockIdx.x; ok; ++k) {
+        int rows;
+        if (DYN) {
+          if (!mbar_wait_or_abort(&ufull[uslot], uphase, p.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int4 ent = uring[uslot];
+          mbar_arrive(&uempty[uslot]);
+          if (++uslot == kUnitRing) {
+            uslot = 0;
+            uphase ^= 1;
+          }
+          u = ent.x;
+          rows = ent.w;
+          if (u < 0) break;
+        } else {
+          if (k > 0) u += gridDim.x;
+          if (u >= n_units) break;
+          rows = rows_n;
+          if (u + (int)gridDim.x < n_units) rows_n = rows_of(u + gridDim.x);
+        }
         const int NKB = (FUSED && u >= n1) ? NKB2 : NKB1;
         const uint32_t idesc = idesc_e4m3_f32(128, rows);
         for (int kb = 0; kb < NKB; ++kb) {
@@ -629,7 +697,31 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
         atomicAdd(p.phase_count, 1);
       }
     }
-    if (blockIdx.x < n_units) {
+    // EPI_FUSED: the next ring entry ({-1}: none left, {-2}: the wait ended
+    // without one). Every epilogue warp reads every entry.
+    int uslot = 0;
+    uint32_t uphase = 0;
+    auto take = [&]() -> int4 {
+      if (!mbar_wait_or_abort(&ufull[uslot], uphase, p.timeout_ns, abort_flag)) return make_int4(-2, 0, 0, 0);
+      const int4 v = uring[uslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&uempty[uslot]);
+      if (++uslot == kUnitRing) {
+        uslot = 0;
+        uphase ^= 1;
+      }
+      return v;
+    };
+    int4 nxt = make_int4(-1, 0, 0, 0);
+    if (DYN) {
+      nxt = take();
+      if (nxt.x >= 0) {
+        bool s2;
+        int c, nt;
+        unit_of(nxt.x, s2, c, nt);
+        load_ws(s2, nxt.y, nt);
+      }
+    } else if (blockIdx.x < n_units) {
       bool s2;
       int c, nt;
       unit_of(blockIdx.x, s2, c, nt);
@@ -638,18 +730,37 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
       rows_n = ld_meta<ROUTE>(&p.chunk_rows[c]);
       load_ws(s2, e_n, nt);
     }
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (int k = 0, u = blockIdx.x;; ++k) {
+      int e, p0, rows;
+      if (DYN) {
+        u = nxt.x;
+        if (u < 0) {
+          if (u == -2 && !*abort_flag) {
+            atomicOr(p.err, ERR_DEV_TIMEOUT);
+            *abort_flag = 1;
+          }
+          break;
+        }
+        e = nxt.y;
+        p0 = nxt.z;
+        rows = nxt.w;
+      } else {
+        if (k > 0) u += gridDim.x;
+        if (u >= n_units) break;
+        e = e_n;
+        p0 = p0_n;
+        rows = rows_n;
+      }
       bool s2;
       int chunk, nt;
       unit_of(u, s2, chunk, nt);
       const int NKB = s2 ? NKB2 : NKB1;
-      const int e = e_n, p0 = p0_n, rows = rows_n;
       const float ws0 = wl0, ws1 = wl1;
       const float* wsp = ws_row(s2, e, nt);
-      const int un = u + gridDim.x;
+      const int un = DYN ? -1 : u + (int)gridDim.x;
       bool s2n = false;
       int cn = 0, ntn = 0;
-      if (un < n_units) {
+      if (!DYN && un < n_units) {
         unit_of(un, s2n, cn, ntn);
         e_n = ld_meta<ROUTE>(&p.chunk_expert[cn]);
         p0_n = ld_meta<ROUTE>(&p.chunk_row0[cn]);
@@ -737,7 +848,17 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
         atomicOr(p.err, ERR_DEV_TIMEOUT);
         *abort_flag = 1;
       }
-      if (un < n_units) load_ws(s2n, e_n, ntn);
+      if (DYN) {
+        // The next unit only now: the producer hands it on after issuing this
+        // unit's loads, which needed this unit's TMEM buffers drained first.
+        nxt = ok ? take() : make_int4(-1, 0, 0, 0);
+        if (nxt.x >= 0) {
+          unit_of(nxt.x, s2n, cn, ntn);
+          load_ws(s2n, nxt.y, ntn);
+        }
+      } else if (un < n_units) {
+        load_ws(s2n, e_n, ntn);
+      }
 
       if (EPI == EPI_SILU || (FUSED && !s2)) {
         // Lane pair (2k, 2k+1) holds weight rows 2k (gate) and 2k+1 (up) of
@@ -806,6 +927,7 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
           if (n_pub >= 2 && lane == 0)
             free_slot = mbar_wait_or_abort(&pub[2 + sl], ((n_pub >> 1) & 1) ^ 1, p.timeout_ns, abort_flag);
           __syncwarp();
+          if (DYN && tid == 0 && free_slot) pub_chunk[sl] = chunk;
           if (lane == 0 && free_slot) mbar_arrive(&pub[sl]);
           ++n_pub;
         }
@@ -834,6 +956,16 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
           }
         }
       }
+    }
+    if (DYN) {
+      // No more stage-1 units from this CTA: the publisher may stop.
+      const int sl = n_pub & 1;
+      bool free_slot = true;
+      if (n_pub >= 2 && lane == 0)
+        free_slot = mbar_wait_or_abort(&pub[2 + sl], ((n_pub >> 1) & 1) ^ 1, p.timeout_ns, abort_flag);
+      __syncwarp();
+      if (tid == 0 && free_slot) pub_chunk[sl] = -1;
+      if (lane == 0 && free_slot) mbar_arrive(&pub[sl]);
     }
     if (PHASES) {
       // Last phase: the top-k reduce, once every CTA has stored all its
@@ -866,7 +998,7 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
     // ------------------------------------------------------------ publisher
     if (lane == 0) {
       int k = 0;
-      for (int u = blockIdx.x; u < n1; u += gridDim.x, ++k) {
+      for (int u = blockIdx.x; DYN || u < n1; u += gridDim.x, ++k) {
         const int sl = k & 1;
         if (!mbar_wait_or_abort(&pub[sl], (k >> 1) & 1, p.timeout_ns, abort_flag)) {
           if (!*abort_flag) {
@@ -875,9 +1007,15 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
           }
           break;
         }
-        bool s2;
-        int chunk, nt;
-        unit_of(u, s2, chunk, nt);
+        int chunk;
+        if (DYN) {
+          chunk = pub_chunk[sl];
+          if (chunk < 0) break;
+        } else {
+          bool s2;
+          int nt;
+          unit_of(u, s2, chunk, nt);
+        }
         __threadfence();
         atomicAdd(p.chunk_ready + chunk, 1);
         mbar_arrive(&pub[2 + sl]);
