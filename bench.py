@@ -14,7 +14,9 @@ scales, 1x128 activation scales, bf16 in/out).
   e2e         the same metric through the public API moe_decode_megakernel_full
               with host (pinned) inputs copied in (one copy of the packed
               hidden rows, ids and weights) and the output copied out inside
-              the timed region;
+              the timed region, every step; the copies run on their own
+              stream with two buffer sets, overlapping the neighbouring
+              steps' layers as a serving loop would;
   roofline    the dominant kernel (the grouped GEMMs) against measured HBM
               bandwidth;
   cpu_baseline the fp32 CPU oracle on a bounded sample of experts (rank 0, N=1),
@@ -223,6 +225,65 @@ def packed_inputs(*tensors):
         host[o:o + n].copy_(t.contiguous().view(-1).view(torch.uint8).cpu())
         views.append(dev[o:o + n].view(t.dtype).view(t.shape))
     return host, dev, views
+
+
+def pipelined_e2e(inputs, layer, out_shape, steps, warmup, sync):
+    """End-to-end steps through the public API with host buffers. Every step
+    copies its inputs in from pinned host memory (one copy of the packed
+    tensors) and its (M, H) bf16 result back to pinned host memory. The input
+    and result copies run on two streams of their own with two buffer sets, so
+    that step k+1's input copy and step k-1's result copy overlap step k's
+    layer (as a serving loop overlaps them); the timed region starts before
+    the first input copy and ends after the last result copy. layer(views) runs one layer on the device
+    input views and returns its output. sync() is called on both sides of the
+    timed region (barrier + synchronise). -> (ms per step, h2d bytes, d2h
+    bytes)."""
+    import torch
+
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    slots = []
+    for _ in range(2):
+        host, dev, views = packed_inputs(*inputs)
+        slots.append({"host": host, "dev": dev, "views": views, "out": None,
+                      "out_host": torch.empty(out_shape, dtype=torch.bfloat16).pin_memory(),
+                      "in_ready": torch.cuda.Event(), "computed": torch.cuda.Event(), "out_done": torch.cuda.Event(),
+                      "used": False})
+
+    def step(k):
+        sl = slots[k % 2]
+        with torch.cuda.stream(h2d):
+            if sl["used"]:
+                h2d.wait_event(sl["computed"])  # the layer two steps back has read these inputs
+            sl["dev"].copy_(sl["host"], non_blocking=True)
+            sl["in_ready"].record(h2d)
+        comp.wait_event(sl["in_ready"])
+        if sl["used"]:
+            comp.wait_event(sl["out_done"])  # the result two steps back is on the host: its buffer may go
+        sl["out"] = layer(sl["views"])
+        sl["computed"].record(comp)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(sl["computed"])
+            sl["out_host"].copy_(sl["out"], non_blocking=True)
+            sl["out_done"].record(d2h)
+        sl["used"] = True
+
+    for k in range(warmup):
+        step(k)
+    comp.wait_stream(h2d)
+    comp.wait_stream(d2h)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync()
+    start.record(comp)
+    h2d.wait_stream(comp)
+    d2h.wait_stream(comp)
+    for k in range(steps):
+        step(warmup + k)
+    comp.wait_stream(h2d)
+    comp.wait_stream(d2h)
+    end.record(comp)
+    sync()
+    return start.elapsed_time(end) / steps, slots[0]["host"].numel(), slots[0]["out_host"].numel() * 2
 
 
 def gemm2_bytes(shape, active, pairs):
@@ -483,45 +544,40 @@ def run_ep(args, shape, config):
     ms, stage_ms = timed(model, hidden, tw, ids, args.steps, args.warmup, "main")
     errs = model.device_errors()
     # Ours per step: plan, pack (quantising on the way with the peer exchange; a
-    # separate quant before it with NCCL), unpack, route, gather, the experts
-    # launch (two for token-major tiles), top-k reduce, combine; routing is two
-    # launches from 16,384 slots. The NCCL exchange adds its own all-to-all
-    # kernels, not counted.
+    # separate quant before it with NCCL), routing (which also waits for and
+    # unpacks the received rows with the peer exchange when it runs on one CTA;
+    # the unpack is a launch of its own otherwise), gather, the experts launch
+    # (two for token-major tiles; two more for the heavy-expert list of a
+    # mixed-list batch), top-k reduce, combine; routing is two launches from
+    # 16,384 slots. The NCCL exchange adds its own all-to-all kernels, not
+    # counted.
     from trials_b200 import _lib
     from trials_b200.stages import pick_tile_tokens
 
     def launches_per_step(M_rank):
+        lib = _lib.lib()
+        R = ws * M_rank  # received rows
         # the packed layer picks its tile from the slots expected on the rank
-        experts_launches = 2 if pick_tile_tokens(M_rank * shape.topk, per) > 64 else 1
-        route_launches = 2 if _lib.lib().b200moe_route_scratch_ints(ws * M_rank * shape.topk, per) > 0 else 1
-        return 6 + route_launches + experts_launches + (0 if args.exchange == "peer" else 1)
+        tile = pick_tile_tokens(M_rank * shape.topk, per)
+        heavy = lib.b200moe_heavy_rows(R, shape.topk, tile) > 0
+        multi_route = lib.b200moe_route_scratch_ints(R * shape.topk, per) > 0 and not heavy
+        n = 2 + (2 if multi_route else 1) + 1 + (2 if tile > 64 else 1) + (2 if heavy else 0) + 2
+        if args.exchange == "peer":
+            return n + (1 if multi_route else 0)
+        return n + 2  # quant, unpack
 
     ep_launches = launches_per_step(shape.M)
 
     e2e = None
     if not args.no_e2e:
-        in_host, in_dev, (h_dev, ids_dev, tw_dev) = packed_inputs(hidden, ids, tw)
-        out_host = torch.empty(shape.M, shape.H, dtype=torch.bfloat16).pin_memory()
-
-        def e2e_step():
-            in_dev.copy_(in_host, non_blocking=True)
-            out_host.copy_(model(h_dev, tw_dev, ids_dev), non_blocking=True)
-
-        for _ in range(args.warmup):
-            e2e_step()
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
         t0 = clocks.mark()
-        s2.record()
-        for _ in range(args.steps):
-            e2e_step()
-        e2.record()
-        barrier()
+        ms_copy, h2d, d2h = pipelined_e2e((hidden, ids, tw), lambda v: model(v[0], v[2], v[1]), (shape.M, shape.H),
+                                     args.steps, args.warmup, barrier)
         clocks.window(t0, clocks.mark())
-        ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps)
-        e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": in_host.numel() * ws,
-               "d2h_bytes_per_step": out_host.numel() * 2 * ws, "ms_per_step": ms_e2e}
+        ms_e2e = max_over_ranks(ms_copy)
+        e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d * ws,
+               "d2h_bytes_per_step": d2h * ws, "ms_per_step": ms_e2e,
+               "copies": "input and result copies on streams of their own, double-buffered: they overlap the neighbouring steps' layers"}
 
     other_x = "nccl" if args.exchange == "peer" else "peer"
 
@@ -872,29 +928,16 @@ def run_ours(args, shape, config):
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        in_host, in_dev, (h_dev, ids_dev, tw_dev) = packed_inputs(L.hidden, L.topk_ids, L.topk_weights)
-        out_host = torch.empty(shape.M, shape.H, dtype=torch.bfloat16).pin_memory()
-
-        def e2e_step():
-            in_dev.copy_(in_host, non_blocking=True)
-            out = moe.moe_decode_megakernel_full(h_dev, L.w13, L.w13_scale, L.w2, L.w2_scale, tw_dev, ids_dev)
-            out_host.copy_(out, non_blocking=True)
-
-        for _ in range(args.warmup):
-            e2e_step()
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
         t0 = clocks.mark()
-        s2.record()
-        for _ in range(args.steps):
-            e2e_step()
-        e2.record()
-        barrier()
+        ms_copy, h2d, d2h = pipelined_e2e(
+            (L.hidden, L.topk_ids, L.topk_weights),
+            lambda v: moe.moe_decode_megakernel_full(v[0], L.w13, L.w13_scale, L.w2, L.w2_scale, v[2], v[1]),
+            (shape.M, shape.H), args.steps, args.warmup, barrier)
         clocks.window(t0, clocks.mark())
-        ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps)
-        h2d = in_host.numel()
+        ms_e2e = max_over_ranks(ms_copy)
         e2e = {"value": shape.M * ws / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": out_host.numel() * 2, "ms_per_step": ms_e2e}
+               "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
+               "copies": "input and result copies on streams of their own, double-buffered: they overlap the neighbouring steps' layers"}
 
     peak, peak_kind = measured_peaks()
     sweep = None
