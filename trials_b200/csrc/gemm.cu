@@ -44,12 +44,25 @@ cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const G
   cfg.blockDim = dim3(C::THREADS + 32, 1, 1);  // + the publisher warp
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeCooperative;
-  attr.val.cooperative = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, tm_w, tm_a, p, tm_w2, tm_a2, p2);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  // EPI_FUSED follows the gather launch: launched programmatically, its
+  // prologue (barriers, TMEM, tensor maps) overlaps the gather's end. Should
+  // the runtime refuse the pair of attributes, the launch goes without it.
+  static bool pdl_ok = true;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (B200MOE_PDL && EPI == EPI_FUSED && pdl_ok) ? 2 : 1;
+  err = cudaLaunchKernelEx(&cfg, kernel, tm_w, tm_a, p, tm_w2, tm_a2, p2);
+  if (err != cudaSuccess && cfg.numAttrs == 2) {
+    cudaGetLastError();  // clear it, then launch as before
+    pdl_ok = false;
+    cfg.numAttrs = 1;
+    err = cudaLaunchKernelEx(&cfg, kernel, tm_w, tm_a, p, tm_w2, tm_a2, p2);
+  }
+  return err;
 }
 
 template <int EPI>

@@ -10,6 +10,28 @@
 
 namespace b200moe {
 
+// Launch with the programmatic stream serialisation attribute: the kernel may
+// begin while the kernel ahead of it in the stream finishes, so it must call
+// griddep_wait() (ptx.cuh) before it touches memory that kernel writes.
+#ifndef B200MOE_PDL
+#define B200MOE_PDL 1
+#endif
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = B200MOE_PDL ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 struct AlignArgs {
   const int32_t* topk_ids;
   int64_t n;               // M * topk

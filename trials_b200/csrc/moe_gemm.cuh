@@ -407,6 +407,9 @@ __global__ void __launch_bounds__(GemmCfg<T, CS>::THREADS + (EPI >= EPI_FUSED ? 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched programmatically after the gather: everything above overlapped
+  // its end; nothing below may read its rows (or the routing) before this.
+  griddep_wait();
 
   int n_chunks;
   if constexpr (ROUTE) {

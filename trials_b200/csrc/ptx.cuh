@@ -109,6 +109,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* t
       : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream serialisation attribute may start before the kernel ahead of it in
+// the stream has finished; griddep_wait() blocks until that kernel has
+// completed and its memory is visible (a no-op without the attribute), and
+// griddep_launch_dependents() lets the next such kernel start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // 1D bulk copy global -> shared (size and both addresses 16-byte aligned),
 // completion counted on `bar` (bytes).
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {

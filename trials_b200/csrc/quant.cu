@@ -17,6 +17,8 @@ namespace b200moe {
 constexpr int kQuantWarps = 8;
 
 __global__ void __launch_bounds__(kQuantWarps * 32) quant_1x128_kernel(const QuantArgs a) {
+  griddep_wait();  // the routing ahead of it (programmatic launch)
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
   const int64_t n_rows = a.num_rows ? (int64_t)(*a.num_rows) : a.rows;
@@ -28,8 +30,7 @@ cudaError_t launch_quant_1x128(const QuantArgs& a, cudaStream_t stream) {
   if (a.rows <= 0 || a.K <= 0) return cudaSuccess;
   const int64_t blocks = (a.rows + kQuantWarps - 1) / kQuantWarps;
   const dim3 grid((unsigned)blocks, (unsigned)((a.K + kQuantSegCols - 1) / kQuantSegCols));
-  quant_1x128_kernel<<<grid, kQuantWarps * 32, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(quant_1x128_kernel, grid, dim3(kQuantWarps * 32), 0, stream, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -110,6 +111,7 @@ __global__ void __launch_bounds__(256) combine_reduce_kernel(const __nv_bfloat16
                                                              const int32_t* __restrict__ slot_pos, int sorted_rows,
                                                              int64_t M, int topk, int64_t H,
                                                              __nv_bfloat16* __restrict__ out) {
+  griddep_wait();  // the experts launch ahead of it (programmatic launch)
   const int64_t per_row = H / 8;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t t = idx / per_row;
@@ -123,13 +125,12 @@ cudaError_t launch_combine_reduce(const void* pair_rows, const int32_t* slot_pos
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = (n + 255) / 256;
   const __nv_bfloat16* pair = static_cast<const __nv_bfloat16*>(pair_rows);
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out);
   if (M * topk <= 1024)
-    combine_reduce_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, M, topk, H,
-                                                                   reinterpret_cast<__nv_bfloat16*>(out));
-  else
-    combine_reduce_kernel<B200MOE_REDUCE_B_LARGE><<<(unsigned)blocks, 256, 0, stream>>>(
-        pair, slot_pos, sorted_rows, M, topk, H, reinterpret_cast<__nv_bfloat16*>(out));
-  return cudaGetLastError();
+    return launch_pdl(combine_reduce_kernel<8>, dim3((unsigned)blocks), dim3(256), 0, stream, pair, slot_pos,
+                      sorted_rows, M, topk, H, o);
+  return launch_pdl(combine_reduce_kernel<B200MOE_REDUCE_B_LARGE>, dim3((unsigned)blocks), dim3(256), 0, stream,
+                    pair, slot_pos, sorted_rows, M, topk, H, o);
 }
 
 // ---------------------------------------------------------------------------

@@ -6,6 +6,7 @@
 #include "common.cuh"
 #include "ep_wait.cuh"
 #include "launch.h"
+#include "ptx.cuh"
 #include "router.cuh"
 
 namespace b200moe {
@@ -18,6 +19,7 @@ constexpr int kRouteMaxCtas = 128;
 
 __global__ void __launch_bounds__(kRouteThreads, 1) align_kernel(const AlignArgs a) {
   extern __shared__ int32_t sm[];
+  griddep_launch_dependents();  // the gather may start launching (it waits for this grid)
   align_body<false, kRouteThreads>(a, sm);
 }
 
