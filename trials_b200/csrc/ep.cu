@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "ep_place.cuh"
 #include "launch.h"
+#include "ptx.cuh"
 
 namespace b200moe {
 
@@ -32,6 +33,7 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int32_t* __
                                                                 int32_t* __restrict__ counts, int32_t* err) {
   __shared__ int warp_tot[32];
   __shared__ int base_s;
+  griddep_launch_dependents();  // the pack may start launching (it waits for this grid)
   const int d = blockIdx.x;
   const int G = pl.G, num_experts = pl.num_experts;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

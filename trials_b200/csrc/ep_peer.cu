@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(256) ep_pack_peer_kernel(const __nv_bfloat16* 
                                                            const EpPlace pl, const int32_t* __restrict__ tok_of,
                                                            const int32_t* __restrict__ counts, int64_t row_bytes,
                                                            const EpPeerArgs a, int32_t* counter) {
+  griddep_wait();  // the plan ahead of it (programmatic launch)
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int64_t seg0 = (int64_t)blockIdx.y * kQuantSegCols;
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(256) ep_reduce_peer_kernel(const __nv_bfloat16
                                                              const int32_t* __restrict__ slot_pos, int sorted_rows,
                                                              int topk, int64_t H, const EpPeerArgs a,
                                                              int32_t* counter) {
+  griddep_wait();  // the experts launch ahead of it (programmatic launch)
   const int64_t per_row = H / 8;
   const int64_t R = (int64_t)a.G * a.rows_per_rank;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -151,6 +153,7 @@ __global__ void __launch_bounds__(256) ep_combine_peer_kernel(const uint8_t* own
                                                               int G, int64_t rows_per_rank, int32_t epoch,
                                                               __nv_bfloat16* __restrict__ out, int32_t* err,
                                                               uint64_t limit_ns) {
+  griddep_wait();  // the reduce ahead of it (programmatic launch)
   wait_flags(reinterpret_cast<const int32_t*>(own + EpPeerLayout::kCombineFlags), G, epoch, err, limit_ns);
   const __nv_bfloat16* comb = reinterpret_cast<const __nv_bfloat16*>(own + area_off);
   const int64_t per_row = H / 8;
@@ -189,9 +192,8 @@ cudaError_t launch_ep_pack_peer(const void* hidden, const uint8_t* q, const floa
   const int64_t rows = (int64_t)a.G * a.rows_per_rank;
   const dim3 grid((unsigned)(rows > 0 ? (rows + 7) / 8 : 1),  // one CTA at least, to raise the flags
                   (unsigned)((H + kQuantSegCols - 1) / kQuantSegCols));
-  ep_pack_peer_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(hidden), q, s, ids, w, H, topk, pl,
-                                                tok_of, counts, row_bytes, a, counter);
-  return cudaGetLastError();
+  return launch_pdl(ep_pack_peer_kernel, grid, dim3(256), 0, stream, static_cast<const __nv_bfloat16*>(hidden), q, s,
+                    ids, w, H, topk, pl, tok_of, counts, row_bytes, a, counter);
 }
 
 cudaError_t launch_ep_unpack_meta_peer(const uint8_t* own, const uint8_t* rows, int64_t R, int64_t row_bytes,
@@ -210,10 +212,10 @@ cudaError_t launch_ep_reduce_peer(const __nv_bfloat16* pair, const int32_t* slot
   const int64_t n = R * (H / 8);
   const int64_t blocks = n > 0 ? (n + 255) / 256 : 1;
   if (R * topk <= 1024)
-    ep_reduce_peer_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, topk, H, a, counter);
-  else
-    ep_reduce_peer_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(pair, slot_pos, sorted_rows, topk, H, a, counter);
-  return cudaGetLastError();
+    return launch_pdl(ep_reduce_peer_kernel<8>, dim3((unsigned)blocks), dim3(256), 0, stream, pair, slot_pos,
+                      sorted_rows, topk, H, a, counter);
+  return launch_pdl(ep_reduce_peer_kernel<4>, dim3((unsigned)blocks), dim3(256), 0, stream, pair, slot_pos,
+                    sorted_rows, topk, H, a, counter);
 }
 
 cudaError_t launch_ep_combine_peer(const uint8_t* own, int64_t area_off, const int32_t* pos, int64_t M, int64_t H,
@@ -221,9 +223,8 @@ cudaError_t launch_ep_combine_peer(const uint8_t* own, int64_t area_off, const i
                                    uint64_t limit_ns, cudaStream_t stream) {
   const int64_t n = M * (H / 8);
   if (n <= 0) return cudaSuccess;
-  ep_combine_peer_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-      own, area_off, pos, M, H, G, rows_per_rank, epoch, reinterpret_cast<__nv_bfloat16*>(out), err, limit_ns);
-  return cudaGetLastError();
+  return launch_pdl(ep_combine_peer_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, stream, own, area_off,
+                    pos, M, H, G, rows_per_rank, epoch, reinterpret_cast<__nv_bfloat16*>(out), err, limit_ns);
 }
 
 }  // namespace b200moe

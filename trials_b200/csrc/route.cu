@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) router_align_kernel(const Al
                                                                        int64_t M, int tpc, int32_t* counter) {
   extern __shared__ int32_t sm[];
   __shared__ int last;
+  griddep_launch_dependents();  // the gather may start launching (it waits for this grid)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t t = (int64_t)blockIdx.x * tpc + warp;
   if (warp < tpc && t < M) {
@@ -60,6 +61,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) router_align_kernel(const Al
 // align_kernel does (reading the ids just stored through L2).
 __global__ void __launch_bounds__(kRouteThreads, 1) unpack_align_kernel(const AlignArgs a, const PackedMeta pm) {
   extern __shared__ int32_t sm[];
+  griddep_launch_dependents();  // the gather may start launching (it waits for this grid)
   wait_flags(reinterpret_cast<const int32_t*>(pm.own + EpPeerLayout::kDispatchFlags), pm.G, pm.epoch, a.err,
              pm.limit_ns);
   const int64_t n = pm.R * pm.topk;
@@ -181,6 +183,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_scatter_kernel(const A
                                                                         const int32_t* __restrict__ scratch) {
   extern __shared__ int32_t sm[];
   __shared__ int warp_tot[32];
+  griddep_launch_dependents();  // the gather may start launching (it waits for this grid)
   const int E = a.E;
   int32_t* cnt = sm;                      // [kRouteWarps][E]
   int32_t* base = cnt + kRouteWarps * E;  // [E + 1]
