@@ -1,4 +1,6 @@
 // Instantiations and launcher of the persistent grouped GEMM.
+#include <atomic>
+
 #include "launch.h"
 #include "moe_gemm.cuh"
 #include "moe_gemm_tok.cuh"
@@ -50,15 +52,15 @@ cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const G
   // EPI_FUSED follows the gather launch: launched programmatically, its
   // prologue (barriers, TMEM, tensor maps) overlaps the gather's end. Should
   // the runtime refuse the pair of attributes, the launch goes without it.
-  static bool pdl_ok = true;
+  static std::atomic<bool> pdl_ok{true};
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = (B200MOE_PDL && EPI == EPI_FUSED && pdl_ok) ? 2 : 1;
+  cfg.numAttrs = (B200MOE_PDL && EPI == EPI_FUSED && pdl_ok.load()) ? 2 : 1;
   err = cudaLaunchKernelEx(&cfg, kernel, tm_w, tm_a, p, tm_w2, tm_a2, p2);
   if (err != cudaSuccess && cfg.numAttrs == 2) {
     cudaGetLastError();  // clear it, then launch as before
-    pdl_ok = false;
+    pdl_ok.store(false);
     cfg.numAttrs = 1;
     err = cudaLaunchKernelEx(&cfg, kernel, tm_w, tm_a, p, tm_w2, tm_a2, p2);
   }
