@@ -74,8 +74,7 @@ cudaError_t launch_tok(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const G
   auto kernel = moe_grouped_gemm_tok_kernel<EPI>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (err != cudaSuccess) return err;
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_a, p);
-  return cudaGetLastError();
+  return launch_pdl(kernel, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, tm_w, tm_a, p);
 }
 
 template <int EPI>

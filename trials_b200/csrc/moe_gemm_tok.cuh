@@ -163,6 +163,9 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int NKB = p.K >> 7;
   const int NT = p.Nw / C::UNIT_ROWS;
+  // Launched programmatically: the kernel ahead of it (the routing's work
+  // list, the gather's rows, stage 1's rows) must be done before any read.
+  griddep_wait();
   // An empty work list (the heavy list of a batch without heavy experts)
   // ends the launch before any set-up.
   if (*p.n_chunks == 0) return;
