@@ -441,7 +441,9 @@ B200MOE_API int b200moe_gemm1_silu(const uint8_t* a1_q, const float* a1_sT, int6
  * (the reference rounds this product to bf16 too, aiter.py:164-177). Tiles of 16..64 tokens
  * write it to row f of out_pair (M*topk, H); token-major tiles (128, 256) to
  * row p of out_pair (rows_capacity, H), which keeps a unit's rows together in
- * memory. Padding rows and dropped slots are not written. */
+ * memory (tiles of 128 store them with TMA: out_pair 16-byte aligned, and the
+ * rows of a chunk without a slot, its expert's padding, are written as zeros).
+ * Other padding rows and dropped slots are not written. */
 B200MOE_API int b200moe_gemm2_combine(const uint8_t* a2_q, const float* a2_sT, int64_t a_s_ld, int64_t rows_capacity,
                           const uint8_t* w2, const float* w2_scale, int num_local_experts, int64_t H, int64_t I,
                           const int32_t* chunk_expert, const int32_t* chunk_row0, const int32_t* chunk_rows,

@@ -71,6 +71,23 @@ int make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, i
   return B200MOE_OK;
 }
 
+// 2D bf16 matrix [rows][cols] (row pitch = cols elements), boxes of 64
+// columns (128 bytes) x box_rows, 128-byte swizzle: the token-major stage-2
+// output, stored from swizzled shared-memory staging.
+int make_tmap_rows_bf16(CUtensorMap* m, void* base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable%s");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed%s");
+  return B200MOE_OK;
+}
+
 int sm_count() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -232,10 +249,17 @@ int run_gemm(int epi, const uint8_t* a_q, const float* a_sT, int64_t as_ld, int6
   int st = prep_gemm(a_q, a_sT, as_ld, rows_cap, w, w_scale, E_local, Nw, K, ce, cr0, crows, n_chunks, tile_tokens,
                      p, tm_w, tm_a);
   if (st) return st;
+  // Token-major stage 2 (tiles of 128) stores its sorted rows with TMA.
+  CUtensorMap tm_o = tm_w;
+  if (epi == EPI_COMBINE && tile_tokens == 128 && !p.rows_by_slot) {
+    if (!aligned16(p.out_pair)) return fail(B200MOE_ERR_UNSUPPORTED, "out_pair: 16-byte alignment required%s");
+    st = make_tmap_rows_bf16(&tm_o, p.out_pair, rows_cap, Nw, 16);
+    if (st) return st;
+  }
   const int64_t units_cap = chunks_cap * (Nw / 256);
   int64_t grid = grid_ctas > 0 ? grid_ctas : sm_count();
   if (grid > units_cap) grid = units_cap;
-  return cuda_status(launch_grouped_gemm(epi, tile_tokens, tm_w, tm_a, p, (int)grid, stream), "grouped gemm");
+  return cuda_status(launch_grouped_gemm(epi, tile_tokens, tm_w, tm_a, tm_o, p, (int)grid, stream), "grouped gemm");
 }
 
 }  // namespace

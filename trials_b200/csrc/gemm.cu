@@ -68,13 +68,13 @@ cudaError_t launch_cfg(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const G
 }
 
 template <int EPI>
-cudaError_t launch_tok(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p, int grid,
-                       cudaStream_t stream) {
+cudaError_t launch_tok(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const CUtensorMap& tm_o, const GemmParams& p,
+                       int grid, cudaStream_t stream) {
   using C = TokCfgE<EPI>;
   auto kernel = moe_grouped_gemm_tok_kernel<EPI>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (err != cudaSuccess) return err;
-  return launch_pdl(kernel, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, tm_w, tm_a, p);
+  return launch_pdl(kernel, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, stream, tm_w, tm_a, tm_o, p);
 }
 
 template <int EPI>
@@ -106,8 +106,8 @@ cudaError_t launch_tok2(const CUtensorMap& tm_w, const CUtensorMap& tm_a, const 
 }
 
 template <int EPI>
-cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a, const GemmParams& p,
-                       int grid, cudaStream_t stream) {
+cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a, const CUtensorMap& tm_o,
+                       const GemmParams& p, int grid, cudaStream_t stream) {
   switch (tile_tokens) {
     case 16:
     case 32:
@@ -118,7 +118,7 @@ cudaError_t launch_epi(int tile_tokens, const CUtensorMap& tm_w, const CUtensorM
       return launch_cfg<64, EPI == EPI_SILU ? 1 : 2, EPI>(tm_w, tm_a, p, tm_w, tm_a, p, grid, stream);
     case 128:
       // Many tokens per expert: routed rows on the MMA M side.
-      return launch_tok<EPI>(tm_w, tm_a, p, grid, stream);
+      return launch_tok<EPI>(tm_w, tm_a, tm_o, p, grid, stream);
     case 256:
       // Even more: CTA pairs with a 256-row MMA.
       return launch_tok2<EPI>(tm_w, tm_a, p, grid, stream);
@@ -166,11 +166,11 @@ cudaError_t launch_grouped_gemm_fused(int tile_tokens, const CUtensorMap& tm_w1,
 }
 
 cudaError_t launch_grouped_gemm(int epi, int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a,
-                                const GemmParams& p, int grid, cudaStream_t stream) {
+                                const CUtensorMap& tm_o, const GemmParams& p, int grid, cudaStream_t stream) {
   if (grid <= 0) return cudaSuccess;
   if (tile_tokens == 256 && grid < 2) grid = 2;
-  if (epi == EPI_SILU) return launch_epi<EPI_SILU>(tile_tokens, tm_w, tm_a, p, grid, stream);
-  return launch_epi<EPI_COMBINE>(tile_tokens, tm_w, tm_a, p, grid, stream);
+  if (epi == EPI_SILU) return launch_epi<EPI_SILU>(tile_tokens, tm_w, tm_a, tm_o, p, grid, stream);
+  return launch_epi<EPI_COMBINE>(tile_tokens, tm_w, tm_a, tm_o, p, grid, stream);
 }
 
 }  // namespace b200moe

@@ -228,8 +228,10 @@ struct GemmParams;
 cudaError_t launch_grouped_gemm_fused(int tile_tokens, const CUtensorMap& tm_w1, const CUtensorMap& tm_a1,
                                       const GemmParams& p1, const CUtensorMap& tm_w2, const CUtensorMap& tm_a2,
                                       const GemmParams& p2, int grid, cudaStream_t stream);
+// tm_o: stage 2's out_pair for the token-major tiles of 128 that store sorted
+// rows with TMA (make_tmap_rows_bf16); any map otherwise (not read).
 cudaError_t launch_grouped_gemm(int epi, int tile_tokens, const CUtensorMap& tm_w, const CUtensorMap& tm_a,
-                                const GemmParams& p, int grid, cudaStream_t stream);
+                                const CUtensorMap& tm_o, const GemmParams& p, int grid, cudaStream_t stream);
 // Activation tile rows the kernel for this tile_tokens loads per stage (per CTA).
 int gemm_tile_rows(int tile_tokens);
 // Weight rows per TMA box (per CTA).

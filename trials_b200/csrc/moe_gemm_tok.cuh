@@ -27,12 +27,12 @@ namespace b200moe {
 // sub-partition, 64 columns per thread, to hide more of the TMEM-load and FMA
 // latencies of the per-K-block promotion). 16 measured 3% slower at 4,096
 // and 8,192 tokens (96 registers a thread, some spilled), so 8 it is. Stage 2
-// keeps 8 either way: its store transpose buffers would cost a pipeline stage.
+// keeps 8 either way: its output staging would cost another pipeline stage.
 #ifndef B200MOE_TOK_EW_SILU
 #define B200MOE_TOK_EW_SILU 8
 #endif
 
-template <int EW_, bool XPOSE_>
+template <int EW_, bool OUT_>
 struct TokCfgT {
   static constexpr int TM = 128;                 // routed rows per unit (MMA M)
   static constexpr int UNIT_ROWS = 256;          // weight rows per unit (MMA N)
@@ -49,15 +49,19 @@ struct TokCfgT {
   static constexpr int RED = 2 * CQ * TM * 4;    // amax exchange, double-buffered by unit parity
   static constexpr int SMEM_LIMIT = 232448;
   static constexpr int MAX_STAGE = 6;
-  static constexpr int XPOSE = XPOSE_ ? EW * 32 * 20 * 4 : 0;  // stage-2 store transpose blocks
+  // Stage 2: each epilogue warp's 32 rows x COLS bf16 output columns, staged
+  // for TMA stores in 64-column boxes with the 128-byte swizzle (1024-byte
+  // aligned, hence the extra 1024).
+  static constexpr int OUT_STAGE = OUT_ ? EW * 32 * COLS * 2 : 0;
   static constexpr int NU = 4;                    // unit hand-off ring (producer -> MMA, epilogue)
-  static constexpr int FIXED = 1024 + RED + (MAX_STAGE + NBUF) * S_BYTES + 1024 + XPOSE;
+  static constexpr int FIXED = 1024 + RED + (MAX_STAGE + NBUF) * S_BYTES + 1024 + (OUT_ ? OUT_STAGE + 1024 : 0);
   static constexpr int NSTAGE_RAW = (SMEM_LIMIT - FIXED) / TILE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > MAX_STAGE ? MAX_STAGE : NSTAGE_RAW;
   static constexpr int NSLOT = NSTAGE + NBUF;
   static constexpr int SMEM_BYTES = FIXED + NSTAGE * TILE_BYTES;
   static_assert(EW == 8 || EW == 16, "8 or 16 epilogue warps");
   static_assert(COLS % 32 == 0 && COLS <= 128, "a thread's columns lie in one 128-row scale block");
+  static_assert(!OUT_ || COLS % 64 == 0, "stage-2 output boxes are 64 columns wide");
   static_assert(NSTAGE >= 2, "shared memory too small");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory budget");
 };
@@ -72,8 +76,8 @@ using TokCfg = TokCfgT<8, true>;
 // calling warp holds rows row0 .. row0+31 of the unit (lane = row) x NC
 // output columns in acc. They pass through tb (this warp's 32 x 20 floats of
 // shared memory) 16 columns at a time, so that every store instruction writes
-// 64 contiguous bytes of 8 rows (whole 32-byte sectors) instead of 16 bytes of
-// 32 rows. Only rows whose bit is set in `valid` (bit i = row row0 + i, a
+// 32 contiguous bytes (one whole sector) of each of 8 rows instead of 8 bytes
+// of 32 rows. Only rows whose bit is set in `valid` (bit i = row row0 + i, a
 // routed slot) are written; w_l is the lane's router weight.
 template <int NC>
 __device__ __forceinline__ void store_sorted_rows(const float (&acc)[NC], float w_l, unsigned valid, float* tb,
@@ -129,10 +133,13 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
 #define B200MOE_TOK_FFMA2 1
 #endif
 
+// tm_o: stage 2's out_pair (rows_capacity, Nw) bf16, boxes of 64 columns x 16
+// rows with the 128-byte swizzle; read only when stage-2 rows go to their
+// sorted position (not rows_by_slot).
 template <int EPI>
 __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
     moe_grouped_gemm_tok_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
-                                const GemmParams p) {
+                                const __grid_constant__ CUtensorMap tm_o, const GemmParams p) {
   using C = TokCfgE<EPI>;
   constexpr int EW = C::EW;
   constexpr int COLS = C::COLS;
@@ -157,7 +164,8 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
   // Units in the order the producer takes them (-1 = no more), read by the MMA
   // thread and every epilogue warp before the slot is reused.
   volatile int* unit_sh = reinterpret_cast<volatile int*>(tmem_slot + 4);
-  float* xpose = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 1024);  // EW x 32 x 20
+  uint8_t* out_stage = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(full) + 1024 + 1023) & ~uintptr_t(1023));  // EW x 32 x COLS bf16
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -197,6 +205,7 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_a);
+    if (EPI != EPI_SILU && !p.rows_by_slot) prefetch_tmap(&tm_o);
   }
   tc_fence_before();
   __syncthreads();
@@ -390,6 +399,12 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
       const float ws0 = wl0, ws1 = wl1;
       const bool live = q * 32 < rows;  // warp-uniform
       const float* wsp = ws_row(e, nt);
+      // Stage 2: the row's slot id is loaded now and its router weight after
+      // the first partial, so that neither load waits in the unit's tail.
+      int f_row = p.sentinel;
+      float w_row = 0.f;
+      if constexpr (EPI != EPI_SILU)
+        if (live && r < rows) f_row = __ldg(&p.sorted_ids[p0 + r]);
 
       float acc[COLS];
 #pragma unroll
@@ -403,6 +418,8 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
           break;
         }
         tc_fence_after();
+        if constexpr (EPI != EPI_SILU)
+          if (kb == 0 && f_row < p.sentinel) w_row = __ldg(&p.topk_w[f_row]);
         if (!mbar_wait_bounded(&sfull[slot], sphase, p.timeout_ns)) {
           ok = false;
           break;
@@ -502,8 +519,8 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
         // memory (rows by slot id scatter them over the whole buffer, and the
         // stores then cost more than the unit's MMAs at prefill sizes).
         if (live) {
-          const int f = r < rows ? __ldg(&p.sorted_ids[p0 + r]) : p.sentinel;
-          const float w = f < p.sentinel ? __ldg(&p.topk_w[f]) : 0.f;
+          const int f = f_row;
+          const float w = w_row;
           if (p.rows_by_slot) {
             // Row f (the slot), as the swap-AB tiles write it: COLS contiguous
             // bf16 per thread (few heavy experts of a decode batch take this path).
@@ -519,9 +536,50 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
               }
             }
           } else {
-            const unsigned valid = __ballot_sync(0xffffffffu, f < p.sentinel);
-            store_sorted_rows(acc, w, valid, xpose + ew * (32 * 20), lane, q * 32,
-                              p.out_pair + (int64_t)p0 * p.Nw + nt * C::UNIT_ROWS + cq * COLS, p.Nw);
+            // The warp's 32 rows x COLS columns go to shared memory (bf16,
+            // 64-column boxes of 32 rows x 128 bytes, 16-byte pieces swizzled
+            // by row: piece c of row r at c ^ (r & 7), so the 8 rows of a
+            // quarter-warp store hit different banks), then one lane stores
+            // them with TMA, 16 rows per box. Chunks of an expert follow one
+            // another in the sorted rows, so only the chunk's own rows are
+            // written: 16-row blocks inside it by TMA (their rows without a
+            // slot as zeros), the rows of a block that the chunk ends inside
+            // by their own threads (chunks from routing are multiples of 16
+            // rows and never end inside a block). The staging buffer is
+            // reused once the warp's previous stores have read it.
+            uint8_t* sb = out_stage + ew * (32 * COLS * 2);
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+            const bool valid = f < p.sentinel;
+            const bool own_store = r < rows && (r & ~15) + 16 > rows;
+            __nv_bfloat16* orow = p.out_pair + (int64_t)(p0 + r) * p.Nw + nt * C::UNIT_ROWS + cq * COLS;
+#pragma unroll
+            for (int b = 0; b < COLS / 64; ++b)
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  const int j = b * 64 + c * 8 + 2 * t;
+                  __nv_bfloat162 h = __floats2bfloat162_rn(valid ? w * acc[j] : 0.f, valid ? w * acc[j + 1] : 0.f);
+                  pk[t] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                const uint4 v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<uint4*>(sb + b * 4096 + lane * 128 + ((c ^ (lane & 7)) << 4)) = v;
+                if (own_store) *reinterpret_cast<uint4*>(orow + b * 64 + c * 8) = v;
+              }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                if (q * 32 + h * 16 + 16 <= rows)
+#pragma unroll
+                  for (int b = 0; b < COLS / 64; ++b)
+                    tma_store_2d(&tm_o, sb + b * 4096 + h * 2048, nt * C::UNIT_ROWS + cq * COLS + b * 64,
+                                 p0 + q * 32 + h * 16);
+              bulk_commit_group();
+            }
           }
         }
       }
@@ -530,6 +588,9 @@ __global__ void __launch_bounds__(TokCfgE<EPI>::THREADS, 1)
       atomicOr(p.err, ERR_DEV_TIMEOUT);
       *abort_flag = 1;
     }
+    // Stage-2 rows stored with TMA are complete (and the staging buffer
+    // read) before the CTA exits.
+    if (EPI != EPI_SILU && lane == 0) bulk_wait_all();
   }
 
   __syncwarp();

@@ -109,6 +109,29 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* t
       : "memory");
 }
 
+// 2D tiled TMA store shared -> global of one box at (x, y) (x in elements of
+// the map's type, x * element size a multiple of 16 bytes, both coordinates
+// non-negative), tracked in this thread's bulk async-group. The writes to
+// smem_src must be made visible to the async proxy first (fence_proxy_async
+// by the writing threads, then a barrier).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tmap, const void* smem_src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Until this thread's committed bulk stores have read their shared memory
+// (the source may be rewritten after it).
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Until this thread's committed bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Programmatic dependent launch: a kernel launched with the programmatic
 // stream serialisation attribute may start before the kernel ahead of it in
 // the stream has finished; griddep_wait() blocks until that kernel has

@@ -186,7 +186,8 @@ def gemm1_silu(a1_q, a1_sT, w13, w13_scale, r: Routing, grid_ctas: int = 0):
 def gemm2_combine(a2_q, a2_sT, w2, w2_scale, r: Routing, topk_weights: torch.Tensor, grid_ctas: int = 0,
                   out_pair: Optional[torch.Tensor] = None):
     """-> out_pair bf16 rows of H: row p = sorted row p for token-major tiles (rows_cap
-    rows), else row f = slot (M*topk rows). Padding rows / dropped slots untouched."""
+    rows), else row f = slot (M*topk rows). Dropped slots untouched; padding rows
+    untouched, except inside a chunk of 128-token tiles (written as zeros)."""
     dev = _require_cuda(a2_q, w2)
     E, H, I = w2.shape
     M, topk = topk_weights.shape
